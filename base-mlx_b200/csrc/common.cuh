@@ -1,0 +1,115 @@
+// Shared device helpers for the sm_100a Qwen3 4-bit decode kernels.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+typedef __nv_bfloat16 bf16;
+
+#define QW_DEV __device__ __forceinline__
+
+// Device-side error flag bits (qw_model::d_err).  A kernel that detects an
+// out-of-range index records a bit here and skips the access instead of
+// faulting; the host turns a non-zero flag into QW_ERR_DEVICE_FLAG.
+enum : int {
+    QW_DERR_KV_RANGE = 1,     // KV write/read position >= max_pos
+    QW_DERR_TOKEN_RANGE = 2,  // token id >= vocab
+    QW_DERR_SHAPE = 4,        // kernel launched with an unsupported shape
+};
+
+QW_DEV float bf2f(bf16 v) { return __bfloat162float(v); }
+QW_DEV bf16 f2bf(float v) { return __float2bfloat16_rn(v); }
+// round an fp32 value to the nearest bf16 and return it as fp32
+QW_DEV float bfr(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+QW_DEV float bits_lo_f(uint32_t w) { return __uint_as_float(w << 16); }
+QW_DEV float bits_hi_f(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+QW_DEV float u16_to_f(uint16_t h) { return __uint_as_float(((uint32_t)h) << 16); }
+QW_DEV uint16_t f_to_bf16bits(float v) {
+    bf16 b = __float2bfloat16_rn(v);
+    return *reinterpret_cast<uint16_t*>(&b);
+}
+QW_DEV uint32_t pack_bf16x2(float lo, float hi) {
+    return (uint32_t)f_to_bf16bits(lo) | ((uint32_t)f_to_bf16bits(hi) << 16);
+}
+
+// ---- programmatic dependent launch (sm_90+) -------------------------------
+// Every kernel of a forward calls pdl_wait() before touching data written by
+// the previous kernel; weight prefetches (static data) may run before it.
+QW_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+QW_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---- warp-level tensor core op -----------------------------------------
+// D[16x8] (fp32) = A[16x16] (bf16, row) * B[16x8] (bf16, col) + C.
+// Fragment ownership (lane = 4*g + t): a0:(g, 2t..2t+1) a1:(g+8, 2t..) a2:(g, 2t+8..)
+// a3:(g+8, 2t+8..); b0:(k=2t..2t+1, n=g) b1:(k=2t+8.., n=g); c0,c1:(g, 2t..2t+1) c2,c3:(g+8, ..).
+QW_DEV void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                     uint32_t b0, uint32_t b1, const float (&c)[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};\n"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1),
+          "f"(c[0]), "f"(c[1]), "f"(c[2]), "f"(c[3]));
+}
+
+// ---- 4-bit nibbles -> bf16 pairs ----------------------------------------
+// For a packed word w (element i at bits 4i), nib_pair(w, j) is a bf16x2
+// register holding (128 + q_j, 128 + q_{j+4}): the nibble is dropped into the
+// low mantissa bits of bf16 128.0 (0x4300), which represents 128 + q exactly.
+QW_DEV uint32_t nib_pair(uint32_t w, int j) {
+    return ((w >> (4 * j)) & 0x000F000Fu) | 0x43004300u;
+}
+// bf16x2 (128.0, 128.0): the A operand whose product with B yields 128 * sum(x).
+#define QW_BF16X2_128 0x43004300u
+
+// byte permute (PRMT)
+QW_DEV uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+
+// Rearrange 16 consecutive bf16 values (8 words X0..X7, value 2i in the low
+// half of Xi) into the B-fragment order used with nib_pair():
+// out = {(x0,x4),(x1,x5),(x2,x6),(x3,x7),(x8,x12),(x9,x13),(x10,x14),(x11,x15)}
+QW_DEV void permute16(const uint32_t (&X)[8], uint32_t (&o)[8]) {
+    o[0] = prmt(X[0], X[2], 0x5410);
+    o[1] = prmt(X[0], X[2], 0x7632);
+    o[2] = prmt(X[1], X[3], 0x5410);
+    o[3] = prmt(X[1], X[3], 0x7632);
+    o[4] = prmt(X[4], X[6], 0x5410);
+    o[5] = prmt(X[4], X[6], 0x7632);
+    o[6] = prmt(X[5], X[7], 0x5410);
+    o[7] = prmt(X[5], X[7], 0x7632);
+}
+
+// ---- argmax keys ----------------------------------------------------------
+// 64-bit key ordering (value desc, index asc): max over keys is the argmax
+// with the lowest index winning ties (MLX argmax semantics).
+QW_DEV unsigned long long amax_key(float v, uint32_t idx) {
+    uint32_t u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
+}
+QW_DEV uint32_t amax_key_index(unsigned long long k) { return 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull); }
+QW_DEV unsigned long long umax64(unsigned long long a, unsigned long long b) { return a > b ? a : b; }
+
+QW_DEV float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+QW_DEV float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// ---- seeded generator shared with the CPU oracle ------------------------
+QW_DEV uint64_t splitmix64(uint64_t x) {
+    uint64_t z = x + 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}

@@ -1,0 +1,265 @@
+// The Qwen3 forward step and the device-resident greedy loop.
+//
+// forward_dev restates crates/base-mlx-core/src/model/qwen3.rs:314-563
+// (Qwen3::forward_internal) as a chain of sm_100a kernels on one stream:
+//
+//   S <= 8 rows (decode / speculative verify):
+//     embed -> per layer { qgemv[RMSNorm -> q|k|v] -> attn_decode[q/k norm, RoPE,
+//     KV write, split-T attention] -> qgemv[o_proj + residual] ->
+//     qgemv[RMSNorm -> gate|up -> SiLU*up] -> qgemv[down_proj + residual] }
+//     -> qgemv[final norm -> lm_head -> argmax] -> step_finish
+//   S > 8 rows (prefill): the same with rmsnorm + qgemm + qk_norm_rope_kvwrite +
+//     attn_prefill kernels.
+//
+// Every kernel is launched with programmatic dependent launch, so a kernel's
+// weight prefetch overlaps the tail of its predecessor.  The KV length lives
+// on the device, which lets one captured CUDA graph serve every decode step.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+#include "model.h"
+
+namespace qw {
+
+namespace {
+
+QSeg seg_of(const QLin& q, void* y, int ldy) {
+    QSeg s;
+    s.w = q.w;
+    s.s = q.s;
+    s.b = q.b;
+    s.y = y;
+    s.n = q.n;
+    s.ldy = ldy;
+    s.rb0 = 0;
+    return s;
+}
+
+QmmArgs qmm_base(qw_model* m, const bf16* x, int ldx, int M, int K) {
+    QmmArgs a;
+    std::memset(&a, 0, sizeof(a));
+    Workspace& w = m->ws;
+    a.x = x;
+    a.ldx = ldx;
+    a.M = M;
+    a.K = K;
+    a.eps = m->cfg.eps;
+    a.partial = w.partial;
+    a.partial_cap = w.partial_cap;
+    a.counters = w.counters;
+    a.amax_partial = w.amax_partial;
+    a.amax_counter = w.amax_counter;
+    a.err = m->d_err;
+    return a;
+}
+
+void qmm(qw_model* m, QmmArgs a, cudaStream_t st) {
+    if (a.M <= 8)
+        QW_CUDA(launch_qgemv(a, st, true, m->num_sms));
+    else
+        QW_CUDA(launch_qgemm(a, st, m->num_sms));
+}
+
+}  // namespace
+
+void forward_dev(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_mode, bool store_logits,
+                 int* d_argmax, cudaStream_t st, StepCtl* ctl, int* next_tok, int* out, const int* gate) {
+    const Config& cf = m->cfg;
+    Workspace& w = m->ws;
+    const int H = cf.hidden, D = cf.head_dim, QD = m->hq_l * D, KD = m->hkv_l * D, I = m->inter_l;
+    const bool decode = S <= 8;
+    const bool tp = m->tp_size > 1;
+    if (S > w.cap_rows) throw Error(QW_ERR_INFERENCE, "workspace too small for forward");
+
+    QW_CUDA(launch_embed(d_ids, S, m->embed.w, m->embed.s, m->embed.b, H, cf.vocab, w.x, m->d_err, st, true));
+
+    AttnArgs aa;
+    std::memset(&aa, 0, sizeof(aa));
+    aa.q = w.q;
+    aa.k = w.k;
+    aa.v = w.v;
+    aa.ldq = QD;
+    aa.ldk = KD;
+    aa.ldv = KD;
+    aa.eps = cf.eps;
+    aa.rope_cos = m->rope_cos;
+    aa.rope_sin = m->rope_sin;
+    aa.max_pos = c->max_pos;
+    aa.seq_len = c->d_seq_len;
+    aa.S = S;
+    aa.Hq = m->hq_l;
+    aa.Hkv = m->hkv_l;
+    aa.scale = 1.0f / sqrtf((float)D);
+    aa.part = w.attn_part;
+    aa.counters = w.attn_counters;
+    aa.out = w.attn;
+    aa.ldo = QD;
+    aa.nsplit = std::max(1, std::min(2 * m->num_sms, m->num_sms / std::max(1, m->hkv_l)));
+    aa.err = m->d_err;
+
+    for (int l = 0; l < cf.layers; ++l) {
+        Layer& L = m->layers[l];
+        aa.q_norm_w = L.q_norm;
+        aa.k_norm_w = L.k_norm;
+        aa.kcache = c->kl(l);
+        aa.vcache = c->vl(l);
+        const bf16* xin = w.x;
+        if (!decode) {
+            QW_CUDA(launch_rmsnorm(w.x, L.in_norm, w.h, S, H, cf.eps, st));
+            xin = w.h;
+        }
+        {
+            QmmArgs a = qmm_base(m, xin, H, S, H);
+            if (decode) a.norm_w = L.in_norm;
+            a.seg[0] = seg_of(L.q, w.q, QD);
+            a.seg[1] = seg_of(L.k, w.k, KD);
+            a.seg[2] = seg_of(L.v, w.v, KD);
+            a.nseg = 3;
+            a.epi = EPI_STORE;
+            qmm(m, a, st);
+        }
+        if (decode) {
+            QW_CUDA(launch_attn_decode(aa, st, true));
+        } else {
+            QW_CUDA(launch_qk_norm_rope_kvwrite(aa, w.qr, st));
+            QW_CUDA(launch_attn_prefill(aa, w.qr, st));
+        }
+        {
+            QmmArgs a = qmm_base(m, w.attn, QD, S, QD);
+            a.seg[0] = seg_of(L.o, tp ? (void*)w.f32 : (void*)w.x, H);
+            a.nseg = 1;
+            a.epi = tp ? EPI_F32 : EPI_RESID;
+            qmm(m, a, st);
+            if (tp) {
+                tp_allreduce_sum_f32(m, w.f32, (size_t)S * H, st);
+                QW_CUDA(launch_resid_add_f32(w.x, w.f32, S * H, st));
+            }
+        }
+        xin = w.x;
+        if (!decode) {
+            QW_CUDA(launch_rmsnorm(w.x, L.post_norm, w.h, S, H, cf.eps, st));
+            xin = w.h;
+        }
+        {
+            QmmArgs a = qmm_base(m, xin, H, S, H);
+            if (decode) a.norm_w = L.post_norm;
+            a.seg[0] = seg_of(L.gate, w.mlp, I);
+            a.seg[1] = seg_of(L.up, w.mlp, I);
+            a.nseg = 2;
+            a.epi = EPI_SWIGLU;
+            qmm(m, a, st);
+        }
+        {
+            QmmArgs a = qmm_base(m, w.mlp, I, S, I);
+            a.seg[0] = seg_of(L.down, tp ? (void*)w.f32 : (void*)w.x, H);
+            a.nseg = 1;
+            a.epi = tp ? EPI_F32 : EPI_RESID;
+            qmm(m, a, st);
+            if (tp) {
+                tp_allreduce_sum_f32(m, w.f32, (size_t)S * H, st);
+                QW_CUDA(launch_resid_add_f32(w.x, w.f32, S * H, st));
+            }
+        }
+    }
+
+    if (logits_mode) {
+        const int rows = logits_mode == 2 ? S : 1;
+        const bf16* xin = w.x + (size_t)(S - rows) * H;
+        const bool vocab_split = tp && !cf.tied;
+        if (rows > w.cap_logits) throw Error(QW_ERR_INFERENCE, "logits workspace too small");
+        if (rows <= 8) {
+            QmmArgs a = qmm_base(m, xin, H, rows, H);
+            a.norm_w = m->final_norm;
+            a.seg[0] = seg_of(m->lm_head, w.logits, m->vocab_l);
+            a.nseg = 1;
+            a.epi = EPI_LOGITS;
+            a.store_logits = store_logits ? 1 : 0;
+            a.amax_out = d_argmax;
+            a.amax_row_offset = vocab_split ? m->tp_rank * m->vocab_l : 0;
+            a.amax_key_out = vocab_split ? w.amax_keys : nullptr;
+            qmm(m, a, st);
+        } else {
+            QW_CUDA(launch_rmsnorm(xin, m->final_norm, w.h, rows, H, cf.eps, st));
+            QmmArgs a = qmm_base(m, w.h, H, rows, H);
+            a.seg[0] = seg_of(m->lm_head, w.logits, m->vocab_l);
+            a.nseg = 1;
+            a.epi = EPI_STORE;
+            qmm(m, a, st);
+            QW_CUDA(launch_argmax_rows(w.logits, rows, m->vocab_l, d_argmax, vocab_split ? w.amax_keys : nullptr,
+                                       vocab_split ? m->tp_rank * m->vocab_l : 0, st));
+        }
+        if (vocab_split) {
+            // global argmax across the vocab shards: max over packed (logit, index) keys
+            tp_allreduce_max_u64(m, w.amax_keys, (size_t)rows, st);
+            QW_CUDA(launch_keys_to_index(w.amax_keys, rows, d_argmax, st));
+        }
+    }
+    QW_CUDA(launch_step_finish(c->d_seq_len, S, d_argmax, ctl, next_tok, out, gate, st, true));
+}
+
+void generate_greedy_dev(qw_model* m, qw_cache* c, int n_prompt, int max_new, const std::vector<int>& eos,
+                         qw_gen_stats* stats, cudaStream_t st) {
+    Workspace& w = m->ws;
+    if (n_prompt + max_new > c->max_pos)
+        throw Error(QW_ERR_KV_EXHAUSTED, "KV cache exhausted: requested " + std::to_string(n_prompt + max_new) +
+                                             " positions, max " + std::to_string(c->max_pos));
+    if (max_new > w.out_cap) throw Error(QW_ERR_INVALID_ARG, "max_new too large");
+    StepCtl ctl;
+    std::memset(&ctl, 0, sizeof(ctl));
+    ctl.max_new = max_new;
+    ctl.n_eos = (int)std::min<size_t>(eos.size(), 8);
+    for (int i = 0; i < ctl.n_eos; ++i) ctl.eos[i] = eos[i];
+    QW_CUDA(cudaMemcpyAsync(w.ctl, &ctl, sizeof(ctl), cudaMemcpyHostToDevice, st));
+    int zero = 0;
+    QW_CUDA(cudaMemcpyAsync(c->d_seq_len, &zero, sizeof(int), cudaMemcpyHostToDevice, st));
+    c->seq_len = 0;
+
+    cudaEvent_t e0, e1, e2;
+    QW_CUDA(cudaEventCreate(&e0));
+    QW_CUDA(cudaEventCreate(&e1));
+    QW_CUDA(cudaEventCreate(&e2));
+    QW_CUDA(cudaEventRecord(e0, st));
+    forward_dev(m, c, w.ids, n_prompt, 1, false, w.argmax, st, w.ctl, w.next_tok, w.out);
+    QW_CUDA(cudaEventRecord(e1, st));
+    if (max_new > 1) {
+        if (!c->step_graph || c->step_graph_gen != w.generation) {
+            if (c->step_graph) {
+                cudaGraphExecDestroy(c->step_graph);
+                c->step_graph = nullptr;
+            }
+            cudaGraph_t g;
+            QW_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+            try {
+                forward_dev(m, c, w.next_tok, 1, 1, false, w.argmax, st, w.ctl, w.next_tok, w.out);
+            } catch (...) {
+                cudaStreamEndCapture(st, &g);
+                throw;
+            }
+            QW_CUDA(cudaStreamEndCapture(st, &g));
+            QW_CUDA(cudaGraphInstantiate(&c->step_graph, g, 0));
+            cudaGraphDestroy(g);
+            c->step_graph_gen = w.generation;
+        }
+        for (int i = 1; i < max_new; ++i) QW_CUDA(cudaGraphLaunch(c->step_graph, st));
+    }
+    QW_CUDA(cudaEventRecord(e2, st));
+    QW_CUDA(cudaStreamSynchronize(st));
+    QW_CUDA(cudaMemcpy(&ctl, w.ctl, sizeof(ctl), cudaMemcpyDeviceToHost));
+    float pf = 0, dc = 0;
+    cudaEventElapsedTime(&pf, e0, e1);
+    cudaEventElapsedTime(&dc, e1, e2);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaEventDestroy(e2);
+    QW_CUDA(cudaMemcpy(&c->seq_len, c->d_seq_len, sizeof(int), cudaMemcpyDeviceToHost));
+    if (stats) {
+        stats->prompt_tokens = n_prompt;
+        stats->completion_tokens = ctl.produced;
+        stats->finish_reason = ctl.finish;
+        stats->prefill_ms = pf;
+        stats->decode_ms = dc;
+    }
+}
+
+}  // namespace qw

@@ -1,0 +1,111 @@
+// Kernel launch interface shared by the runtime (host) and the .cu kernel files.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace qw {
+
+// Output treatment of a quantized matmul.
+enum Epi : int {
+    EPI_STORE = 0,   // y = bf16(acc)
+    EPI_RESID = 1,   // y = bf16(y + bf16(acc))             (o_proj / down_proj + residual)
+    EPI_SWIGLU = 2,  // y = bf16(bf16(g*bf16(sigmoid(g))) * u), g/u = bf16(gate/up acc)
+    EPI_LOGITS = 3,  // bf16 logits (optional store) + fused argmax per row
+    EPI_F32 = 4,     // y_f32 = acc (tensor-parallel partial sums)
+};
+
+// One quantized linear segment [n rows x K] (MLX layout).
+struct QSeg {
+    const uint32_t* w;  // [n, K/8]
+    const bf16* s;      // [n, K/64]
+    const bf16* b;      // [n, K/64]
+    void* y;            // output base (bf16 or fp32), element (m, row) at y[m*ldy + row]
+    int n;
+    int ldy;
+    int rb0;            // first row block of this segment in the launch grid
+};
+
+struct QmmArgs {
+    const bf16* x;   // [M, ldx] activations
+    int ldx;
+    int M, K;
+    const bf16* norm_w;  // optional RMSNorm weight [K] applied to x first (decode path)
+    float eps;
+    QSeg seg[3];
+    int nseg;
+    int epi;
+    int nrb;             // row blocks in the grid (gridDim.x)
+    // split-K scratch (decode path)
+    float* partial;
+    size_t partial_cap;  // floats available at `partial`
+    unsigned* counters;  // >= nrb entries, zero between launches
+    // fused argmax (EPI_LOGITS)
+    unsigned long long* amax_partial;  // [nrb, M]
+    unsigned* amax_counter;            // one counter, zero between launches
+    int* amax_out;                     // [M]
+    unsigned long long* amax_key_out;  // optional [M]: packed (logit, index) keys
+    int store_logits;
+    int amax_row_offset;               // global index of row 0 (vocab-parallel shards)
+    int* err;
+};
+
+// Decode / verify path: M <= 8.  Picks split-K and launches qgemv.
+cudaError_t launch_qgemv(QmmArgs a, cudaStream_t st, bool pdl, int num_sms);
+// Prefill path: M > 8 (no norm prologue, no argmax; EPI_STORE/RESID/SWIGLU/F32).
+cudaError_t launch_qgemm(QmmArgs a, cudaStream_t st, int num_sms);
+
+// ---- other kernels ------------------------------------------------------
+struct AttnArgs {
+    const bf16* q; const bf16* k; const bf16* v;   // [S, ldq] etc.
+    int ldq, ldk, ldv;
+    const bf16* q_norm_w; const bf16* k_norm_w; float eps;
+    const float* rope_cos; const float* rope_sin;  // [max_pos, 64]
+    bf16* kcache; bf16* vcache;                    // this layer: [Hkv, max_pos, 128]
+    int max_pos;
+    const int* seq_len;                            // device offset (positions already cached)
+    int S, Hq, Hkv;                                // local heads
+    float scale;
+    float* part;          // [Hkv, nsplit, R, 130]
+    unsigned* counters;   // [Hkv]
+    bf16* out; int ldo;   // [S, Hq*128]
+    int nsplit;
+    int* err;
+};
+cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl);
+// prefill: q/k norm + rope + cache write for all S rows, roped q to qout
+cudaError_t launch_qk_norm_rope_kvwrite(const AttnArgs& a, bf16* qout, cudaStream_t st);
+cudaError_t launch_attn_prefill(const AttnArgs& a, const bf16* qroped, cudaStream_t st);
+
+cudaError_t launch_embed(const int* ids, int S, const uint32_t* w, const bf16* s, const bf16* b,
+                         int H, int vocab, bf16* x, int* err, cudaStream_t st, bool pdl);
+cudaError_t launch_rmsnorm(const bf16* x, const bf16* w, bf16* y, int S, int H, float eps,
+                           cudaStream_t st);
+cudaError_t launch_argmax_rows(const bf16* logits, int rows, int V, int* out, unsigned long long* keys_out,
+                               int index_offset, cudaStream_t st);
+cudaError_t launch_keys_to_index(const unsigned long long* keys, int n, int* out, cudaStream_t st);
+cudaError_t launch_resid_add_f32(bf16* x, const float* p, int n, cudaStream_t st);
+
+// Random-init: fill a quantized tensor [rows, K] (rows r0.. of a [*, Kfull] tensor,
+// columns k0.. of it) from the seeded generator.
+cudaError_t launch_init_qweight(uint32_t* w, bf16* s, bf16* b, int rows, int K, int row0, int k0,
+                                int Kfull, uint64_t key, float mult, cudaStream_t st);
+cudaError_t launch_init_norm(bf16* w, int n, uint64_t key, float mult, int ones, cudaStream_t st);
+
+// ---- step control (device-side generation loops) ----------------------
+struct StepCtl {
+    int produced;    // tokens picked so far (includes a terminating EOS)
+    int n_out;       // tokens written to out
+    int done;        // 1 once EOS or max_new reached
+    int finish;      // 0 length, 1 stop
+    int max_new;
+    int n_eos;
+    int eos[8];
+};
+// After a forward of S rows: seq_len += S (skipped while *gate != 0); greedy
+// loop bookkeeping when ctl != null.
+cudaError_t launch_step_finish(int* seq_len, int S, const int* argmax, StepCtl* ctl, int* next_tok,
+                               int* out, const int* gate, cudaStream_t st, bool pdl);
+
+}  // namespace qw

@@ -1,0 +1,174 @@
+/* qwen3_b200.h -- C ABI of the B200 (sm_100a) Qwen3 4-bit decode library.
+ *
+ * Drop-in boundary for base-mlx's decode hot path.  Every entry point replaces
+ * one piece of the Rust crate base-mlx-core (paths relative to the
+ * flakerimi/base-mlx project root):
+ *
+ *   qw_model_load            Architecture::load / Qwen3::load      model.rs:36-43, model/qwen3.rs:194-295
+ *   qw_model_init_random     (benchmark helper: seeded random-init weights in the same layout)
+ *   qw_cache_new             Architecture::new_cache / KvCache::new model.rs:45-51, model/qwen3.rs:127-129
+ *   qw_cache_reset           ArchitectureCache::reset              model.rs:88-96, model/qwen3.rs:130-134
+ *   qw_cache_truncate        ArchitectureCache::truncate           model.rs:98-106, model/qwen3.rs:150-161
+ *   qw_forward               Architecture::forward / forward_multi model.rs:53-80, model/qwen3.rs:297-312
+ *   qw_kv_slice_update       mlx_ext::slice_update on a cache tensor mlx_ext.rs:36-64
+ *   qw_quantized_matmul      mlx_rs::ops::quantized_matmul(transpose=true, 64, 4) model/qwen3.rs:30-41
+ *   qw_generate_greedy       LoadedModel::generate_text (greedy)   engine.rs:149-201
+ *   qw_spec_generate         speculative::generate                 speculative.rs:57-286
+ *   qw_check_compatible      speculative::check_compatible         speculative.rs:40-54
+ *
+ * Conventions
+ *   - every function returns an int status: QW_OK (0) or a negative QW_ERR_*
+ *     code; qw_last_error() copies the thread's last error message.  The codes
+ *     map onto the crate's Error enum (error.rs:6-32): QW_ERR_MODEL_LOAD ->
+ *     Error::ModelLoad, QW_ERR_INVALID_CONFIG -> Error::InvalidConfig, every
+ *     other code -> Error::Inference.
+ *   - handles are opaque and owned by the library; one handle is used by one
+ *     thread at a time (the crate serialises requests behind a Mutex,
+ *     base-mlx-server/src/state.rs:18-27).
+ *   - token ids are uint32; logits are bf16 bit patterns (uint16).
+ *   - pointers named *_host are host memory; qw_quantized_matmul takes device
+ *     pointers (it stands in for an op on MLX arrays that already live on the GPU).
+ *   - there is no CPU fallback: without a usable sm_100 GPU every compute call
+ *     fails with QW_ERR_CUDA.
+ */
+#ifndef QWEN3_B200_H
+#define QWEN3_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define QW_API __attribute__((visibility("default")))
+#else
+#define QW_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QW_OK 0
+#define QW_ERR_INVALID_ARG -1     /* bad pointer / size / shape */
+#define QW_ERR_INVALID_CONFIG -2  /* Error::InvalidConfig */
+#define QW_ERR_MODEL_LOAD -3      /* Error::ModelLoad (missing / unmapped tensors, io) */
+#define QW_ERR_INFERENCE -4       /* Error::Inference */
+#define QW_ERR_KV_EXHAUSTED -5    /* Error::Inference("KV cache exhausted ...") qwen3.rs:423-428 */
+#define QW_ERR_CUDA -6            /* CUDA runtime error or no usable GPU */
+#define QW_ERR_UNSUPPORTED -7     /* e.g. bits != 4, group_size != 64, model_type != qwen3 */
+#define QW_ERR_DEVICE_FLAG -8     /* a kernel raised its device-side error flag */
+
+typedef struct qw_model qw_model;
+typedef struct qw_cache qw_cache;
+
+typedef struct qw_model_info {
+    int32_t num_layers, hidden, intermediate, num_heads, num_kv_heads, head_dim;
+    int32_t vocab, tied_embeddings, tp_rank, tp_size;
+    float rms_eps, rope_theta;
+    uint64_t weight_bytes;  /* device bytes of this rank's quantized weights + norms */
+} qw_model_info;
+
+typedef struct qw_gen_stats {
+    int32_t prompt_tokens;
+    int32_t completion_tokens; /* counts a terminating EOS, as GenerationResult does (engine.rs:178) */
+    int32_t finish_reason;     /* 0 = "length", 1 = "stop" */
+    int32_t pad;
+    double prefill_ms, decode_ms; /* device time (CUDA events) */
+} qw_gen_stats;
+
+typedef struct qw_spec_stats {
+    int32_t iters, proposed, accepted, completion_tokens;
+    int32_t finish_reason, pad;
+    double prefill_ms, total_ms;         /* device time of the whole call */
+    double draft_ms_mean, verify_ms_mean, accept_ms_mean; /* speculative.rs:242-264 */
+} qw_spec_stats;
+
+/* Copy the calling thread's last error message (NUL-terminated, truncated to len). */
+QW_API int qw_last_error(char* buf, size_t len);
+
+/* Library build / runtime version string. */
+QW_API int qw_version(char* buf, size_t len);
+
+/* ---- models ---------------------------------------------------------- */
+
+/* Load an MLX-format Qwen3 checkpoint directory (config.json + *.safetensors).
+ * tp_rank/tp_size select this rank's shard of a tensor-parallel split (1 = whole model). */
+QW_API int qw_model_load(const char* dir, int device, int tp_rank, int tp_size, qw_model** out);
+
+/* Seeded random-init model with the tensors of `config_json` (a config.json
+ * string), generated on the device: N(0,0.02) weights quantized affine 4-bit
+ * g64; norm_mode 0 = norm weights 1.0, 1 = bf16(1 + N(0,0.1)). */
+QW_API int qw_model_init_random(const char* config_json, uint64_t seed, int norm_mode, int device,
+                                int tp_rank, int tp_size, qw_model** out);
+
+/* Frees the model and every cache still attached to it. */
+QW_API int qw_model_free(qw_model* m);
+QW_API int qw_model_info_get(const qw_model* m, qw_model_info* out);
+
+/* Copy one named tensor of this rank (MLX name, e.g. "model.layers.0.mlp.up_proj.scales")
+ * to host memory.  bytes must equal the tensor's size. */
+QW_API int qw_model_export_tensor(const qw_model* m, const char* name, void* dst_host, size_t bytes);
+
+/* The CUDA stream the model's work runs on (cudaStream_t as void*). */
+QW_API int qw_model_stream(const qw_model* m, void** stream_out);
+
+/* Tensor parallel: attach an NCCL communicator (ncclUniqueId bytes, 128) to a
+ * model loaded with tp_size > 1.  Must be called on every rank before forward. */
+QW_API int qw_model_tp_attach(qw_model* m, const void* nccl_unique_id, int rank, int size);
+
+QW_API int qw_check_compatible(const qw_model* target, const qw_model* draft);
+
+/* ---- KV cache --------------------------------------------------------- */
+
+QW_API int qw_cache_new(qw_model* m, int max_pos, qw_cache** out);
+QW_API int qw_cache_free(qw_cache* c);
+QW_API int qw_cache_reset(qw_cache* c);
+/* Roll back to the first new_len positions (no-op when already shorter). */
+QW_API int qw_cache_truncate(qw_cache* c, int new_len);
+QW_API int qw_cache_len(const qw_cache* c, int* out);
+
+/* cache[layer].{k|v}[:, start:stop, :] = update_host ([kv_heads_local, stop-start, head_dim] bf16). */
+QW_API int qw_kv_slice_update(qw_cache* c, int layer, int which_v, const uint16_t* update_host,
+                              int start, int stop);
+/* Read cache[layer].{k|v}[:, start:stop, :] back to the host. */
+QW_API int qw_kv_read(const qw_cache* c, int layer, int which_v, uint16_t* dst_host, int start, int stop);
+
+/* ---- forward ------------------------------------------------------------ */
+
+/* Run `n` tokens through the model at the cache's current length and extend it.
+ * all_rows = 0 -> Architecture::forward (last row), 1 -> forward_multi (every row).
+ * logits_out_host (optional) receives bf16 logits [rows, vocab_local];
+ * argmax_out_host (optional) receives the argmax of each returned row. */
+QW_API int qw_forward(qw_model* m, qw_cache* c, const uint32_t* ids_host, int n, int all_rows,
+                      uint16_t* logits_out_host, uint32_t* argmax_out_host);
+
+/* ---- generation --------------------------------------------------------- */
+
+/* Greedy generation (temperature 0).  out_host receives up to max_new ids (a
+ * terminating EOS is not written); *n_out = ids written.  eos == NULL uses the
+ * model config's eos ids (or 151645/151643 when the config has none). */
+QW_API int qw_generate_greedy(qw_model* m, const uint32_t* prompt_host, int n_prompt, int max_new,
+                              const uint32_t* eos, int n_eos, uint32_t* out_host, int* n_out,
+                              qw_gen_stats* stats);
+
+/* Greedy speculative decoding: k drafted tokens per iteration, one (k+1)-row
+ * target verify, on-device accept and rollback.  k = 3 reproduces the
+ * reference loop (SPEC_K = 4).  With forced_seq != NULL and force_p > 0 each
+ * drafted token is replaced, with probability force_p, by forced_seq[pos]
+ * (the plain-greedy target sequence) -- the benchmark's acceptance control. */
+QW_API int qw_spec_generate(qw_model* target, qw_model* draft, const uint32_t* prompt_host, int n_prompt,
+                            int max_new, int k, float force_p, uint64_t seed,
+                            const uint32_t* forced_seq_host, int n_forced, const uint32_t* eos, int n_eos,
+                            uint32_t* out_host, int* n_out, qw_spec_stats* stats);
+
+/* ---- standalone op ----------------------------------------------------- */
+
+/* y[M,N] (bf16) = x[M,K] (bf16) . dequant(W)^T with W uint32 [N,K/8],
+ * scales/biases bf16 [N,K/64]; device pointers; stream may be NULL (default
+ * stream).  Only group_size 64 and bits 4 are supported. */
+QW_API int qw_quantized_matmul(const void* x, const void* w, const void* scales, const void* biases,
+                               void* y, int M, int N, int K, int group_size, int bits, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QWEN3_B200_H */
