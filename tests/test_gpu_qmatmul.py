@@ -1,0 +1,69 @@
+"""quantized_matmul parity: CUDA (qgemv M<=8 / qgemm M>8) vs the CPU oracle.
+
+Shapes are BASELINE config 2 (Qwen3-4B projections) plus odd-sized edge cases.
+Tolerance: the CUDA path and the oracle both accumulate in fp32 and round the
+output once to bf16, so they agree to within one bf16 rounding of values of
+the output's magnitude: |gpu - ref| <= 1e-2 * max|ref| + 1e-3 elementwise, and
+at least 99% of elements bit-identical.
+"""
+import numpy as np
+import pytest
+
+from oracle import numerics as nm
+
+pytestmark = pytest.mark.gpu
+
+SHAPES_4B = [(2560, 4096), (2560, 1024), (4096, 2560), (2560, 9728), (9728, 2560)]
+
+
+def _case(M, K, N, seed):
+    rng = np.random.default_rng(seed)
+    w, s, b = nm.quantized_weight(seed, 99, N, K)
+    x = nm.bf16_round(rng.standard_normal((M, K)).astype(np.float32))
+    return x, w, s, b
+
+
+def _run_gpu(x, w, s, b):
+    import torch
+    import qwen3_b200 as q
+    dev = torch.device("cuda:0")
+    M, K = x.shape
+    N = w.shape[0]
+    xt = torch.from_numpy(nm.f32_to_bf16_bits(x).view(np.int16)).to(dev)
+    wt = torch.from_numpy(w.view(np.int32)).to(dev)
+    st = torch.from_numpy(s.view(np.int16)).to(dev)
+    bt = torch.from_numpy(b.view(np.int16)).to(dev)
+    yt = torch.zeros((M, N), dtype=torch.int16, device=dev)
+    q.quantized_matmul(xt.data_ptr(), wt.data_ptr(), st.data_ptr(), bt.data_ptr(), yt.data_ptr(), M, N, K,
+                       stream=torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    return nm.bf16_bits_to_f32(yt.cpu().numpy().view(np.uint16))
+
+
+def _check(y, ref):
+    tol = 1e-2 * np.abs(ref).max() + 1e-3
+    err = np.abs(y - ref)
+    assert err.max() <= tol, f"max err {err.max()} > {tol}"
+    assert (y == ref).mean() >= 0.99, f"only {(y == ref).mean():.4f} bit-identical"
+
+
+@pytest.mark.parametrize("M", [1, 5, 128])
+@pytest.mark.parametrize("K,N", SHAPES_4B)
+def test_qmatmul_4b_shapes(M, K, N):
+    x, w, s, b = _case(M, K, N, seed=1000 + K + N)
+    ref = nm.bf16_round(x @ nm.dequantize(w, s, b).T)
+    _check(_run_gpu(x, w, s, b), ref)
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 64, 16), (3, 192, 40), (8, 320, 96), (9, 128, 48), (33, 256, 200),
+                                   (2048, 2560, 1024)])
+def test_qmatmul_edges(M, K, N):
+    x, w, s, b = _case(M, K, N, seed=7 + M + K + N)
+    ref = nm.bf16_round(x @ nm.dequantize(w, s, b).T)
+    _check(_run_gpu(x, w, s, b), ref)
+
+
+def test_qmatmul_lm_head_m1():
+    x, w, s, b = _case(1, 2560, 151936, seed=5)
+    ref = nm.bf16_round(x @ nm.dequantize(w, s, b).T)
+    _check(_run_gpu(x, w, s, b), ref)
