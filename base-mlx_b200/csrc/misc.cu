@@ -128,7 +128,7 @@ __global__ void step_finish_kernel(int* seq_len, int S, const int* argmax, StepC
     }
     if (ctl->done) return;
     *seq_len += S;
-    const int tok = argmax[S - 1];
+    const int tok = argmax[0];  // the greedy loop computes logits of the last row only
     ctl->produced += 1;
     bool eos = false;
     for (int i = 0; i < ctl->n_eos; ++i) eos |= (ctl->eos[i] == tok);
