@@ -51,21 +51,30 @@ QW_DEV void norm_rope_row(const bf16* row, const bf16* nw, float eps, const floa
 // CTA handles the G = Hq/Hkv query heads of one kv head (R = G*S rows) over one
 // contiguous slice of key positions, writes an unnormalised partial
 // (max, sum, o[128]) per row, and the last CTA of the kv head merges them.
-// The CTA whose slice holds the new positions normalises + rotates + writes
-// their k/v into the cache first.
+// Cached K/V rows stream through two 64-key shared-memory tiles with 16-byte
+// asynchronous copies (K chunks XOR-swizzled by row, so a thread-per-key read
+// is bank-conflict free); the new positions' k/v are normalised + rotated by
+// the CTA that owns them, written to the cache and placed into the tile
+// directly.
 // ---------------------------------------------------------------------------
 template <int RMAX>
+struct DecSmem {
+    float qs[RMAX][D];
+    float sc[RMAX][TILE];
+    float mrow[RMAX], lrow[RMAX], alph[RMAX];
+    bf16 kt[2][TILE][D];
+    bf16 vt[2][TILE][D];
+    bf16 nk[8][D], nv[8][D];
+    int last;
+};
+
+template <int RMAX>
 __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
-    extern __shared__ __align__(16) float sm[];
+    extern __shared__ __align__(16) unsigned char smraw[];
+    DecSmem<RMAX>& sm = *reinterpret_cast<DecSmem<RMAX>*>(smraw);
     const int kvh = blockIdx.x, split = blockIdx.y, nsplit = gridDim.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int S = a.S, G = a.Hq / a.Hkv, R = G * S;
-    float* qs = sm;                  // [RMAX][D]
-    float* sc = qs + RMAX * D;       // [RMAX][TILE]
-    float* mrow = sc + RMAX * TILE;  // [RMAX]
-    float* lrow = mrow + RMAX;
-    float* alph = lrow + RMAX;
-    __shared__ int s_last;
 
     pdl_wait();
     pdl_launch_dependents();
@@ -79,6 +88,22 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
     per = (per + 15) & ~15;
     const int lo = split * per;
     const int hi = min(T, lo + per);
+    const int ntiles = hi > lo ? (hi - lo + TILE - 1) / TILE : 0;
+    const bf16* kbase = a.kcache + (size_t)kvh * a.max_pos * D;
+    const bf16* vbase = a.vcache + (size_t)kvh * a.max_pos * D;
+
+    // cached (old) rows of a tile -> shared memory, asynchronously
+    auto load_tile = [&](int buf, int j0) {
+        const int nold = max(0, min(j0 + TILE, min(hi, off)) - j0);
+        for (int idx = tid; idx < nold * 16; idx += 128) {
+            const int r = idx >> 4, c = idx & 15;
+            cp_async16(&sm.kt[buf][r][(c ^ (r & 15)) * 8], kbase + (size_t)(j0 + r) * D + c * 8);
+            cp_async16(&sm.vt[buf][r][c * 8], vbase + (size_t)(j0 + r) * D + c * 8);
+        }
+        cp_async_commit();
+    };
+    if (ntiles > 0) load_tile(0, lo);
+    if (ntiles > 1) load_tile(1, lo + TILE);
 
     // queries: q_norm + rope
     for (int r = warp; r < R; r += 4) {
@@ -87,38 +112,55 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
         float o[4];
         norm_rope_row(a.q + (size_t)i * a.ldq + h * D, a.q_norm_w, a.eps, a.rope_cos + (size_t)pos * HALF,
                       a.rope_sin + (size_t)pos * HALF, lane, o);
-        qs[r * D + 2 * lane] = o[0];
-        qs[r * D + 2 * lane + 1] = o[1];
-        qs[r * D + HALF + 2 * lane] = o[2];
-        qs[r * D + HALF + 2 * lane + 1] = o[3];
+        sm.qs[r][2 * lane] = o[0];
+        sm.qs[r][2 * lane + 1] = o[1];
+        sm.qs[r][HALF + 2 * lane] = o[2];
+        sm.qs[r][HALF + 2 * lane + 1] = o[3];
     }
-    // new keys / values owned by this slice
+    // new keys / values owned by this slice: cache write + local copy
     const int nlo = max(lo, off), nhi = min(hi, T);
     for (int p = nlo + warp; p < nhi; p += 4) {
         const int i = p - off;
         float o[4];
         norm_rope_row(a.k + (size_t)i * a.ldk + kvh * D, a.k_norm_w, a.eps, a.rope_cos + (size_t)p * HALF,
                       a.rope_sin + (size_t)p * HALF, lane, o);
+        const uint32_t k01 = pack_bf16x2(o[0], o[1]), k23 = pack_bf16x2(o[2], o[3]);
         bf16* kd = a.kcache + ((size_t)kvh * a.max_pos + p) * D;
-        *reinterpret_cast<uint32_t*>(kd + 2 * lane) = pack_bf16x2(o[0], o[1]);
-        *reinterpret_cast<uint32_t*>(kd + HALF + 2 * lane) = pack_bf16x2(o[2], o[3]);
+        *reinterpret_cast<uint32_t*>(kd + 2 * lane) = k01;
+        *reinterpret_cast<uint32_t*>(kd + HALF + 2 * lane) = k23;
+        *reinterpret_cast<uint32_t*>(&sm.nk[i][2 * lane]) = k01;
+        *reinterpret_cast<uint32_t*>(&sm.nk[i][HALF + 2 * lane]) = k23;
         const uint2 vv = *reinterpret_cast<const uint2*>(a.v + (size_t)i * a.ldv + kvh * D + 4 * lane);
         *reinterpret_cast<uint2*>(a.vcache + ((size_t)kvh * a.max_pos + p) * D + 4 * lane) = vv;
+        *reinterpret_cast<uint2*>(&sm.nv[i][4 * lane]) = vv;
     }
     if (tid < RMAX) {
-        mrow[tid] = -INFINITY;
-        lrow[tid] = 0.f;
+        sm.mrow[tid] = -INFINITY;
+        sm.lrow[tid] = 0.f;
     }
     __syncthreads();
 
     float o_acc[RMAX];
 #pragma unroll
     for (int r = 0; r < RMAX; ++r) o_acc[r] = 0.f;
-
-    const bf16* kbase = a.kcache + (size_t)kvh * a.max_pos * D;
-    const bf16* vbase = a.vcache + (size_t)kvh * a.max_pos * D;
     constexpr int RH = (RMAX + 1) / 2;
-    for (int j0 = lo; j0 < hi; j0 += TILE) {
+
+    for (int it = 0; it < ntiles; ++it) {
+        const int buf = it & 1, j0 = lo + it * TILE;
+        if (it + 1 < ntiles)
+            cp_async_wait<1>();
+        else
+            cp_async_wait<0>();
+        // new positions of this tile come from the locally computed rows
+        for (int idx = tid; idx < TILE * 16; idx += 128) {
+            const int r = idx >> 4, c = idx & 15, j = j0 + r;
+            if (j >= off && j < hi) {
+                *reinterpret_cast<uint4*>(&sm.kt[buf][r][(c ^ (r & 15)) * 8]) =
+                    *reinterpret_cast<const uint4*>(&sm.nk[j - off][c * 8]);
+                *reinterpret_cast<uint4*>(&sm.vt[buf][r][c * 8]) = *reinterpret_cast<const uint4*>(&sm.nv[j - off][c * 8]);
+            }
+        }
+        __syncthreads();
         // scores: thread -> key (tid & 63), rows of parity (tid >> 6)
         {
             const int jj = tid & (TILE - 1), par = tid >> 6;
@@ -127,18 +169,17 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
 #pragma unroll
             for (int q = 0; q < RH; ++q) acc[q] = 0.f;
             if (j < hi) {
-                const uint4* kp = reinterpret_cast<const uint4*>(kbase + (size_t)j * D);
-#pragma unroll 1
+#pragma unroll 4
                 for (int dc = 0; dc < D / 8; ++dc) {
-                    const uint4 u = kp[dc];
+                    const uint4 u = *reinterpret_cast<const uint4*>(&sm.kt[buf][jj][(dc ^ (jj & 15)) * 8]);
                     const float kf[8] = {bits_lo_f(u.x), bits_hi_f(u.x), bits_lo_f(u.y), bits_hi_f(u.y),
                                          bits_lo_f(u.z), bits_hi_f(u.z), bits_lo_f(u.w), bits_hi_f(u.w)};
 #pragma unroll
                     for (int q = 0; q < RH; ++q) {
                         const int r = par + 2 * q;
                         if (r < R) {
-                            const float4 q0 = *reinterpret_cast<const float4*>(qs + r * D + dc * 8);
-                            const float4 q1 = *reinterpret_cast<const float4*>(qs + r * D + dc * 8 + 4);
+                            const float4 q0 = *reinterpret_cast<const float4*>(&sm.qs[r][dc * 8]);
+                            const float4 q1 = *reinterpret_cast<const float4*>(&sm.qs[r][dc * 8 + 4]);
                             float s = acc[q];
                             s = fmaf(q0.x, kf[0], s); s = fmaf(q0.y, kf[1], s);
                             s = fmaf(q0.z, kf[2], s); s = fmaf(q0.w, kf[3], s);
@@ -155,16 +196,16 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
                 if (r < R) {
                     const int i = r % S;
                     const bool ok = (j < hi) && (j <= off + i);
-                    sc[r * TILE + jj] = ok ? acc[q] * a.scale : -INFINITY;
+                    sm.sc[r][jj] = ok ? acc[q] * a.scale : -INFINITY;
                 }
             }
         }
         __syncthreads();
         // online softmax update, one warp per row
         for (int r = warp; r < R; r += 4) {
-            const float s0 = sc[r * TILE + lane], s1 = sc[r * TILE + lane + 32];
+            const float s0 = sm.sc[r][lane], s1 = sm.sc[r][lane + 32];
             const float mx = warp_max(fmaxf(s0, s1));
-            const float mold = mrow[r];
+            const float mold = sm.mrow[r];
             const float mnew = fmaxf(mold, mx);
             float p0 = 0.f, p1 = 0.f, al = 1.f;
             if (mnew != -INFINITY) {
@@ -172,13 +213,13 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
                 p1 = expf(s1 - mnew);
                 al = expf(mold - mnew);
             }
-            sc[r * TILE + lane] = p0;
-            sc[r * TILE + lane + 32] = p1;
+            sm.sc[r][lane] = p0;
+            sm.sc[r][lane + 32] = p1;
             const float ps = warp_sum(p0 + p1);
             if (lane == 0) {
-                lrow[r] = lrow[r] * al + ps;
-                mrow[r] = mnew;
-                alph[r] = al;
+                sm.lrow[r] = sm.lrow[r] * al + ps;
+                sm.mrow[r] = mnew;
+                sm.alph[r] = al;
             }
         }
         __syncthreads();
@@ -187,16 +228,17 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
             const int d = tid;
 #pragma unroll
             for (int r = 0; r < RMAX; ++r)
-                if (r < R) o_acc[r] *= alph[r];
+                if (r < R) o_acc[r] *= sm.alph[r];
             const int nj = min(TILE, hi - j0);
             for (int jj = 0; jj < nj; ++jj) {
-                const float vv = bf2f(vbase[(size_t)(j0 + jj) * D + d]);
+                const float vv = bf2f(sm.vt[buf][jj][d]);
 #pragma unroll
                 for (int r = 0; r < RMAX; ++r)
-                    if (r < R) o_acc[r] = fmaf(sc[r * TILE + jj], vv, o_acc[r]);
+                    if (r < R) o_acc[r] = fmaf(sm.sc[r][jj], vv, o_acc[r]);
             }
         }
         __syncthreads();
+        if (it + 2 < ntiles) load_tile(buf, lo + (it + 2) * TILE);
     }
 
     // partial -> global
@@ -205,31 +247,31 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
     for (int r = 0; r < RMAX; ++r)
         if (r < R) a.part[(pbase + r) * (D + 2) + tid] = o_acc[r];
     if (tid < R) {
-        a.part[(pbase + tid) * (D + 2) + D] = mrow[tid];
-        a.part[(pbase + tid) * (D + 2) + D + 1] = lrow[tid];
+        a.part[(pbase + tid) * (D + 2) + D] = sm.mrow[tid];
+        a.part[(pbase + tid) * (D + 2) + D + 1] = sm.lrow[tid];
     }
     __threadfence();
     __syncthreads();
-    if (tid == 0) s_last = (atomicAdd(&a.counters[kvh], 1u) == (unsigned)(nsplit - 1));
+    if (tid == 0) sm.last = (atomicAdd(&a.counters[kvh], 1u) == (unsigned)(nsplit - 1));
     __syncthreads();
-    if (!s_last) return;
+    if (!sm.last) return;
     __threadfence();
     // merge the splits (fixed order) and write bf16 output
     for (int r = 0; r < R; ++r) {
         float mm = -INFINITY;
-        for (int s = 0; s < nsplit; ++s)
-            mm = fmaxf(mm, __ldcg(&a.part[(((size_t)kvh * nsplit + s) * RMAX + r) * (D + 2) + D]));
-        float L = 0.f, O = 0.f;
-        for (int s = 0; s < nsplit; ++s) {
-            const float* pp = a.part + (((size_t)kvh * nsplit + s) * RMAX + r) * (D + 2);
+        for (int s2 = 0; s2 < nsplit; ++s2)
+            mm = fmaxf(mm, __ldcg(&a.part[(((size_t)kvh * nsplit + s2) * RMAX + r) * (D + 2) + D]));
+        float Lsum = 0.f, O = 0.f;
+        for (int s2 = 0; s2 < nsplit; ++s2) {
+            const float* pp = a.part + (((size_t)kvh * nsplit + s2) * RMAX + r) * (D + 2);
             const float ms = __ldcg(pp + D);
             if (ms == -INFINITY) continue;
             const float f = expf(ms - mm);
-            L = fmaf(__ldcg(pp + D + 1), f, L);
+            Lsum = fmaf(__ldcg(pp + D + 1), f, Lsum);
             O = fmaf(__ldcg(pp + tid), f, O);
         }
         const int gi = r / S, i = r - gi * S;
-        a.out[(size_t)i * a.ldo + (kvh * G + gi) * D + tid] = f2bf(O / L);
+        a.out[(size_t)i * a.ldo + (kvh * G + gi) * D + tid] = f2bf(O / Lsum);
     }
     if (tid == 0) a.counters[kvh] = 0u;
 }
@@ -423,7 +465,7 @@ cudaError_t launch(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st
 
 template <int RMAX>
 cudaError_t launch_decode_t(const AttnArgs& a, cudaStream_t st, bool pdl) {
-    const size_t smem = (size_t)(RMAX * D + RMAX * TILE + 3 * RMAX) * sizeof(float);
+    const size_t smem = sizeof(DecSmem<RMAX>);
     static bool set = false;
     if (!set) {
         cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<RMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -15,6 +15,7 @@ enum : int {
     QW_DERR_KV_RANGE = 1,     // KV write/read position >= max_pos
     QW_DERR_TOKEN_RANGE = 2,  // token id >= vocab
     QW_DERR_SHAPE = 4,        // kernel launched with an unsupported shape
+    QW_DERR_TIMEOUT = 8,      // a bounded wait on an asynchronous copy gave up
 };
 
 QW_DEV float bf2f(bf16 v) { return __bfloat162float(v); }
@@ -104,6 +105,54 @@ QW_DEV float warp_max(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
+}
+
+// ---- shared-memory staging: bulk copies (TMA engine) + mbarriers --------
+QW_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+QW_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+QW_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+// one arrival that also raises the barrier's expected transaction bytes
+QW_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+// global -> shared bulk copy (16-byte aligned addresses, size a multiple of 16),
+// completion counted on `bar` in bytes.  Non-multicast: the source is always
+// this GPU's own memory.
+QW_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+QW_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: gives up after ~2^22 polls (each try_wait already suspends
+// for a while), so a lost transfer becomes an error flag instead of a hang.
+QW_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+    for (uint32_t i = 0; i < (1u << 22); ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+// Ampere-style 16-byte asynchronous copies (used where each thread places its
+// own chunk, e.g. swizzled tiles).  Waiting is done by the hardware.
+QW_DEV void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+QW_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+QW_DEV void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // ---- seeded generator shared with the CPU oracle ------------------------

@@ -41,11 +41,6 @@ struct Tile {
     int nrows;
 };
 
-struct Chunk {
-    uint2 w[CG][2][2];     // [group][row tile][row g / g+8] -> words (2t, 2t+1)
-    uint32_t sb[CG][2][2]; // scale bits | bias bits << 16
-};
-
 QW_DEV void gv_tiles(const QmmArgs& a, int rb, Tile (&tl)[2], int& si, int& lrb) {
     si = 0;
 #pragma unroll
@@ -59,31 +54,6 @@ QW_DEV void gv_tiles(const QmmArgs& a, int rb, Tile (&tl)[2], int& si, int& lrb)
         const QSeg& sg = a.seg[si];
         tl[0] = Tile{sg.w, sg.s, sg.b, lrb * 32, sg.n};
         tl[1] = Tile{sg.w, sg.s, sg.b, lrb * 32 + 16, sg.n};
-    }
-}
-
-QW_DEV void gv_load_chunk(Chunk& c, const Tile (&tl)[2], int KW, int KG, int gbase, int ng, int g,
-                          int t) {
-#pragma unroll
-    for (int gi = 0; gi < CG; ++gi) {
-#pragma unroll
-        for (int rt = 0; rt < 2; ++rt) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int row = tl[rt].row0 + g + 8 * h;
-                if (gi < ng && row < tl[rt].nrows) {
-                    const size_t r = (size_t)row;
-                    c.w[gi][rt][h] = __ldcs(reinterpret_cast<const uint2*>(
-                        tl[rt].w + r * KW + (size_t)(gbase + gi) * 8 + 2 * t));
-                    const uint32_t sv = __ldcs(reinterpret_cast<const unsigned short*>(tl[rt].s) + r * KG + gbase + gi);
-                    const uint32_t bv = __ldcs(reinterpret_cast<const unsigned short*>(tl[rt].b) + r * KG + gbase + gi);
-                    c.sb[gi][rt][h] = sv | (bv << 16);
-                } else {
-                    c.w[gi][rt][h] = make_uint2(0u, 0u);
-                    c.sb[gi][rt][h] = 0u;
-                }
-            }
-        }
     }
 }
 
@@ -150,37 +120,107 @@ QW_DEV void store_out(const QmmArgs& a, int si, int epi, int row, int feat, int 
 
 // ===========================================================================
 // Decode / verify GEMV: M <= 8 activation rows.
-// CTA = 32 weight rows (two 16-row mma tiles) x one K slice (gridDim.y splits K).
-// Warps of a CTA take 4-group chunks round-robin; partial sums are reduced in
-// shared memory, and across K splits by the last-arriving CTA (in split order,
-// so the result is deterministic).
+// CTA = 32 weight rows (two 16-row mma tiles) x one K slice (gridDim.y splits
+// K in units of 8 groups).  At kernel start, before waiting on the previous
+// kernel, warp 0 issues bulk copies of the CTA's whole weight slab (row r of
+// the slab by lane r, one copy per 8-group stage, one mbarrier per stage) and
+// of its scales / biases into shared memory, so every byte the CTA needs is in
+// flight at once.  Rows are padded so that a row's stride is 8 mod 32 words:
+// the mma fragment loads (lane g,t reads words 2t..2t+1 of rows g and g+8) are
+// then bank-conflict free.  Warps take groups of each stage round-robin;
+// partial sums are reduced in shared memory, and across K splits by the
+// last-arriving CTA (in split order, so the result is deterministic).
 // ===========================================================================
+struct Gv2Layout {
+    int ng, nst, rs, ngp;
+    unsigned off_w, off_sb, off_x, off_red, total;
+};
+constexpr int GV2_MAX_STAGES = 16;  // 128 groups (8192 inputs) per CTA
+
+__host__ __device__ inline Gv2Layout gv2_layout(int ng, int M) {
+    Gv2Layout L;
+    L.ng = ng;
+    L.nst = (ng + 7) / 8;
+    const int kw = ng * 8;
+    L.rs = kw + ((8 - (kw % 32)) + 32) % 32;
+    L.ngp = (ng + 7) & ~7;
+    L.off_w = 8 * GV2_MAX_STAGES;
+    L.off_sb = L.off_w + 32u * L.rs * 4u;
+    L.off_x = L.off_sb + 32u * L.ngp * 4u;
+    L.off_red = L.off_x + (unsigned)ng * M * XS_BLOCK_WORDS * 4u;
+    L.total = L.off_red + (8 + GV_WARPS * 8 * 32) * 4;
+    return L;
+}
+
+template <bool SB_BULK>
 __global__ void __launch_bounds__(GV_THREADS) qgemv_kernel(const QmmArgs a) {
-    extern __shared__ __align__(16) uint32_t smem[];
+    extern __shared__ __align__(128) unsigned char smraw[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int rb = blockIdx.x, ks = blockIdx.y, nks = gridDim.y;
     const int M = a.M, K = a.K, KW = K / 8, KG = K / 64;
-    const int kg0 = (int)((long long)KG * ks / nks), kg1 = (int)((long long)KG * (ks + 1) / nks);
-    const int ngc = kg1 - kg0;
-    const int nchunks = (ngc + CG - 1) / CG;
+    const int nunits = (KG + 7) / 8;
+    const int kg0 = min(KG, 8 * (int)((long long)nunits * ks / nks));
+    const int kg1 = min(KG, 8 * (int)((long long)nunits * (ks + 1) / nks));
+    const int ng = kg1 - kg0;
+    const Gv2Layout L = gv2_layout(ng, M);
+
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smraw);
+    uint32_t* W = reinterpret_cast<uint32_t*>(smraw + L.off_w);
+    uint16_t* Ssm = reinterpret_cast<uint16_t*>(smraw + L.off_sb);
+    uint16_t* Bsm = Ssm + 32 * L.ngp;
+    uint32_t* xs = reinterpret_cast<uint32_t*>(smraw + L.off_x);
+    float* rnorm = reinterpret_cast<float*>(smraw + L.off_red);
+    float* red = rnorm + 8;
 
     Tile tl[2];
     int si, lrb;
     gv_tiles(a, rb, tl, si, lrb);
 
-    // Weights are static: fetch this warp's first chunk before waiting on the
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < L.nst; ++s) mbar_init(&bar[s], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    // Weights are static: put the whole slab in flight before waiting on the
     // previous kernel (programmatic dependent launch).
-    Chunk cur;
-    int c = warp;
-    if (c < nchunks) gv_load_chunk(cur, tl, KW, KG, kg0 + c * CG, min(CG, ngc - c * CG), g, t);
+    if (warp == 0) {
+        const int rt = lane >> 4, rr = lane & 15;
+        const int row = tl[rt].row0 + rr;
+        const bool valid = row < tl[rt].nrows;
+        const int nvalid = __popc(__ballot_sync(0xffffffffu, valid));
+        for (int s = 0; s < L.nst; ++s) {
+            const int gs0 = 8 * s, gsn = min(8, ng - gs0);
+            uint32_t bytes = (uint32_t)nvalid * gsn * 32;
+            if (SB_BULK && s == 0) bytes += (uint32_t)nvalid * ng * 4;
+            if (lane == 0) mbar_arrive_expect_tx(&bar[s], bytes);
+            __syncwarp();
+            if (valid) {
+                bulk_g2s(W + lane * L.rs + gs0 * 8, tl[rt].w + (size_t)row * KW + (size_t)(kg0 + gs0) * 8,
+                         (uint32_t)gsn * 32, &bar[s]);
+                if (SB_BULK && s == 0) {
+                    bulk_g2s(Ssm + lane * L.ngp, tl[rt].s + (size_t)row * KG + kg0, (uint32_t)ng * 2, &bar[0]);
+                    bulk_g2s(Bsm + lane * L.ngp, tl[rt].b + (size_t)row * KG + kg0, (uint32_t)ng * 2, &bar[0]);
+                }
+            }
+        }
+    }
+    if (!SB_BULK) {
+        for (int i = threadIdx.x; i < 32 * ng; i += GV_THREADS) {
+            const int r = i / ng, gl = i - r * ng;
+            const int rt = r >> 4, row = tl[rt].row0 + (r & 15);
+            uint16_t sv = 0, bv = 0;
+            if (row < tl[rt].nrows) {
+                sv = reinterpret_cast<const uint16_t*>(tl[rt].s)[(size_t)row * KG + kg0 + gl];
+                bv = reinterpret_cast<const uint16_t*>(tl[rt].b)[(size_t)row * KG + kg0 + gl];
+            }
+            Ssm[r * L.ngp + gl] = sv;
+            Bsm[r * L.ngp + gl] = bv;
+        }
+    }
 
-    pdl_wait();
     pdl_launch_dependents();
-
-    uint32_t* xs = smem;
-    float* rnorm = reinterpret_cast<float*>(smem + (size_t)ngc * M * XS_BLOCK_WORDS);
-    float* red = rnorm + 8;
+    pdl_wait();
 
     if (a.norm_w) {
         for (int m = 0; m < M; ++m) {
@@ -206,7 +246,7 @@ __global__ void __launch_bounds__(GV_THREADS) qgemv_kernel(const QmmArgs a) {
         }
     }
     {
-        const int units = ngc * M * 4;
+        const int units = ng * M * 4;
         for (int u = threadIdx.x; u < units; u += GV_THREADS) {
             const int gl = u / (M * 4);
             const int rem = u - gl * M * 4;
@@ -224,51 +264,53 @@ __global__ void __launch_bounds__(GV_THREADS) qgemv_kernel(const QmmArgs a) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[rt][e] = bacc[rt][e] = 0.f;
 
-    for (; c < nchunks; c += GV_WARPS) {
-        Chunk nxt;
-        const int cn = c + GV_WARPS;
-        if (cn < nchunks) gv_load_chunk(nxt, tl, KW, KG, kg0 + cn * CG, min(CG, ngc - cn * CG), g, t);
-        const int gb = c * CG;
-        const int ng = min(CG, ngc - gb);
+    for (int s = 0; s < L.nst; ++s) {
+        const bool ok = mbar_wait_bounded(&bar[s], 0);
+        if (__syncthreads_or(!ok)) {
+            // a transfer never completed: flag it, give the copies another
+            // bounded chance to land in this CTA's memory, and leave
+            if (threadIdx.x == 0) atomicOr(a.err, QW_DERR_TIMEOUT);
+            for (int s2 = s; s2 < L.nst; ++s2) mbar_wait_bounded(&bar[s2], 0);
+            return;
+        }
+        const int gs0 = 8 * s, gsn = min(8, ng - gs0);
+        for (int gi = warp; gi < gsn; gi += GV_WARPS) {
+            const int gl = gs0 + gi;
+            uint32_t bq[8];
+            if (g < M) {
+                const uint4* p = reinterpret_cast<const uint4*>(xs + (size_t)(gl * M + g) * XS_BLOCK_WORDS + t * 8);
+                const uint4 v0 = p[0], v1 = p[1];
+                bq[0] = v0.x; bq[1] = v0.y; bq[2] = v0.z; bq[3] = v0.w;
+                bq[4] = v1.x; bq[5] = v1.y; bq[6] = v1.z; bq[7] = v1.w;
+            } else {
 #pragma unroll
-        for (int gi = 0; gi < CG; ++gi) {
-            if (gi < ng) {
-                uint32_t bq[8];
-                if (g < M) {
-                    const uint4* p = reinterpret_cast<const uint4*>(
-                        xs + (size_t)((gb + gi) * M + g) * XS_BLOCK_WORDS + t * 8);
-                    uint4 v0 = p[0], v1 = p[1];
-                    bq[0] = v0.x; bq[1] = v0.y; bq[2] = v0.z; bq[3] = v0.w;
-                    bq[4] = v1.x; bq[5] = v1.y; bq[6] = v1.z; bq[7] = v1.w;
-                } else {
+                for (int i = 0; i < 8; ++i) bq[i] = 0u;
+            }
+            // z = 128 * sum(x) of this group for columns 2t, 2t+1 (rows identical)
+            float z[4] = {0.f, 0.f, 0.f, 0.f};
+            mma_bf16(z, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, bq[0], bq[1], z);
+            mma_bf16(z, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, bq[2], bq[3], z);
+            mma_bf16(z, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, bq[4], bq[5], z);
+            mma_bf16(z, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, bq[6], bq[7], z);
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) bq[i] = 0u;
-                }
-                // z = 128 * sum(x) of this group for columns 2t, 2t+1 (rows identical)
-                float z[4] = {0.f, 0.f, 0.f, 0.f};
-                mma_bf16(z, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, bq[0], bq[1], z);
-                mma_bf16(z, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, bq[2], bq[3], z);
-                mma_bf16(z, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, bq[4], bq[5], z);
-                mma_bf16(z, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, bq[6], bq[7], z);
-#pragma unroll
-                for (int rt = 0; rt < 2; ++rt) {
-                    float cc[4] = {-z[0], -z[1], -z[2], -z[3]};
-                    group_mma(cc, cur.w[gi][rt][0].x, cur.w[gi][rt][0].y, cur.w[gi][rt][1].x,
-                              cur.w[gi][rt][1].y, bq);
-                    const float s0 = bits_lo_f(cur.sb[gi][rt][0]), s1 = bits_lo_f(cur.sb[gi][rt][1]);
-                    const float b0 = bits_hi_f(cur.sb[gi][rt][0]), b1 = bits_hi_f(cur.sb[gi][rt][1]);
-                    acc[rt][0] = fmaf(s0, cc[0], acc[rt][0]);
-                    acc[rt][1] = fmaf(s0, cc[1], acc[rt][1]);
-                    acc[rt][2] = fmaf(s1, cc[2], acc[rt][2]);
-                    acc[rt][3] = fmaf(s1, cc[3], acc[rt][3]);
-                    bacc[rt][0] = fmaf(b0, z[0], bacc[rt][0]);
-                    bacc[rt][1] = fmaf(b0, z[1], bacc[rt][1]);
-                    bacc[rt][2] = fmaf(b1, z[2], bacc[rt][2]);
-                    bacc[rt][3] = fmaf(b1, z[3], bacc[rt][3]);
-                }
+            for (int rt = 0; rt < 2; ++rt) {
+                const int r0 = rt * 16 + g;
+                const uint2 wa = *reinterpret_cast<const uint2*>(W + r0 * L.rs + gl * 8 + 2 * t);
+                const uint2 wb = *reinterpret_cast<const uint2*>(W + (r0 + 8) * L.rs + gl * 8 + 2 * t);
+                float cc[4] = {-z[0], -z[1], -z[2], -z[3]};
+                group_mma(cc, wa.x, wa.y, wb.x, wb.y, bq);
+                const float s0 = u16_to_f(Ssm[r0 * L.ngp + gl]), s1 = u16_to_f(Ssm[(r0 + 8) * L.ngp + gl]);
+                const float b0 = u16_to_f(Bsm[r0 * L.ngp + gl]), b1 = u16_to_f(Bsm[(r0 + 8) * L.ngp + gl]);
+                acc[rt][0] = fmaf(s0, cc[0], acc[rt][0]);
+                acc[rt][1] = fmaf(s0, cc[1], acc[rt][1]);
+                acc[rt][2] = fmaf(s1, cc[2], acc[rt][2]);
+                acc[rt][3] = fmaf(s1, cc[3], acc[rt][3]);
+                bacc[rt][0] = fmaf(b0, z[0], bacc[rt][0]);
+                bacc[rt][1] = fmaf(b0, z[1], bacc[rt][1]);
+                bacc[rt][2] = fmaf(b1, z[2], bacc[rt][2]);
+                bacc[rt][3] = fmaf(b1, z[3], bacc[rt][3]);
             }
         }
-        if (cn < nchunks) cur = nxt;
     }
 
     // cross-warp reduction (fixed order)
@@ -518,10 +560,6 @@ __global__ void __launch_bounds__(128) qgemm_kernel(const QmmArgs a) {
         }
 }
 
-size_t gv_smem_bytes(int ngc, int M) {
-    return (size_t)ngc * M * XS_BLOCK_WORDS * 4 + 8 * 4 + (size_t)GV_WARPS * 8 * 32 * 4;
-}
-
 template <typename Kern>
 cudaError_t launch_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
                       const QmmArgs& a) {
@@ -541,11 +579,14 @@ cudaError_t launch_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStrea
 }  // namespace
 
 cudaError_t launch_qgemv(QmmArgs a, cudaStream_t st, bool pdl, int num_sms) {
+    (void)num_sms;
     if (a.M < 1 || a.M > 8 || a.K <= 0 || a.K % 64 != 0 || a.nseg < 1 || a.nseg > 3)
         return cudaErrorInvalidValue;
     static bool attr_set = false;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(qgemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaError_t e = cudaFuncSetAttribute(qgemv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(qgemv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
@@ -564,25 +605,21 @@ cudaError_t launch_qgemv(QmmArgs a, cudaStream_t st, bool pdl, int num_sms) {
     }
     a.nrb = nrb;
     const int KG = a.K / 64;
-    int best_ks = 1;
-    double best = 1e300;
-    for (int ks = 1; ks <= 8; ++ks) {
-        const int ngc = (KG + ks - 1) / ks;
-        if (ks > 1 && (ngc < CG || a.partial == nullptr || a.counters == nullptr)) break;
-        if (ks > 1 && (size_t)ks * a.M * nrb * 32 > a.partial_cap) break;
-        if (gv_smem_bytes(ngc, a.M) > 200 * 1024) continue;
-        const long long ctas = (long long)nrb * ks;
-        const int rounds = ((ngc + CG - 1) / CG + GV_WARPS - 1) / GV_WARPS;
-        const double cost = (double)((ctas + num_sms - 1) / num_sms) * (rounds + 0.75);
-        if (cost < best * 0.97) {
-            best = cost;
-            best_ks = ks;
-        }
+    const int nunits = (KG + 7) / 8;
+    // Smallest K split whose weight slab (32 rows x ng groups x 36 B with
+    // scales/biases) stays near 28 KB, so several CTAs fit per SM and the
+    // kernel's whole weight stream can be in flight at once.
+    auto max_ng = [&](int ks) { return std::min(KG, 8 * ((nunits + ks - 1) / ks)); };
+    int ks = 1;
+    while (ks < nunits && ks < 16 && (32 * max_ng(ks) * 36 > 28 * 1024 || max_ng(ks) > 8 * GV2_MAX_STAGES)) ++ks;
+    if (ks > 1 && (a.partial == nullptr || a.counters == nullptr || (size_t)ks * a.M * nrb * 32 > a.partial_cap)) {
+        ks = 1;
+        if (max_ng(1) > 8 * GV2_MAX_STAGES) return cudaErrorInvalidValue;
     }
-    const int ngc_max = (KG + best_ks - 1) / best_ks;
-    const size_t smem = gv_smem_bytes(ngc_max, a.M);
-    if (smem > 200 * 1024) return cudaErrorInvalidValue;
-    return launch_ex(qgemv_kernel, dim3(nrb, best_ks), dim3(GV_THREADS), smem, st, pdl, a);
+    const Gv2Layout L = gv2_layout(max_ng(ks), a.M);
+    if (L.total > 200 * 1024) return cudaErrorInvalidValue;
+    if (KG % 8 == 0) return launch_ex(qgemv_kernel<true>, dim3(nrb, ks), dim3(GV_THREADS), L.total, st, pdl, a);
+    return launch_ex(qgemv_kernel<false>, dim3(nrb, ks), dim3(GV_THREADS), L.total, st, pdl, a);
 }
 
 cudaError_t launch_qgemm(QmmArgs a, cudaStream_t st, int num_sms) {
