@@ -256,22 +256,47 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
     __syncthreads();
     if (!sm.last) return;
     __threadfence();
-    // merge the splits (fixed order) and write bf16 output
-    for (int r = 0; r < R; ++r) {
+    // merge the splits (fixed order) and write bf16 output.  All split maxima
+    // and sums are gathered in one parallel pass; the tile buffers (no longer
+    // needed) hold them: nsplit * R <= 148 * 64 floats.
+    float* mb = reinterpret_cast<float*>(&sm.kt[0][0][0]);
+    float* lb = mb + nsplit * R;
+    for (int idx = tid; idx < nsplit * R; idx += 128) {
+        const int s2 = idx / R, r = idx - s2 * R;
+        const float* pp = a.part + (((size_t)kvh * nsplit + s2) * RMAX + r) * (D + 2);
+        mb[idx] = __ldcg(pp + D);
+        lb[idx] = __ldcg(pp + D + 1);
+    }
+    __syncthreads();
+    if (tid < R) {
+        // row tid: global max, then split weights e^(m_s - max) (in place of m_s)
         float mm = -INFINITY;
-        for (int s2 = 0; s2 < nsplit; ++s2)
-            mm = fmaxf(mm, __ldcg(&a.part[(((size_t)kvh * nsplit + s2) * RMAX + r) * (D + 2) + D]));
-        float Lsum = 0.f, O = 0.f;
+        for (int s2 = 0; s2 < nsplit; ++s2) mm = fmaxf(mm, mb[s2 * R + tid]);
+        float Lsum = 0.f;
         for (int s2 = 0; s2 < nsplit; ++s2) {
-            const float* pp = a.part + (((size_t)kvh * nsplit + s2) * RMAX + r) * (D + 2);
-            const float ms = __ldcg(pp + D);
-            if (ms == -INFINITY) continue;
-            const float f = expf(ms - mm);
-            Lsum = fmaf(__ldcg(pp + D + 1), f, Lsum);
-            O = fmaf(__ldcg(pp + tid), f, O);
+            const float ms = mb[s2 * R + tid];
+            const float f = ms == -INFINITY ? 0.f : expf(ms - mm);
+            mb[s2 * R + tid] = f;
+            Lsum = fmaf(lb[s2 * R + tid], f, Lsum);
+        }
+        sm.lrow[tid] = Lsum;
+    }
+    __syncthreads();
+    for (int r = 0; r < R; ++r) {
+        float O = 0.f;
+        for (int s0 = 0; s0 < nsplit; s0 += 8) {
+            float pv[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                pv[j] = (s0 + j < nsplit && mb[(s0 + j) * R + r] != 0.f)
+                            ? __ldcg(&a.part[(((size_t)kvh * nsplit + s0 + j) * RMAX + r) * (D + 2) + tid])
+                            : 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (s0 + j < nsplit) O = fmaf(pv[j], mb[(s0 + j) * R + r], O);
         }
         const int gi = r / S, i = r - gi * S;
-        a.out[(size_t)i * a.ldo + (kvh * G + gi) * D + tid] = f2bf(O / Lsum);
+        a.out[(size_t)i * a.ldo + (kvh * G + gi) * D + tid] = f2bf(O / sm.lrow[r]);
     }
     if (tid == 0) a.counters[kvh] = 0u;
 }

@@ -50,28 +50,6 @@ std::vector<int> eos_list(const qw_model* m, const uint32_t* eos, int n_eos) {
     return v;
 }
 
-// Split-K scratch of the standalone quantized_matmul: one buffer of partial
-// sums and one set of (self-resetting) counters per device, allocated on the
-// first call.  Calls on the same device that overlap on the GPU must not share it.
-struct QmmScratch {
-    float* partial = nullptr;
-    size_t cap = 0;
-    unsigned* counters = nullptr;
-};
-QmmScratch& qmm_scratch(int dev) {
-    static std::mutex mu;
-    static std::map<int, QmmScratch> per_dev;
-    std::lock_guard<std::mutex> lk(mu);
-    QmmScratch& s = per_dev[dev];
-    if (!s.partial) {
-        s.cap = (size_t)16 * 8 * 160000;
-        QW_CUDA(cudaMalloc(&s.partial, s.cap * sizeof(float)));
-        QW_CUDA(cudaMalloc(&s.counters, 16384 * sizeof(unsigned)));
-        QW_CUDA(cudaMemset(s.counters, 0, 16384 * sizeof(unsigned)));
-    }
-    return s;
-}
-
 void check_ids(const qw_model* m, const uint32_t* ids, int n) {
     for (int i = 0; i < n; ++i)
         if (ids[i] >= (uint32_t)m->cfg.vocab)
@@ -397,13 +375,6 @@ int qw_quantized_matmul(const void* x, const void* w, const void* scales, const 
         a.nseg = 1;
         a.epi = qw::EPI_STORE;
         cudaStream_t st = (cudaStream_t)stream;
-        if (M <= 8) {
-            QmmScratch& sc = qmm_scratch(dev);
-            if ((N + 31) / 32 > 16384) throw qw::Error(QW_ERR_UNSUPPORTED, "N too large for the M<=8 path");
-            a.partial = sc.partial;
-            a.partial_cap = sc.cap;
-            a.counters = sc.counters;
-        }
         if (M <= 8)
             QW_CUDA(qw::launch_qgemv(a, st, false, sms));
         else

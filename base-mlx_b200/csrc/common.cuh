@@ -64,6 +64,25 @@ QW_DEV uint32_t nib_pair(uint32_t w, int j) {
 // bf16x2 (128.0, 128.0): the A operand whose product with B yields 128 * sum(x).
 #define QW_BF16X2_128 0x43004300u
 
+// fp16 variant used by the decode GEMV: 0x6400 is fp16 1024.0 and its ten
+// mantissa bits take a nibble at bits 0-3 (1024 + q) or at bits 4-7
+// (1024 + 16q) without shifting, so the eight nibbles of a word become four
+// fp16 pairs with one shift and four LOP3s:
+//   nib_even(w, 0) = (e0, e4), nib_even(w, 8) = (e2, e6)      [1024 + q]
+//   nib_odd (w, 0) = (e1, e5), nib_odd (w, 8) = (e3, e7)      [1024 + 16q]
+QW_DEV uint32_t nib_even(uint32_t w) { return (w & 0x000F000Fu) | 0x64006400u; }
+QW_DEV uint32_t nib_odd(uint32_t w) { return (w & 0x00F000F0u) | 0x64006400u; }
+
+// D[16x8] (fp32) = A[16x16] (fp16, row) * B[16x8] (fp16, col) + C (same fragment layout as mma_bf16).
+QW_DEV void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1,
+                    const float (&c)[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};\n"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]), "f"(c[3]));
+}
+
 // byte permute (PRMT)
 QW_DEV uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     uint32_t r;

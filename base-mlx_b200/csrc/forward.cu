@@ -45,11 +45,7 @@ QmmArgs qmm_base(qw_model* m, const bf16* x, int ldx, int M, int K) {
     a.M = M;
     a.K = K;
     a.eps = m->cfg.eps;
-    a.partial = w.partial;
-    a.partial_cap = w.partial_cap;
-    a.counters = w.counters;
     a.amax_partial = w.amax_partial;
-    a.amax_counter = w.amax_counter;
     a.err = m->d_err;
     return a;
 }
@@ -175,10 +171,10 @@ void forward_dev(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_m
             a.nseg = 1;
             a.epi = EPI_LOGITS;
             a.store_logits = store_logits ? 1 : 0;
-            a.amax_out = d_argmax;
             a.amax_row_offset = vocab_split ? m->tp_rank * m->vocab_l : 0;
-            a.amax_key_out = vocab_split ? w.amax_keys : nullptr;
             qmm(m, a, st);
+            QW_CUDA(launch_amax_finalize(w.amax_partial, qgemv_row_blocks(a), rows, d_argmax,
+                                         vocab_split ? w.amax_keys : nullptr, st));
         } else {
             QW_CUDA(launch_rmsnorm(xin, m->final_norm, w.h, rows, H, cf.eps, st));
             QmmArgs a = qmm_base(m, w.h, H, rows, H);

@@ -37,22 +37,21 @@ struct QmmArgs {
     int nseg;
     int epi;
     int nrb;             // row blocks in the grid (gridDim.x)
-    // split-K scratch (decode path)
-    float* partial;
-    size_t partial_cap;  // floats available at `partial`
-    unsigned* counters;  // >= nrb entries, zero between launches
-    // fused argmax (EPI_LOGITS)
+    // fused argmax (EPI_LOGITS): per-CTA (logit, index) maxima, reduced by
+    // launch_amax_finalize
     unsigned long long* amax_partial;  // [nrb, M]
-    unsigned* amax_counter;            // one counter, zero between launches
-    int* amax_out;                     // [M]
-    unsigned long long* amax_key_out;  // optional [M]: packed (logit, index) keys
     int store_logits;
     int amax_row_offset;               // global index of row 0 (vocab-parallel shards)
     int* err;
 };
 
-// Decode / verify path: M <= 8.  Picks split-K and launches qgemv.
+// Decode / verify path: M <= 8.
 cudaError_t launch_qgemv(QmmArgs a, cudaStream_t st, bool pdl, int num_sms);
+// Row blocks of the qgemv grid for these segments (size of amax_partial / M).
+int qgemv_row_blocks(const QmmArgs& a);
+// argmax[m] (and optionally packed keys) from the EPI_LOGITS per-CTA maxima.
+cudaError_t launch_amax_finalize(const unsigned long long* partial, int nrb, int M, int* out,
+                                 unsigned long long* keys_out, cudaStream_t st);
 // Prefill path: M > 8 (no norm prologue, no argmax; EPI_STORE/RESID/SWIGLU/F32).
 cudaError_t launch_qgemm(QmmArgs a, cudaStream_t st, int num_sms);
 

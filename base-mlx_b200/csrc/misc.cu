@@ -97,6 +97,38 @@ __global__ void argmax_rows_kernel(const bf16* logits, int V, int* out, unsigned
     }
 }
 
+// Final argmax over the per-CTA maxima of the lm_head GEMV (one CTA).
+__global__ void amax_finalize_kernel(const unsigned long long* partial, int nrb, int M, int* out,
+                                     unsigned long long* keys) {
+    pdl_wait();
+    pdl_launch_dependents();
+    __shared__ unsigned long long red[32];
+    for (int m = 0; m < M; ++m) {
+        unsigned long long b = 0ull;
+        for (int r0 = threadIdx.x; r0 < nrb; r0 += blockDim.x * 4) {
+            unsigned long long kv[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int r = r0 + j * blockDim.x;
+                kv[j] = r < nrb ? partial[(size_t)r * M + m] : 0ull;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) b = umax64(b, kv[j]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) b = umax64(b, __shfl_xor_sync(0xffffffffu, b, o));
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = b;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            unsigned long long bb = 0ull;
+            for (int i = 0; i < (int)(blockDim.x >> 5); ++i) bb = umax64(bb, red[i]);
+            out[m] = (int)amax_key_index(bb);
+            if (keys) keys[m] = bb;
+        }
+        __syncthreads();
+    }
+}
+
 __global__ void keys_to_index_kernel(const unsigned long long* keys, int n, int* out) {
     pdl_wait();
     pdl_launch_dependents();
@@ -206,6 +238,11 @@ cudaError_t launch_rmsnorm(const bf16* x, const bf16* w, bf16* y, int S, int H, 
 cudaError_t launch_argmax_rows(const bf16* logits, int rows, int V, int* out, unsigned long long* keys_out,
                                int index_offset, cudaStream_t st) {
     return launch(argmax_rows_kernel, dim3(rows), dim3(1024), 0, st, true, logits, V, out, keys_out, index_offset);
+}
+
+cudaError_t launch_amax_finalize(const unsigned long long* partial, int nrb, int M, int* out,
+                                 unsigned long long* keys_out, cudaStream_t st) {
+    return launch(amax_finalize_kernel, dim3(1), dim3(1024), 0, st, true, partial, nrb, M, out, keys_out);
 }
 
 cudaError_t launch_keys_to_index(const unsigned long long* keys, int n, int* out, cudaStream_t st) {

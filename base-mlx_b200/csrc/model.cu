@@ -359,7 +359,7 @@ void ensure_workspace(qw_model* m, int rows, int logits_rows) {
     Workspace& w = m->ws;
     rows = std::max(rows, 8);
     logits_rows = std::max(logits_rows, 8);
-    if (rows <= w.cap_rows && logits_rows <= w.cap_logits && w.partial) return;
+    if (rows <= w.cap_rows && logits_rows <= w.cap_logits && w.amax_partial) return;
     QW_CUDA(cudaStreamSynchronize(m->stream));
     for (void* p : w.allocs) cudaFree(p);
     w.allocs.clear();
@@ -385,12 +385,8 @@ void ensure_workspace(qw_model* m, int rows, int logits_rows) {
     w.f32 = (float*)alloc(rows * H * 4);
     w.ids = (int*)alloc(rows * 4);
     w.argmax = (int*)alloc(rows * 4);
-    w.partial_cap = (size_t)8 * 8 * 40960;  // ksplit x M x rows
-    w.partial = (float*)alloc(w.partial_cap * 4);
-    const size_t nrb_max = (size_t)std::max<int64_t>(m->vocab_l / 16 + 64, 8192);
-    w.counters = (unsigned*)alloc(nrb_max * 4);
+    const size_t nrb_max = (size_t)m->vocab_l / 16 + 64;
     w.amax_partial = (unsigned long long*)alloc(nrb_max * 8 * 8);
-    w.amax_counter = (unsigned*)alloc(64);
     w.amax_keys = (unsigned long long*)alloc((size_t)logits_rows * 8);
     const int nsplit_max = std::max(1, 2 * m->num_sms);
     w.attn_part = (float*)alloc((size_t)m->hkv_l * nsplit_max * 64 * 130 * 4);
@@ -399,8 +395,6 @@ void ensure_workspace(qw_model* m, int rows, int logits_rows) {
     w.out_cap = std::max(w.out_cap, 65536);
     w.out = (int*)alloc((size_t)w.out_cap * 4);
     w.ctl = (StepCtl*)alloc(sizeof(StepCtl));
-    QW_CUDA(cudaMemset(w.counters, 0, nrb_max * 4));
-    QW_CUDA(cudaMemset(w.amax_counter, 0, 64));
     QW_CUDA(cudaMemset(w.attn_counters, 0, (size_t)std::max(m->hkv_l, 8) * 4));
     QW_CUDA(cudaMemset(w.next_tok, 0, 64));
     w.cap_rows = rows;

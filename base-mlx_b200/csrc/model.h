@@ -65,11 +65,7 @@ struct Workspace {
     float* f32 = nullptr;        // tensor-parallel partial sums [rows, hidden]
     int* ids = nullptr;          // input token ids [rows]
     int* argmax = nullptr;       // [rows]
-    float* partial = nullptr;    // split-K scratch
-    size_t partial_cap = 0;
-    unsigned* counters = nullptr;  // split-K counters
-    unsigned long long* amax_partial = nullptr;
-    unsigned* amax_counter = nullptr;
+    unsigned long long* amax_partial = nullptr;  // lm_head per-CTA maxima [row blocks, rows]
     unsigned long long* amax_keys = nullptr;  // [logits rows] (tensor-parallel argmax)
     float* attn_part = nullptr;
     unsigned* attn_counters = nullptr;

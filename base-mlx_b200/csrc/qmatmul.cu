@@ -23,13 +23,15 @@
 // staged into shared memory.
 #include <algorithm>
 
+#include <cuda_fp16.h>
+
 #include "kernels.h"
 
 namespace qw {
 namespace {
 
-constexpr int GV_WARPS = 4;
-constexpr int GV_THREADS = GV_WARPS * 32;
+
+
 constexpr int CG = 4;               // groups per chunk (256 inputs)
 constexpr int XS_BLOCK_WORDS = 36;  // one (group, column) block: 4 quads x 8 words + 4 pad words
 
@@ -40,22 +42,6 @@ struct Tile {
     int row0;
     int nrows;
 };
-
-QW_DEV void gv_tiles(const QmmArgs& a, int rb, Tile (&tl)[2], int& si, int& lrb) {
-    si = 0;
-#pragma unroll
-    for (int i = 1; i < 3; ++i)
-        if (i < a.nseg && rb >= a.seg[i].rb0) si = i;
-    lrb = rb - a.seg[si].rb0;
-    if (a.epi == EPI_SWIGLU) {
-        tl[0] = Tile{a.seg[0].w, a.seg[0].s, a.seg[0].b, lrb * 16, a.seg[0].n};
-        tl[1] = Tile{a.seg[1].w, a.seg[1].s, a.seg[1].b, lrb * 16, a.seg[1].n};
-    } else {
-        const QSeg& sg = a.seg[si];
-        tl[0] = Tile{sg.w, sg.s, sg.b, lrb * 32, sg.n};
-        tl[1] = Tile{sg.w, sg.s, sg.b, lrb * 32 + 16, sg.n};
-    }
-}
 
 // Four chained mma over one group for one 16-row tile.  w0/w1: words 2t/2t+1 of
 // row g, w2/w3: of row g+8; bq: permuted activations; c seeded with -128*sum(x).
@@ -96,6 +82,46 @@ QW_DEV void stage16(const bf16* src, const bf16* normw, float r, uint32_t* dst, 
     d4[1] = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
+// Stage 16 activations (optionally RMS-normalised, rounded to bf16 like the
+// reference's rms_norm output) as fp16 in the decode GEMV's fragment order:
+// dst[0..3] = even-chain pairs (x0,x4),(x2,x6),(x8,x12),(x10,x14),
+// dst[4..7] = odd-chain pairs  (x1,x5),(x3,x7),(x9,x13),(x11,x15).
+// bf16 -> fp16 is exact for |x| >= 2^-14; the even / odd sums are taken over
+// the converted values so they match what the tensor cores multiply.
+QW_DEV void stage16_f16(const bf16* src, const bf16* normw, float r, uint32_t* dst, float& se, float& so) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+    const uint4 u0 = s4[0], u1 = s4[1];
+    const uint32_t X[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+    uint32_t W8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (normw) {
+        const uint4* w4 = reinterpret_cast<const uint4*>(normw);
+        const uint4 v0 = w4[0], v1 = w4[1];
+        W8[0] = v0.x; W8[1] = v0.y; W8[2] = v0.z; W8[3] = v0.w;
+        W8[4] = v1.x; W8[5] = v1.y; W8[6] = v1.z; W8[7] = v1.w;
+    }
+    uint32_t F[8];
+    se = 0.f;
+    so = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        float lo = bits_lo_f(X[i]), hi = bits_hi_f(X[i]);
+        if (normw) {
+            lo = bfr(__fmul_rn(__fmul_rn(lo, r), bits_lo_f(W8[i])));
+            hi = bfr(__fmul_rn(__fmul_rn(hi, r), bits_hi_f(W8[i])));
+        }
+        const __half2 h = __floats2half2_rn(lo, hi);
+        const float2 back = __half22float2(h);
+        se += back.x;
+        so += back.y;
+        F[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+    d4[0] = make_uint4(prmt(F[0], F[2], 0x5410), prmt(F[1], F[3], 0x5410), prmt(F[4], F[6], 0x5410),
+                       prmt(F[5], F[7], 0x5410));
+    d4[1] = make_uint4(prmt(F[0], F[2], 0x7632), prmt(F[1], F[3], 0x7632), prmt(F[4], F[6], 0x7632),
+                       prmt(F[5], F[7], 0x7632));
+}
+
 // Final per-element epilogue shared by both kernels (not EPI_LOGITS).
 QW_DEV void store_out(const QmmArgs& a, int si, int epi, int row, int feat, int col, float v0, float v1) {
     if (epi == EPI_SWIGLU) {
@@ -120,99 +146,156 @@ QW_DEV void store_out(const QmmArgs& a, int si, int epi, int row, int feat, int 
 
 // ===========================================================================
 // Decode / verify GEMV: M <= 8 activation rows.
-// CTA = 32 weight rows (two 16-row mma tiles) x one K slice (gridDim.y splits
-// K in units of 8 groups).  At kernel start, before waiting on the previous
-// kernel, warp 0 issues bulk copies of the CTA's whole weight slab (row r of
-// the slab by lane r, one copy per 8-group stage, one mbarrier per stage) and
-// of its scales / biases into shared memory, so every byte the CTA needs is in
-// flight at once.  Rows are padded so that a row's stride is 8 mod 32 words:
-// the mma fragment loads (lane g,t reads words 2t..2t+1 of rows g and g+8) are
-// then bank-conflict free.  Warps take groups of each stage round-robin;
-// partial sums are reduced in shared memory, and across K splits by the
-// last-arriving CTA (in split order, so the result is deterministic).
+// CTA = RT 16-row mma tiles (RT = 2 pairs gate and up rows for the SwiGLU
+// epilogue) over the full K.  At kernel start, before waiting on the previous
+// kernel, every thread issues 16-byte asynchronous copies of the CTA's weight
+// slab, scales and biases into shared memory (consecutive threads copy
+// consecutive chunks of a row), one commit group per 8-group stage, so all of
+// the CTA's bytes are in flight at once.  Rows are padded to a stride of 8 mod
+// 32 words, which makes the fragment loads (lane g,t reads words 2t..2t+1 of
+// rows g and g+8) bank-conflict free.  While the weights land, the CTA stages
+// its (RMS-normalised) activations in permuted fragment order together with
+// per-group sums.  Warps take two groups at a time (independent mma chains);
+// their partial sums are reduced in shared memory in a fixed order.
 // ===========================================================================
-struct Gv2Layout {
-    int ng, nst, rs, ngp;
-    unsigned off_w, off_sb, off_x, off_red, total;
+struct GvLayout {
+    int nst, rs, ngp;
+    unsigned off_sb, off_x, off_xsum, off_red, total;
 };
-constexpr int GV2_MAX_STAGES = 16;  // 128 groups (8192 inputs) per CTA
 
-__host__ __device__ inline Gv2Layout gv2_layout(int ng, int M) {
-    Gv2Layout L;
-    L.ng = ng;
-    L.nst = (ng + 7) / 8;
-    const int kw = ng * 8;
+__host__ __device__ inline GvLayout gv_layout(int KG, int M, int RT, int NW) {
+    GvLayout L;
+    L.nst = (KG + 7) / 8;
+    const int kw = KG * 8;
     L.rs = kw + ((8 - (kw % 32)) + 32) % 32;
-    L.ngp = (ng + 7) & ~7;
-    L.off_w = 8 * GV2_MAX_STAGES;
-    L.off_sb = L.off_w + 32u * L.rs * 4u;
-    L.off_x = L.off_sb + 32u * L.ngp * 4u;
-    L.off_red = L.off_x + (unsigned)ng * M * XS_BLOCK_WORDS * 4u;
-    L.total = L.off_red + (8 + GV_WARPS * 8 * 32) * 4;
+    L.ngp = (KG + 7) & ~7;
+    const int rows = 16 * RT;
+    L.off_sb = (unsigned)rows * L.rs * 4u;
+    L.off_x = L.off_sb + (unsigned)rows * L.ngp * 4u;
+    L.off_xsum = L.off_x + (unsigned)KG * M * XS_BLOCK_WORDS * 4u;
+    L.off_red = L.off_xsum + (unsigned)KG * 16 * 4u;
+    // rnorm[8] + pad[32], per-warp partials [NW][RT*4*32]
+    L.total = L.off_red + (8 + 32 + NW * RT * 128) * 4;
     return L;
 }
 
-template <bool SB_BULK>
-__global__ void __launch_bounds__(GV_THREADS) qgemv_kernel(const QmmArgs a) {
+// cp.async.wait_group needs an immediate operand
+QW_DEV void cp_async_wait_dyn(int n) {
+    switch (n) {
+        case 0: cp_async_wait<0>(); break;
+        case 1: cp_async_wait<1>(); break;
+        case 2: cp_async_wait<2>(); break;
+        case 3: cp_async_wait<3>(); break;
+        case 4: cp_async_wait<4>(); break;
+        case 5: cp_async_wait<5>(); break;
+        case 6: cp_async_wait<6>(); break;
+        default: cp_async_wait<7>(); break;
+    }
+}
+
+// 16 x 64 tile of one group: two independent half-chains (k-steps 0-1, 2-3).
+QW_DEV void group_mma_split(float (&c)[4], uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3,
+                            const uint32_t (&bq)[8], const float (&init)[4]) {
+    float c1[4] = {0.f, 0.f, 0.f, 0.f};
+    float c0[4] = {init[0], init[1], init[2], init[3]};
+    mma_bf16(c0, nib_pair(w0, 0), nib_pair(w2, 0), nib_pair(w0, 1), nib_pair(w2, 1), bq[0], bq[1], c0);
+    mma_bf16(c1, nib_pair(w1, 0), nib_pair(w3, 0), nib_pair(w1, 1), nib_pair(w3, 1), bq[4], bq[5], c1);
+    mma_bf16(c0, nib_pair(w0, 2), nib_pair(w2, 2), nib_pair(w0, 3), nib_pair(w2, 3), bq[2], bq[3], c0);
+    mma_bf16(c1, nib_pair(w1, 2), nib_pair(w3, 2), nib_pair(w1, 3), nib_pair(w3, 3), bq[6], bq[7], c1);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) c[e] = c0[e] + c1[e];
+}
+
+template <int RT, int NW, bool SB_VEC>
+__global__ void __launch_bounds__(NW * 32) qgemv_kernel(const QmmArgs a) {
+    constexpr int NT = NW * 32;
     extern __shared__ __align__(128) unsigned char smraw[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const int rb = blockIdx.x, ks = blockIdx.y, nks = gridDim.y;
+    const int rb = blockIdx.x;
     const int M = a.M, K = a.K, KW = K / 8, KG = K / 64;
-    const int nunits = (KG + 7) / 8;
-    const int kg0 = min(KG, 8 * (int)((long long)nunits * ks / nks));
-    const int kg1 = min(KG, 8 * (int)((long long)nunits * (ks + 1) / nks));
-    const int ng = kg1 - kg0;
-    const Gv2Layout L = gv2_layout(ng, M);
+    const GvLayout L = gv_layout(KG, M, RT, NW);
 
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smraw);
-    uint32_t* W = reinterpret_cast<uint32_t*>(smraw + L.off_w);
+    uint32_t* W = reinterpret_cast<uint32_t*>(smraw);
     uint16_t* Ssm = reinterpret_cast<uint16_t*>(smraw + L.off_sb);
-    uint16_t* Bsm = Ssm + 32 * L.ngp;
+    uint16_t* Bsm = Ssm + 16 * RT * L.ngp;
     uint32_t* xs = reinterpret_cast<uint32_t*>(smraw + L.off_x);
+    float* xsum = reinterpret_cast<float*>(smraw + L.off_xsum);  // [KG][even, odd][8 columns]
     float* rnorm = reinterpret_cast<float*>(smraw + L.off_red);
-    float* red = rnorm + 8;
+    float* wred = rnorm + 8 + 32;  // [NW][RT*128]
 
-    Tile tl[2];
-    int si, lrb;
-    gv_tiles(a, rb, tl, si, lrb);
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < L.nst; ++s) mbar_init(&bar[s], 1);
-        fence_mbar_init();
+    // tiles of this CTA
+    int si = 0;
+#pragma unroll
+    for (int i = 1; i < 3; ++i)
+        if (i < a.nseg && rb >= a.seg[i].rb0) si = i;
+    const int lrb = rb - a.seg[si].rb0;
+    Tile tl[RT];
+    if (RT == 2) {
+        tl[0] = Tile{a.seg[0].w, a.seg[0].s, a.seg[0].b, lrb * 16, a.seg[0].n};
+        tl[RT - 1] = Tile{a.seg[1].w, a.seg[1].s, a.seg[1].b, lrb * 16, a.seg[1].n};
+    } else {
+        const QSeg& sg = a.seg[si];
+        tl[0] = Tile{sg.w, sg.s, sg.b, lrb * 16, sg.n};
     }
-    __syncthreads();
+
     // Weights are static: put the whole slab in flight before waiting on the
-    // previous kernel (programmatic dependent launch).
-    if (warp == 0) {
-        const int rt = lane >> 4, rr = lane & 15;
-        const int row = tl[rt].row0 + rr;
-        const bool valid = row < tl[rt].nrows;
-        const int nvalid = __popc(__ballot_sync(0xffffffffu, valid));
+    // previous kernel (programmatic dependent launch).  Rows past n are left
+    // unloaded; their results are never stored.
+    if (KG % 8 == 0) {
+        // every stage has 8 groups = 16 chunks of 16 bytes per row: fixed
+        // per-thread (row, chunk) slots, advanced by 64 words per stage
+        constexpr int CPT = (16 * RT * 16) / NT;
+        const uint32_t* src[CPT];
+        uint32_t* dst[CPT];
+        bool ok[CPT];
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) {
+            const int u = threadIdx.x + i * NT;
+            const int r = u >> 4, c = u & 15;
+            const int rt = r >> 4, row = tl[rt].row0 + (r & 15);
+            ok[i] = row < tl[rt].nrows;
+            src[i] = tl[rt].w + (size_t)(ok[i] ? row : 0) * KW + c * 4;
+            dst[i] = W + r * L.rs + c * 4;
+        }
         for (int s = 0; s < L.nst; ++s) {
-            const int gs0 = 8 * s, gsn = min(8, ng - gs0);
-            uint32_t bytes = (uint32_t)nvalid * gsn * 32;
-            if (SB_BULK && s == 0) bytes += (uint32_t)nvalid * ng * 4;
-            if (lane == 0) mbar_arrive_expect_tx(&bar[s], bytes);
-            __syncwarp();
-            if (valid) {
-                bulk_g2s(W + lane * L.rs + gs0 * 8, tl[rt].w + (size_t)row * KW + (size_t)(kg0 + gs0) * 8,
-                         (uint32_t)gsn * 32, &bar[s]);
-                if (SB_BULK && s == 0) {
-                    bulk_g2s(Ssm + lane * L.ngp, tl[rt].s + (size_t)row * KG + kg0, (uint32_t)ng * 2, &bar[0]);
-                    bulk_g2s(Bsm + lane * L.ngp, tl[rt].b + (size_t)row * KG + kg0, (uint32_t)ng * 2, &bar[0]);
+#pragma unroll
+            for (int i = 0; i < CPT; ++i)
+                if (ok[i]) cp_async16(dst[i] + s * 64, src[i] + (size_t)s * 64);
+            if (SB_VEC && s == 0) {
+                const int nch2 = KG / 8;  // 16-byte chunks of a scale row
+                for (int u = threadIdx.x; u < 2 * 16 * RT * nch2; u += NT) {
+                    const int which = u / (16 * RT * nch2), rem = u - which * 16 * RT * nch2;
+                    const int r = rem / nch2, c = rem - r * nch2;
+                    const int rt = r >> 4, row = tl[rt].row0 + (r & 15);
+                    if (row < tl[rt].nrows)
+                        cp_async16((which ? Bsm : Ssm) + r * L.ngp + c * 8,
+                                   (which ? tl[rt].b : tl[rt].s) + (size_t)row * KG + c * 8);
                 }
             }
+            cp_async_commit();
+        }
+    } else {
+        for (int s = 0; s < L.nst; ++s) {
+            const int gs0 = 8 * s, gsn = min(8, KG - gs0);
+            const int nch = gsn * 2;
+            for (int u = threadIdx.x; u < 16 * RT * nch; u += NT) {
+                const int r = u / nch, c = u - r * nch;
+                const int rt = r >> 4, row = tl[rt].row0 + (r & 15);
+                if (row < tl[rt].nrows)
+                    cp_async16(W + r * L.rs + gs0 * 8 + c * 4, tl[rt].w + (size_t)row * KW + (size_t)gs0 * 8 + c * 4);
+            }
+            cp_async_commit();
         }
     }
-    if (!SB_BULK) {
-        for (int i = threadIdx.x; i < 32 * ng; i += GV_THREADS) {
-            const int r = i / ng, gl = i - r * ng;
+    if (!SB_VEC) {
+        for (int i = threadIdx.x; i < 16 * RT * KG; i += NT) {
+            const int r = i / KG, gl = i - r * KG;
             const int rt = r >> 4, row = tl[rt].row0 + (r & 15);
             uint16_t sv = 0, bv = 0;
             if (row < tl[rt].nrows) {
-                sv = reinterpret_cast<const uint16_t*>(tl[rt].s)[(size_t)row * KG + kg0 + gl];
-                bv = reinterpret_cast<const uint16_t*>(tl[rt].b)[(size_t)row * KG + kg0 + gl];
+                sv = reinterpret_cast<const uint16_t*>(tl[rt].s)[(size_t)row * KG + gl];
+                bv = reinterpret_cast<const uint16_t*>(tl[rt].b)[(size_t)row * KG + gl];
             }
             Ssm[r * L.ngp + gl] = sv;
             Bsm[r * L.ngp + gl] = bv;
@@ -223,160 +306,159 @@ __global__ void __launch_bounds__(GV_THREADS) qgemv_kernel(const QmmArgs a) {
     pdl_wait();
 
     if (a.norm_w) {
-        for (int m = 0; m < M; ++m) {
-            float ss = 0.f;
-            for (int k = threadIdx.x * 8; k < K; k += GV_THREADS * 8) {
-                uint4 u = *reinterpret_cast<const uint4*>(a.x + (size_t)m * a.ldx + k);
-                uint32_t X[4] = {u.x, u.y, u.z, u.w};
+        // sum of squares of every activation row in one pass
+        float ss[8];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    float lo = bits_lo_f(X[i]), hi = bits_hi_f(X[i]);
-                    ss += lo * lo + hi * hi;
+        for (int m = 0; m < 8; ++m) ss[m] = 0.f;
+        for (int k = threadIdx.x * 8; k < K; k += NT * 8) {
+#pragma unroll
+            for (int m = 0; m < 8; ++m) {
+                if (m < M) {
+                    const uint4 u = *reinterpret_cast<const uint4*>(a.x + (size_t)m * a.ldx + k);
+                    const uint32_t X[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float lo = bits_lo_f(X[i]), hi = bits_hi_f(X[i]);
+                        ss[m] += lo * lo + hi * hi;
+                    }
                 }
             }
-            ss = warp_sum(ss);
-            if (lane == 0) red[warp] = ss;
-            __syncthreads();
-            if (threadIdx.x == 0) {
-                float tot = 0.f;
-                for (int w = 0; w < GV_WARPS; ++w) tot += red[w];
-                rnorm[m] = 1.0f / sqrtf(tot / (float)K + a.eps);
-            }
-            __syncthreads();
         }
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            if (m < M) {
+                const float v = warp_sum(ss[m]);
+                if (lane == 0) wred[m * NW + warp] = v;
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x < M) {
+            float tot = 0.f;
+            for (int w = 0; w < NW; ++w) tot += wred[threadIdx.x * NW + w];
+            rnorm[threadIdx.x] = 1.0f / sqrtf(tot / (float)K + a.eps);
+        }
+        __syncthreads();
     }
     {
-        const int units = ng * M * 4;
-        for (int u = threadIdx.x; u < units; u += GV_THREADS) {
-            const int gl = u / (M * 4);
-            const int rem = u - gl * M * 4;
-            const int m = rem >> 2, tt = rem & 3;
-            const int k = (kg0 + gl) * 64 + 16 * tt;
-            stage16(a.x + (size_t)m * a.ldx + k, a.norm_w ? a.norm_w + k : nullptr,
-                    a.norm_w ? rnorm[m] : 1.f, xs + (size_t)(gl * M + m) * XS_BLOCK_WORDS + tt * 8, nullptr);
+        // stage activations and even / odd group sums; uniform trip count so
+        // every lane takes part in the quad shuffles
+        const int units = KG * M * 4;
+        for (int u0 = 0; u0 < units; u0 += NT) {
+            const int u = u0 + threadIdx.x;
+            float se = 0.f, so = 0.f;
+            int gl = 0, m = 0, tt = 0;
+            if (u < units) {
+                gl = u / (M * 4);
+                const int rem = u - gl * M * 4;
+                m = rem >> 2;
+                tt = rem & 3;
+                const int k = gl * 64 + 16 * tt;
+                stage16_f16(a.x + (size_t)m * a.ldx + k, a.norm_w ? a.norm_w + k : nullptr,
+                            a.norm_w ? rnorm[m] : 1.f, xs + (size_t)(gl * M + m) * XS_BLOCK_WORDS + tt * 8, se, so);
+            }
+            se += __shfl_xor_sync(0xffffffffu, se, 1);
+            se += __shfl_xor_sync(0xffffffffu, se, 2);
+            so += __shfl_xor_sync(0xffffffffu, so, 1);
+            so += __shfl_xor_sync(0xffffffffu, so, 2);
+            if (u < units && tt == 0) {
+                xsum[gl * 16 + m] = se;
+                xsum[gl * 16 + 8 + m] = so;
+            }
         }
     }
-    __syncthreads();
 
-    float acc[2][4], bacc[2][4];
+    float acc[RT][4], bacc[RT][4];
 #pragma unroll
-    for (int rt = 0; rt < 2; ++rt)
+    for (int rt = 0; rt < RT; ++rt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[rt][e] = bacc[rt][e] = 0.f;
 
+    // per-lane bases: rows g / g+8 of every tile, activation column g
+    const uint32_t* xb = xs + g * XS_BLOCK_WORDS + t * 8;
+    const int xstride = M * XS_BLOCK_WORDS;
+    const bool has_col = g < M;
+
+    auto do_group = [&](int gl) {
+        uint4 be = make_uint4(0u, 0u, 0u, 0u), bo = be;
+        if (has_col) {
+            const uint4* p = reinterpret_cast<const uint4*>(xb + gl * xstride);
+            be = p[0];
+            bo = p[1];
+        }
+        const float2 xe = *reinterpret_cast<const float2*>(xsum + gl * 16 + 2 * t);
+        const float2 xo = *reinterpret_cast<const float2*>(xsum + gl * 16 + 8 + 2 * t);
+        const float xt0 = xe.x + xo.x, xt1 = xe.y + xo.y;
+        const float ie[4] = {-1024.f * xe.x, -1024.f * xe.y, -1024.f * xe.x, -1024.f * xe.y};
+        const float io[4] = {-1024.f * xo.x, -1024.f * xo.y, -1024.f * xo.x, -1024.f * xo.y};
+#pragma unroll
+        for (int rt = 0; rt < RT; ++rt) {
+            const int r0 = rt * 16 + g;
+            const uint2 wa = *reinterpret_cast<const uint2*>(W + r0 * L.rs + gl * 8 + 2 * t);
+            const uint2 wb = *reinterpret_cast<const uint2*>(W + (r0 + 8) * L.rs + gl * 8 + 2 * t);
+            const uint32_t wa8x = wa.x >> 8, wb8x = wb.x >> 8, wa8y = wa.y >> 8, wb8y = wb.y >> 8;
+            float ce[4], co[4];
+            mma_f16(ce, nib_even(wa.x), nib_even(wb.x), nib_even(wa8x), nib_even(wb8x), be.x, be.y, ie);
+            mma_f16(co, nib_odd(wa.x), nib_odd(wb.x), nib_odd(wa8x), nib_odd(wb8x), bo.x, bo.y, io);
+            mma_f16(ce, nib_even(wa.y), nib_even(wb.y), nib_even(wa8y), nib_even(wb8y), be.z, be.w, ce);
+            mma_f16(co, nib_odd(wa.y), nib_odd(wb.y), nib_odd(wa8y), nib_odd(wb8y), bo.z, bo.w, co);
+            const float s0 = u16_to_f(Ssm[r0 * L.ngp + gl]), s1 = u16_to_f(Ssm[(r0 + 8) * L.ngp + gl]);
+            const float b0 = u16_to_f(Bsm[r0 * L.ngp + gl]), b1 = u16_to_f(Bsm[(r0 + 8) * L.ngp + gl]);
+            // sum q*x = ce + co/16 (odd nibbles entered as 16q)
+            acc[rt][0] = fmaf(s0, fmaf(co[0], 0.0625f, ce[0]), acc[rt][0]);
+            acc[rt][1] = fmaf(s0, fmaf(co[1], 0.0625f, ce[1]), acc[rt][1]);
+            acc[rt][2] = fmaf(s1, fmaf(co[2], 0.0625f, ce[2]), acc[rt][2]);
+            acc[rt][3] = fmaf(s1, fmaf(co[3], 0.0625f, ce[3]), acc[rt][3]);
+            bacc[rt][0] = fmaf(b0, xt0, bacc[rt][0]);
+            bacc[rt][1] = fmaf(b0, xt1, bacc[rt][1]);
+            bacc[rt][2] = fmaf(b1, xt0, bacc[rt][2]);
+            bacc[rt][3] = fmaf(b1, xt1, bacc[rt][3]);
+        }
+    };
+
     for (int s = 0; s < L.nst; ++s) {
-        const bool ok = mbar_wait_bounded(&bar[s], 0);
-        if (__syncthreads_or(!ok)) {
-            // a transfer never completed: flag it, give the copies another
-            // bounded chance to land in this CTA's memory, and leave
-            if (threadIdx.x == 0) atomicOr(a.err, QW_DERR_TIMEOUT);
-            for (int s2 = s; s2 < L.nst; ++s2) mbar_wait_bounded(&bar[s2], 0);
-            return;
+        cp_async_wait_dyn(L.nst - 1 - s);
+        __syncthreads();
+        const int gs0 = 8 * s, gsn = min(8, KG - gs0);
+        int gi = warp;
+        for (; gi + NW < gsn; gi += 2 * NW) {
+            do_group(gs0 + gi);
+            do_group(gs0 + gi + NW);
         }
-        const int gs0 = 8 * s, gsn = min(8, ng - gs0);
-        for (int gi = warp; gi < gsn; gi += GV_WARPS) {
-            const int gl = gs0 + gi;
-            uint32_t bq[8];
-            if (g < M) {
-                const uint4* p = reinterpret_cast<const uint4*>(xs + (size_t)(gl * M + g) * XS_BLOCK_WORDS + t * 8);
-                const uint4 v0 = p[0], v1 = p[1];
-                bq[0] = v0.x; bq[1] = v0.y; bq[2] = v0.z; bq[3] = v0.w;
-                bq[4] = v1.x; bq[5] = v1.y; bq[6] = v1.z; bq[7] = v1.w;
-            } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) bq[i] = 0u;
-            }
-            // z = 128 * sum(x) of this group for columns 2t, 2t+1 (rows identical)
-            float z[4] = {0.f, 0.f, 0.f, 0.f};
-            mma_bf16(z, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, bq[0], bq[1], z);
-            mma_bf16(z, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, bq[2], bq[3], z);
-            mma_bf16(z, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, bq[4], bq[5], z);
-            mma_bf16(z, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, QW_BF16X2_128, bq[6], bq[7], z);
-#pragma unroll
-            for (int rt = 0; rt < 2; ++rt) {
-                const int r0 = rt * 16 + g;
-                const uint2 wa = *reinterpret_cast<const uint2*>(W + r0 * L.rs + gl * 8 + 2 * t);
-                const uint2 wb = *reinterpret_cast<const uint2*>(W + (r0 + 8) * L.rs + gl * 8 + 2 * t);
-                float cc[4] = {-z[0], -z[1], -z[2], -z[3]};
-                group_mma(cc, wa.x, wa.y, wb.x, wb.y, bq);
-                const float s0 = u16_to_f(Ssm[r0 * L.ngp + gl]), s1 = u16_to_f(Ssm[(r0 + 8) * L.ngp + gl]);
-                const float b0 = u16_to_f(Bsm[r0 * L.ngp + gl]), b1 = u16_to_f(Bsm[(r0 + 8) * L.ngp + gl]);
-                acc[rt][0] = fmaf(s0, cc[0], acc[rt][0]);
-                acc[rt][1] = fmaf(s0, cc[1], acc[rt][1]);
-                acc[rt][2] = fmaf(s1, cc[2], acc[rt][2]);
-                acc[rt][3] = fmaf(s1, cc[3], acc[rt][3]);
-                bacc[rt][0] = fmaf(b0, z[0], bacc[rt][0]);
-                bacc[rt][1] = fmaf(b0, z[1], bacc[rt][1]);
-                bacc[rt][2] = fmaf(b1, z[2], bacc[rt][2]);
-                bacc[rt][3] = fmaf(b1, z[3], bacc[rt][3]);
-            }
-        }
+        if (gi < gsn) do_group(gs0 + gi);
     }
 
-    // cross-warp reduction (fixed order)
+    // cross-warp reduction in a fixed order
 #pragma unroll
-    for (int rt = 0; rt < 2; ++rt)
+    for (int rt = 0; rt < RT; ++rt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-            red[(warp * 8 + rt * 4 + e) * 32 + lane] = fmaf(bacc[rt][e], 0.0078125f, acc[rt][e]);
+        for (int e = 0; e < 4; ++e) wred[warp * RT * 128 + (rt * 4 + e) * 32 + lane] = acc[rt][e] + bacc[rt][e];
     __syncthreads();
     if (warp != 0) return;
-    float v[2][4];
+    float v[RT][4];
 #pragma unroll
-    for (int rt = 0; rt < 2; ++rt)
+    for (int rt = 0; rt < RT; ++rt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            float s = 0.f;
-            for (int w = 0; w < GV_WARPS; ++w) s += red[(w * 8 + rt * 4 + e) * 32 + lane];
-            v[rt][e] = s;
+            float sum = 0.f;
+            for (int w = 0; w < NW; ++w) sum += wred[w * RT * 128 + (rt * 4 + e) * 32 + lane];
+            v[rt][e] = sum;
         }
 
-    if (nks > 1) {
-        const size_t pstride = (size_t)a.nrb * 32;
-#pragma unroll
-        for (int rt = 0; rt < 2; ++rt)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int col = 2 * t + (e & 1);
-                if (col < M)
-                    a.partial[((size_t)ks * M + col) * pstride + (size_t)rb * 32 + rt * 16 + g + 8 * (e >> 1)] = v[rt][e];
-            }
-        __threadfence();
-        __syncwarp();
-        unsigned prev = 0;
-        if (lane == 0) prev = atomicAdd(&a.counters[rb], 1u);
-        prev = __shfl_sync(0xffffffffu, prev, 0);
-        if (prev != (unsigned)(nks - 1)) return;
-        __threadfence();
-#pragma unroll
-        for (int rt = 0; rt < 2; ++rt)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int col = 2 * t + (e & 1);
-                float s = 0.f;
-                if (col < M)
-                    for (int k2 = 0; k2 < nks; ++k2)
-                        s += __ldcg(&a.partial[((size_t)k2 * M + col) * pstride + (size_t)rb * 32 + rt * 16 + g + 8 * (e >> 1)]);
-                v[rt][e] = s;
-            }
-        if (lane == 0) a.counters[rb] = 0u;
-    }
-
     if (a.epi == EPI_LOGITS) {
+        // bf16 logits (optionally stored) and this CTA's (value, index) maximum
+        // per activation row; a separate kernel reduces over the row blocks
         unsigned long long best[2] = {0ull, 0ull};
         const QSeg& sg = a.seg[si];
 #pragma unroll
-        for (int rt = 0; rt < 2; ++rt)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int row = tl[rt].row0 + g + 8 * (e >> 1);
-                const int col = 2 * t + (e & 1);
-                if (row < tl[rt].nrows && col < M) {
-                    const float l = bfr(v[rt][e]);
-                    if (a.store_logits) reinterpret_cast<bf16*>(sg.y)[(size_t)col * sg.ldy + row] = f2bf(l);
-                    best[e & 1] = umax64(best[e & 1], amax_key(l, (uint32_t)(row + a.amax_row_offset)));
-                }
+        for (int e = 0; e < 4; ++e) {
+            const int row = tl[0].row0 + g + 8 * (e >> 1);
+            const int col = 2 * t + (e & 1);
+            if (row < tl[0].nrows && col < M) {
+                const float l = bfr(v[0][e]);
+                if (a.store_logits) reinterpret_cast<bf16*>(sg.y)[(size_t)col * sg.ldy + row] = f2bf(l);
+                best[e & 1] = umax64(best[e & 1], amax_key(l, (uint32_t)(row + a.amax_row_offset)));
             }
+        }
 #pragma unroll
         for (int cp = 0; cp < 2; ++cp)
 #pragma unroll
@@ -386,24 +468,6 @@ __global__ void __launch_bounds__(GV_THREADS) qgemv_kernel(const QmmArgs a) {
             for (int cp = 0; cp < 2; ++cp)
                 if (2 * t + cp < M) a.amax_partial[(size_t)rb * M + 2 * t + cp] = best[cp];
         }
-        __threadfence();
-        __syncwarp();
-        unsigned prev = 0;
-        if (lane == 0) prev = atomicAdd(a.amax_counter, 1u);
-        prev = __shfl_sync(0xffffffffu, prev, 0);
-        if (prev != (unsigned)(gridDim.x - 1)) return;
-        __threadfence();
-        for (int col = 0; col < M; ++col) {
-            unsigned long long b = 0ull;
-            for (int r = lane; r < (int)gridDim.x; r += 32) b = umax64(b, __ldcg(&a.amax_partial[(size_t)r * M + col]));
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) b = umax64(b, __shfl_xor_sync(0xffffffffu, b, o));
-            if (lane == 0) {
-                a.amax_out[col] = (int)amax_key_index(b);
-                if (a.amax_key_out) a.amax_key_out[col] = b;
-            }
-        }
-        if (lane == 0) *a.amax_counter = 0u;
         return;
     }
 
@@ -411,16 +475,12 @@ __global__ void __launch_bounds__(GV_THREADS) qgemv_kernel(const QmmArgs a) {
     for (int e = 0; e < 4; ++e) {
         const int col = 2 * t + (e & 1);
         if (col >= M) continue;
-        if (a.epi == EPI_SWIGLU) {
-            const int feat = lrb * 16 + g + 8 * (e >> 1);
-            if (feat < a.seg[0].n) store_out(a, si, EPI_SWIGLU, 0, feat, col, v[0][e], v[1][e]);
-        } else {
-#pragma unroll
-            for (int rt = 0; rt < 2; ++rt) {
-                const int row = tl[rt].row0 + g + 8 * (e >> 1);
-                if (row < tl[rt].nrows) store_out(a, si, a.epi, row, 0, col, v[rt][e], 0.f);
-            }
-        }
+        const int row = tl[0].row0 + g + 8 * (e >> 1);
+        if (row >= tl[0].nrows) continue;
+        if (RT == 2)
+            store_out(a, si, EPI_SWIGLU, 0, row, col, v[0][e], v[RT - 1][e]);
+        else
+            store_out(a, si, a.epi, row, 0, col, v[0][e], 0.f);
     }
 }
 
@@ -578,20 +638,37 @@ cudaError_t launch_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStrea
 
 }  // namespace
 
+template <int RT, int NW>
+cudaError_t launch_qgemv_t(const QmmArgs& a, int nrb, size_t smem, cudaStream_t st, bool pdl) {
+    static bool set = false;
+    if (!set) {
+        cudaError_t e = cudaFuncSetAttribute(qgemv_kernel<RT, NW, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             220 * 1024);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(qgemv_kernel<RT, NW, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     220 * 1024);
+        if (e != cudaSuccess) return e;
+        set = true;
+    }
+    const int KG = a.K / 64;
+    if (KG % 8 == 0) return launch_ex(qgemv_kernel<RT, NW, true>, dim3(nrb), dim3(NW * 32), smem, st, pdl, a);
+    return launch_ex(qgemv_kernel<RT, NW, false>, dim3(nrb), dim3(NW * 32), smem, st, pdl, a);
+}
+
+int qgemv_row_blocks(const QmmArgs& a) {
+    if (a.epi == EPI_SWIGLU) return (a.seg[0].n + 15) / 16;
+    int nrb = 0;
+    for (int i = 0; i < a.nseg; ++i) nrb += (a.seg[i].n + 15) / 16;
+    return nrb;
+}
+
 cudaError_t launch_qgemv(QmmArgs a, cudaStream_t st, bool pdl, int num_sms) {
     (void)num_sms;
     if (a.M < 1 || a.M > 8 || a.K <= 0 || a.K % 64 != 0 || a.nseg < 1 || a.nseg > 3)
         return cudaErrorInvalidValue;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(qgemv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(qgemv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    const int RT = a.epi == EPI_SWIGLU ? 2 : 1;
     int nrb = 0;
-    if (a.epi == EPI_SWIGLU) {
+    if (RT == 2) {
         if (a.nseg < 2 || a.seg[0].n != a.seg[1].n) return cudaErrorInvalidValue;
         a.seg[0].rb0 = 0;
         a.seg[1].rb0 = 0;
@@ -600,26 +677,17 @@ cudaError_t launch_qgemv(QmmArgs a, cudaStream_t st, bool pdl, int num_sms) {
     } else {
         for (int i = 0; i < a.nseg; ++i) {
             a.seg[i].rb0 = nrb;
-            nrb += (a.seg[i].n + 31) / 32;
+            nrb += (a.seg[i].n + 15) / 16;
         }
     }
     a.nrb = nrb;
     const int KG = a.K / 64;
-    const int nunits = (KG + 7) / 8;
-    // Smallest K split whose weight slab (32 rows x ng groups x 36 B with
-    // scales/biases) stays near 28 KB, so several CTAs fit per SM and the
-    // kernel's whole weight stream can be in flight at once.
-    auto max_ng = [&](int ks) { return std::min(KG, 8 * ((nunits + ks - 1) / ks)); };
-    int ks = 1;
-    while (ks < nunits && ks < 16 && (32 * max_ng(ks) * 36 > 28 * 1024 || max_ng(ks) > 8 * GV2_MAX_STAGES)) ++ks;
-    if (ks > 1 && (a.partial == nullptr || a.counters == nullptr || (size_t)ks * a.M * nrb * 32 > a.partial_cap)) {
-        ks = 1;
-        if (max_ng(1) > 8 * GV2_MAX_STAGES) return cudaErrorInvalidValue;
-    }
-    const Gv2Layout L = gv2_layout(max_ng(ks), a.M);
-    if (L.total > 200 * 1024) return cudaErrorInvalidValue;
-    if (KG % 8 == 0) return launch_ex(qgemv_kernel<true>, dim3(nrb, ks), dim3(GV_THREADS), L.total, st, pdl, a);
-    return launch_ex(qgemv_kernel<false>, dim3(nrb, ks), dim3(GV_THREADS), L.total, st, pdl, a);
+    // long rows get 8 warps so each warp keeps a short list of groups
+    const int NW = KG > 48 ? 8 : 4;
+    const GvLayout L = gv_layout(KG, a.M, RT, NW);
+    if (L.total > 220 * 1024) return cudaErrorInvalidValue;
+    if (RT == 2) return NW == 8 ? launch_qgemv_t<2, 8>(a, nrb, L.total, st, pdl) : launch_qgemv_t<2, 4>(a, nrb, L.total, st, pdl);
+    return NW == 8 ? launch_qgemv_t<1, 8>(a, nrb, L.total, st, pdl) : launch_qgemv_t<1, 4>(a, nrb, L.total, st, pdl);
 }
 
 cudaError_t launch_qgemm(QmmArgs a, cudaStream_t st, int num_sms) {
