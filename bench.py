@@ -1,0 +1,398 @@
+"""Benchmark: Qwen3-4B 4-bit batch-1 greedy decode on B200.
+
+One step = one request of the reference's benchmark shape: a 512-token
+seeded-random prompt, prefill, then greedy decode of 300 tokens over a KV
+cache pre-allocated to 4096 positions, through qw_generate_greedy (the
+LoadedModel::generate_text equivalent).  Weights are random-init (seeded
+N(0,0.02) quantized to MLX affine 4-bit g64) generated on the device.
+
+* value  -- decode tok/s as the reference CLI bench defines it
+            (crates/base-mlx-cli/src/main.rs:96-179: (n-1) / (total - ttft)),
+            taken from CUDA events inside the library (inputs already on the
+            device; prefill excluded), summed over the K timed steps and all ranks.
+* e2e    -- the same metric through the C ABI with host buffers, timed on the
+            host exactly like main.rs: wall(generate 300) - wall(generate 1).
+* roofline -- the dominant kernel (qgemv, the quantized GEMV: ~3/4 of a decode
+            step in the ncu launch list) timed with CUDA events over the 4B
+            decode shapes on rotating weight copies (> L2), bytes = N*K*0.5625
+            + activations, against the measured HBM copy bandwidth.
+* cpu_baseline -- the oracle's CPU restatement of the same path (C qmatmul +
+            numpy), rank 0 at N=1 only, on a bounded sample (see `sample`).
+
+--impl reference times that CPU restatement alone (the reference itself is
+Rust over MLX/Metal and cannot be built or run on this machine).
+
+Multi-GPU: Qwen3-4B fits one GPU, so N GPUs run N independent replicas
+(weak scaling, no collective on the data path); value is the sum over ranks
+divided by the slowest rank's time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "base-mlx_b200"))
+
+PROMPT_LEN, DECODE_TOKENS, KV_PREALLOC, SEED = 512, 300, 4096, 1234
+REF_TOK_S = 32.75  # reference on M2-class Apple Silicon, 300-token greedy decode
+METRIC = "Qwen3-4B 4-bit batch-1 decode tok/s (plain & spec k=4); qmatmul HBM GB/s"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=lambda: self.lines.extend(self.proc.stdout), daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def prompt_ids(vocab: int) -> np.ndarray:
+    return np.random.default_rng(SEED).integers(0, vocab, PROMPT_LEN).astype(np.uint32)
+
+
+# ----------------------------------------------------------------- CPU leg ---
+
+class CpuModel:
+    """The oracle's CPU restatement of Qwen3-4B (C qmatmul + numpy) on seeded weights."""
+
+    def __init__(self):
+        from oracle import synth
+        from oracle.qwen3_ref import Qwen3Ref
+        cfg = dict(synth.QWEN3_4B)
+        t0 = time.time()
+        self.ref = Qwen3Ref(cfg, synth.build_tensors(cfg, SEED, "ones", fast=True), backend="c")
+        self.build_s = time.time() - t0
+        self.prompt = prompt_ids(cfg["vocab_size"])[:4].tolist()
+
+    def sample(self, decode_tokens: int):
+        """4-token prefill (untimed), then `decode_tokens` timed greedy steps; tok/s."""
+        cache = self.ref.new_cache(64)
+        tok = int(np.argmax(self.ref.forward(self.prompt, cache)))
+        t0 = time.time()
+        for _ in range(decode_tokens):
+            tok = int(np.argmax(self.ref.forward([tok], cache)))
+        return decode_tokens / (time.time() - t0)
+
+    def describe(self, decode_tokens: int) -> str:
+        return (f"oracle CPU restatement (C qmatmul + numpy), Qwen3-4B seeded weights, 4-token prefill then "
+                f"{decode_tokens} timed greedy decode steps at KV length 5-{4 + decode_tokens} (the GPU workload "
+                f"decodes at 512-812; attention is <5% of a 4B decode step's work); weight build "
+                f"{self.build_s:.1f}s not timed")
+
+
+def cpu_sample(decode_tokens: int, threads: int):
+    cm = CpuModel()
+    return cm.sample(decode_tokens), threads, cm.describe(decode_tokens)
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    cm = CpuModel()
+    per_step = []
+    for i in range(args.warmup + args.steps):
+        v = cm.sample(args.ref_tokens)
+        if i >= args.warmup:
+            per_step.append(v)
+    desc = cm.describe(args.ref_tokens)
+    value = float(np.mean(per_step))
+    line = {"metric": METRIC, "impl": "reference", "value": round(value, 4), "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": round(value / REF_TOK_S, 4), "dtype": "u4xbf16->f32", "data": "synthetic",
+            "config": {"workload": "config3: Qwen3-4B 4-bit g64, batch 1, greedy decode", "model": "Qwen3-4B",
+                       "prompt_len": PROMPT_LEN, "decode_tokens": DECODE_TOKENS},
+            "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "flakerimi/base-mlx is Rust over mlx-rs/MLX Metal: no Rust toolchain, no MLX and no Metal here, "
+                    "so the timed reference is the repository's CPU restatement of the same path (oracle/)"}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------- GPU leg ---
+
+def qgemv_roofline(q, torch, info, peak_gbs):
+    """Time the decode GEMV kernel over one layer's 4B shapes + lm_head on
+    rotating weight copies (> L2) in a CUDA graph; return achieved GB/s."""
+    lib = q.lib()
+    dev = torch.device("cuda")
+    H, I, V = info.hidden, info.intermediate, info.vocab
+    QD, KD = info.num_heads * info.head_dim, info.num_kv_heads * info.head_dim
+    shapes = [(H, QD + 2 * KD), (QD, H), (H, 2 * I), (I, H), (H, V)]
+    total_bytes, launches = 0.0, []
+    bufs = []
+    for K, N in shapes:
+        nrep = max(2, int(300e6 // (N * K * 0.5625)) + 1)
+        w = torch.randint(-2 ** 31, 2 ** 31 - 1, (nrep, N, K // 8), dtype=torch.int32, device=dev)
+        s = (torch.rand(nrep, N, K // 64, device=dev) * 0.01).to(torch.bfloat16)
+        b = (torch.rand(nrep, N, K // 64, device=dev) * -0.01).to(torch.bfloat16)
+        x = torch.randn(1, K, device=dev).to(torch.bfloat16)
+        y = torch.empty(1, N, device=dev, dtype=torch.bfloat16)
+        bufs.append((w, s, b, x, y))
+        for i in range(nrep):
+            launches.append((x.data_ptr(), w[i].data_ptr(), s[i].data_ptr(), b[i].data_ptr(), y.data_ptr(), N, K))
+        total_bytes += nrep * (N * K * 0.5625 + 2 * K + 2 * N)
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        def run_all():
+            for (xp, wp, sp, bp, yp, N, K) in launches:
+                q.check(lib.qw_quantized_matmul(xp, wp, sp, bp, yp, 1, N, K, 64, 4, st.cuda_stream))
+        run_all()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            run_all()
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 3
+        e0.record(st)
+        for _ in range(reps):
+            g.replay()
+        e1.record(st)
+        torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3 / reps
+    achieved = total_bytes / sec / 1e9
+    del bufs, g
+    torch.cuda.empty_cache()
+    return achieved, len(launches), total_bytes / len(launches)
+
+
+def launches_per_generation(info, prompt_len, decode_tokens):
+    """Kernels the library launches for one greedy generation (for gpu_launches)."""
+    L = info.num_layers
+    prefill = 1 + 8 * L + 3   # embed; per layer 2 rmsnorm, 4 qgemm, qk-norm/rope/kv, attention; lm_head, finalize, step
+    decode = 1 + 5 * L + 3    # embed; per layer 4 qgemv + attention; lm_head, finalize, step
+    return prefill + (decode_tokens - 1) * decode
+
+
+def run_ours(args):
+    import torch
+    import qwen3_b200 as q
+    from oracle import synth
+    rank, world, local = dist_env()
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300))
+    torch.cuda.set_device(local)
+    cfg = dict(synth.QWEN3_4B)
+    m = q.Qwen3.init_random(cfg, SEED, norm_mode="ones", device=local)
+    info = m.info
+    prompt = prompt_ids(cfg["vocab_size"])
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        m.generate_greedy(prompt, DECODE_TOKENS)
+    barrier()
+    results = []
+    with ClockSampler(local) as clk:
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            results.append(m.generate_greedy(prompt, DECODE_TOKENS))
+        barrier()
+        region = time.perf_counter() - t0
+    decode_ms = sum(r.decode_ms for r in results)
+    prefill_ms = sum(r.prefill_ms for r in results)
+    dec_tokens = sum(max(r.completion_tokens - 1, 0) for r in results)
+    gen_tokens = sum(r.completion_tokens for r in results)
+    vals = torch.tensor([decode_ms, region, float(dec_tokens), float(gen_tokens)], dtype=torch.float64,
+                        device="cuda")
+    if dist is not None:
+        mx = vals.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = vals.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        decode_ms_max, region_max, dec_tokens_all, gen_tokens_all = mx[0].item(), mx[1].item(), sm[2].item(), sm[3].item()
+    else:
+        decode_ms_max, region_max, dec_tokens_all, gen_tokens_all = decode_ms, region, dec_tokens, gen_tokens
+    value = dec_tokens_all / (decode_ms_max / 1e3)
+
+    # e2e through the C ABI with host buffers, the reference CLI bench's way
+    e2e_rates = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        full = m.generate_greedy(prompt, DECODE_TOKENS)
+        t_full = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        m.generate_greedy(prompt, 1)
+        t_ttft = time.perf_counter() - t0
+        e2e_rates.append((full.completion_tokens - 1) / max(t_full - t_ttft, 1e-6))
+    e2e_local = float(np.mean(e2e_rates))
+    e2e_t = torch.tensor([e2e_local], dtype=torch.float64, device="cuda")
+    if dist is not None:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.SUM)
+    e2e_value = e2e_t.item()
+
+    peak, peak_kind = peaks()
+    extra = {}
+    cpu = None
+    if rank == 0:
+        ach, nl, per_launch = qgemv_roofline(q, torch, info, peak)
+        # algorithmic bytes of one decode step: all quantized weights + KV read at the mean position
+        w_bytes = 0
+        H, I, V, L = info.hidden, info.intermediate, info.vocab, info.num_layers
+        QD, KD = info.num_heads * info.head_dim, info.num_kv_heads * info.head_dim
+        w_bytes = (L * (H * (QD + 2 * KD) + QD * H + 2 * H * I + I * H) + V * H) * 0.5625
+        mean_T = PROMPT_LEN + DECODE_TOKENS / 2
+        kv_bytes = L * 2 * KD * 2 * mean_T
+        step_s = decode_ms / 1e3 / max(dec_tokens, 1)
+        extra["step_roofline"] = {"bound": "hbm", "achieved": round((w_bytes + kv_bytes) / step_s / 1e9, 1),
+                                  "peak": peak, "unit": "GB/s",
+                                  "frac": round((w_bytes + kv_bytes) / step_s / 1e9 / peak, 4),
+                                  "bytes_per_token": int(w_bytes + kv_bytes),
+                                  "note": "whole decode step (weights + KV at mean position 662) / device time"}
+        roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
+                "traffic": None, "kernel": "qgemv (decode quantized GEMV), M=1, 4B layer shapes + lm_head",
+                "bytes_per_launch": int(per_launch), "launches_timed": nl, "peak_source": peak_kind}
+        if world == 1 and not args.no_cpu:
+            v, cores, desc = cpu_sample(args.cpu_tokens, os.cpu_count() or 1)
+            cpu = {"value": round(v, 4), "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
+        if args.spec:
+            extra["spec"] = spec_measure(q, m, prompt, cfg)
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(region_max * 1e3 / args.steps, 3),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": round(value / REF_TOK_S, 3),
+                "dtype": "u4xbf16->f32", "data": "synthetic (seeded random-init weights and prompt ids)",
+                "config": {"workload": "config3: Qwen3-4B 4-bit g64, batch 1, 512-token prompt, greedy decode 300, "
+                                       "KV pre-allocated 4096 (bf16)",
+                           "model": "Qwen3-4B (random init)", "prompt_len": PROMPT_LEN,
+                           "decode_tokens": DECODE_TOKENS, "kv_prealloc": KV_PREALLOC,
+                           "parallelism": f"replicas x{world}",
+                           "l2": "no flush: every decode step streams 2.26 GB of weights (> 126 MB L2)"},
+                "roofline": roof, "cpu_baseline": cpu,
+                "e2e": {"value": round(e2e_value, 2), "unit": "tok/s",
+                        "h2d_bytes_per_step": PROMPT_LEN * 4, "d2h_bytes_per_step": DECODE_TOKENS * 4 + 40},
+                "gpu_launches": launches_per_generation(info, PROMPT_LEN, DECODE_TOKENS) * args.steps,
+                "clocks": clk.summary(),
+                "decode_ms_per_token": round(decode_ms / max(dec_tokens, 1), 4),
+                "ttft_ms": round(prefill_ms / len(results), 3),
+                "gen_tok_s_incl_prefill": round(gen_tokens_all / (region_max), 2)}
+        line.update(extra)
+        print(json.dumps(line), flush=True)
+    m.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def spec_measure(q, target, prompt, cfg4):
+    """Config 4: 4B target + 0.6B draft, k=4, forced acceptance p in {0.8, 1.0}."""
+    from oracle import synth
+    draft = q.Qwen3.init_random(dict(synth.QWEN3_0_6B), SEED + 1, norm_mode="ones", device=0)
+    plain = target.generate_greedy(prompt, DECODE_TOKENS)
+    out = {"k": 4, "plain_decode_tok_s": round((plain.completion_tokens - 1) / (plain.decode_ms / 1e3), 2)}
+    for p in (0.8, 1.0):
+        q.speculative_generate(target, draft, prompt, DECODE_TOKENS, k=4, force_p=p, seed=7, forced=plain.tokens)
+        res, st = q.speculative_generate(target, draft, prompt, DECODE_TOKENS, k=4, force_p=p, seed=7,
+                                         forced=plain.tokens)
+        dec_ms = st.total_ms - st.prefill_ms
+        out[f"p{p}"] = {"tok_s": round((res.completion_tokens - 1) / (dec_ms / 1e3), 2),
+                        "tokens_match_plain": res.tokens == plain.tokens,
+                        "iters": st.iters, "accepted": st.accepted, "proposed": st.proposed,
+                        "draft_ms_mean": round(st.draft_ms_mean, 3), "verify_ms_mean": round(st.verify_ms_mean, 3),
+                        "accept_ms_mean": round(st.accept_ms_mean, 3)}
+        out[f"p{p}"]["speedup_vs_plain"] = round(out[f"p{p}"]["tok_s"] / out["plain_decode_tok_s"], 3)
+    draft.close()
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--cpu-tokens", type=int, default=8)
+    ap.add_argument("--ref-tokens", type=int, default=4)
+    ap.add_argument("--no-spec", dest="spec", action="store_false")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

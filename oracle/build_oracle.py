@@ -16,11 +16,13 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 def build(verbose: bool = False) -> str:
     out_dir = os.path.join(HERE, "_build")
     os.makedirs(out_dir, exist_ok=True)
-    src = os.path.join(HERE, "qmm_ref.c")
+    srcs = [os.path.join(HERE, "qmm_ref.c"), os.path.join(HERE, "synth_ref.c")]
     out = os.path.join(out_dir, "libqmm_ref.so")
-    if os.path.exists(out) and os.path.getmtime(out) >= os.path.getmtime(src):
+    if os.path.exists(out) and all(os.path.getmtime(out) >= os.path.getmtime(s) for s in srcs):
         return out
-    cmd = ["gcc", "-O3", "-march=x86-64-v2", "-fopenmp", "-shared", "-fPIC", "-o", out, src]
+    # no -ffast-math / FMA contraction: the restatement relies on IEEE fp32 steps
+    cmd = ["gcc", "-O3", "-march=x86-64-v2", "-ffp-contract=off", "-fopenmp", "-shared", "-fPIC", "-o", out, *srcs,
+           "-lm"]
     if verbose:
         print(" ".join(cmd))
     subprocess.check_call(cmd)

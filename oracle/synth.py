@@ -95,8 +95,42 @@ def iter_tensors(cfg: dict, seed: int, norm_mode: str = "ones"):
         yield "lm_head.biases", b
 
 
-def build_tensors(cfg: dict, seed: int, norm_mode: str = "ones") -> dict:
-    return dict(iter_tensors(cfg, seed, norm_mode))
+def build_tensors(cfg: dict, seed: int, norm_mode: str = "ones", fast: bool = False) -> dict:
+    """All tensors of the synthetic checkpoint; fast=True generates the
+    quantized weights with the multithreaded C restatement (oracle/synth_ref.c)."""
+    if not fast:
+        return dict(iter_tensors(cfg, seed, norm_mode))
+    out = {}
+    for name, arr in iter_tensors_fast(cfg, seed, norm_mode):
+        out[name] = arr
+    return out
+
+
+def quantized_weight_c(seed: int, tensor_id: int, n: int, k: int, std: float = 0.02, threads: int = 0):
+    """Same as numerics.quantized_weight, computed by oracle/synth_ref.c."""
+    import ctypes
+    from .qwen3_ref import _lib
+    lib = _lib()
+    fn = lib.synth_qweight
+    fn.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 5 + [ctypes.c_uint64, ctypes.c_float, ctypes.c_int]
+    fn.restype = ctypes.c_int
+    w = np.empty((n, k // 8), np.uint32)
+    s = np.empty((n, k // 64), np.uint16)
+    b = np.empty((n, k // 64), np.uint16)
+    rc = fn(w.ctypes.data, s.ctypes.data, b.ctypes.data, n, k, 0, 0, k, nm.tensor_key(seed, tensor_id),
+            float(nm.normal_scale(std)), threads)
+    if rc != 0:
+        raise RuntimeError("synth_qweight failed")
+    return w, s, b
+
+
+def iter_tensors_fast(cfg: dict, seed: int, norm_mode: str = "ones"):
+    saved = nm.quantized_weight
+    try:
+        nm.quantized_weight = quantized_weight_c
+        yield from iter_tensors(cfg, seed, norm_mode)
+    finally:
+        nm.quantized_weight = saved
 
 
 _DT = {np.dtype(np.uint32): "U32", np.dtype(np.uint16): "BF16", np.dtype(np.int32): "I32",
