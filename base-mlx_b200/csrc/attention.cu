@@ -84,17 +84,18 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
         if (tid == 0) atomicOr(a.err, T > a.max_pos ? QW_DERR_KV_RANGE : QW_DERR_SHAPE);
         return;
     }
-    int per = (T + nsplit - 1) / nsplit;
-    per = (per + 15) & ~15;
-    const int lo = split * per;
-    const int hi = min(T, lo + per);
-    const int ntiles = hi > lo ? (hi - lo + TILE - 1) / TILE : 0;
+    // Keys are cut into fixed 64-key chunks, chunk c handled by CTA c % nsplit
+    // in increasing c.  The summation order of a row therefore does not depend
+    // on T: a verify of S rows and S single-row decodes produce bit-identical
+    // outputs (chunks past a row's causal limit only add exact zeros).
+    const int nchunks = (T + TILE - 1) / TILE;
+    const int ntiles = split < nchunks ? (nchunks - split + nsplit - 1) / nsplit : 0;
     const bf16* kbase = a.kcache + (size_t)kvh * a.max_pos * D;
     const bf16* vbase = a.vcache + (size_t)kvh * a.max_pos * D;
 
-    // cached (old) rows of a tile -> shared memory, asynchronously
+    // cached (old) rows of a chunk -> shared memory, asynchronously
     auto load_tile = [&](int buf, int j0) {
-        const int nold = max(0, min(j0 + TILE, min(hi, off)) - j0);
+        const int nold = max(0, min(j0 + TILE, min(T, off)) - j0);
         for (int idx = tid; idx < nold * 16; idx += 128) {
             const int r = idx >> 4, c = idx & 15;
             cp_async16(&sm.kt[buf][r][(c ^ (r & 15)) * 8], kbase + (size_t)(j0 + r) * D + c * 8);
@@ -102,8 +103,8 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
         }
         cp_async_commit();
     };
-    if (ntiles > 0) load_tile(0, lo);
-    if (ntiles > 1) load_tile(1, lo + TILE);
+    if (ntiles > 0) load_tile(0, split * TILE);
+    if (ntiles > 1) load_tile(1, (split + nsplit) * TILE);
 
     // queries: q_norm + rope
     for (int r = warp; r < R; r += 4) {
@@ -117,9 +118,9 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
         sm.qs[r][HALF + 2 * lane] = o[2];
         sm.qs[r][HALF + 2 * lane + 1] = o[3];
     }
-    // new keys / values owned by this slice: cache write + local copy
-    const int nlo = max(lo, off), nhi = min(hi, T);
-    for (int p = nlo + warp; p < nhi; p += 4) {
+    // new keys / values of this CTA's chunks: cache write + local copy
+    for (int p = off + warp; p < T; p += 4) {
+        if ((p / TILE) % nsplit != split) continue;
         const int i = p - off;
         float o[4];
         norm_rope_row(a.k + (size_t)i * a.ldk + kvh * D, a.k_norm_w, a.eps, a.rope_cos + (size_t)p * HALF,
@@ -146,7 +147,8 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
     constexpr int RH = (RMAX + 1) / 2;
 
     for (int it = 0; it < ntiles; ++it) {
-        const int buf = it & 1, j0 = lo + it * TILE;
+        const int buf = it & 1, j0 = (split + it * nsplit) * TILE;
+        const int hi = min(T, j0 + TILE);
         if (it + 1 < ntiles)
             cp_async_wait<1>();
         else
@@ -238,7 +240,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
             }
         }
         __syncthreads();
-        if (it + 2 < ntiles) load_tile(buf, lo + (it + 2) * TILE);
+        if (it + 2 < ntiles) load_tile(buf, (split + (it + 2) * nsplit) * TILE);
     }
 
     // partial -> global
