@@ -43,6 +43,16 @@ sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "base-mlx_b200"))
 
 PROMPT_LEN, DECODE_TOKENS, KV_PREALLOC, SEED = 512, 300, 4096, 1234
+
+# Workload shapes (config.json contents of the random-init models)
+CFG_0_6B = dict(
+    model_type="qwen3", hidden_size=1024, intermediate_size=3072, num_hidden_layers=28,
+    num_attention_heads=16, num_key_value_heads=8, head_dim=128, vocab_size=151936,
+    rms_norm_eps=1e-6, rope_theta=1000000.0, tie_word_embeddings=True,
+    max_position_embeddings=40960, bos_token_id=151643, eos_token_id=151645,
+    quantization=dict(group_size=64, bits=4))
+CFG_4B = dict(CFG_0_6B, hidden_size=2560, intermediate_size=9728, num_hidden_layers=36,
+              num_attention_heads=32, num_key_value_heads=8)
 REF_TOK_S = 32.75  # reference on M2-class Apple Silicon, 300-token greedy decode
 METRIC = "Qwen3-4B 4-bit batch-1 decode tok/s (plain & spec k=4); qmatmul HBM GB/s"
 
@@ -240,7 +250,6 @@ def launches_per_generation(info, prompt_len, decode_tokens):
 def run_ours(args):
     import torch
     import qwen3_b200 as q
-    from oracle import synth
     rank, world, local = dist_env()
     dist = None
     if world > 1:
@@ -248,7 +257,7 @@ def run_ours(args):
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300))
     torch.cuda.set_device(local)
-    cfg = dict(synth.QWEN3_4B)
+    cfg = dict(CFG_4B)
     m = q.Qwen3.init_random(cfg, SEED, norm_mode="ones", device=local)
     info = m.info
     prompt = prompt_ids(cfg["vocab_size"])
@@ -356,8 +365,7 @@ def run_ours(args):
 
 def spec_measure(q, target, prompt, cfg4):
     """Config 4: 4B target + 0.6B draft, k=4, forced acceptance p in {0.8, 1.0}."""
-    from oracle import synth
-    draft = q.Qwen3.init_random(dict(synth.QWEN3_0_6B), SEED + 1, norm_mode="ones", device=0)
+    draft = q.Qwen3.init_random(dict(CFG_0_6B), SEED + 1, norm_mode="ones", device=0)
     plain = target.generate_greedy(prompt, DECODE_TOKENS)
     out = {"k": 4, "plain_decode_tok_s": round((plain.completion_tokens - 1) / (plain.decode_ms / 1e3), 2)}
     for p in (0.8, 1.0):
@@ -375,6 +383,20 @@ def spec_measure(q, target, prompt, cfg4):
     return out
 
 
+def profile_decode(n: int) -> None:
+    """The bench model's prefill and n decode steps, one qw_forward each (for ncu launch lists)."""
+    import torch
+    import qwen3_b200 as q
+    cfg = dict(CFG_4B)
+    m = q.Qwen3.init_random(cfg, SEED, norm_mode="ones", device=0)
+    c = m.new_cache(KV_PREALLOC)
+    _, tok = m.forward(prompt_ids(cfg["vocab_size"]).tolist(), c, want_logits=False)
+    for _ in range(n):
+        _, tok = m.forward([tok], c, want_logits=False)
+    torch.cuda.synchronize()
+    print(f"profile_decode: prefill {PROMPT_LEN} + {n} decode steps, last token {tok}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -385,10 +407,15 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=8)
     ap.add_argument("--ref-tokens", type=int, default=4)
     ap.add_argument("--no-spec", dest="spec", action="store_false")
+    ap.add_argument("--profile-decode", type=int, default=0, metavar="N",
+                    help="profiling workload for ncu: weight init, the 512-token prefill and N greedy decode "
+                         "steps of the bench model through qw_forward; prints no bench line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.profile_decode > 0:
+        profile_decode(args.profile_decode)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
