@@ -383,3 +383,76 @@ int qw_quantized_matmul(const void* x, const void* w, const void* scales, const 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// qw_quantized_matmul_argmax_static: the lm_head GEMV + argmax with its
+// per-CTA maxima in a static device array instead of a workspace allocation.
+// ---------------------------------------------------------------------------
+namespace {
+
+// Slot (rb, m) = this row block's packed (logit, index) maximum of row m.
+// Every slot the finalize kernel reads is written earlier by the same call, so
+// nothing in it has to start at zero.
+static __device__ __align__(256) unsigned long long g_static_amax[QW_STATIC_AMAX_SLOTS];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+unsigned long long* g_static_amax_ptr[kMaxDevices] = {};
+
+// Address of g_static_amax on device `dev` (the current device), looked up on
+// the first call for that device.
+unsigned long long* static_amax(int dev) {
+    if (dev < 0 || dev >= kMaxDevices) throw qw::Error(QW_ERR_INVALID_ARG, "device ordinal out of range");
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    if (!g_static_amax_ptr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_static_amax);
+        if (e != cudaSuccess || !p)
+            throw qw::Error(QW_ERR_CUDA, std::string("cudaGetSymbolAddress(static argmax scratch): ") +
+                                             cudaGetErrorString(e));
+        g_static_amax_ptr[dev] = static_cast<unsigned long long*>(p);
+    }
+    return g_static_amax_ptr[dev];
+}
+
+}  // namespace
+
+extern "C" int qw_quantized_matmul_argmax_static(const void* x, const void* w, const void* scales,
+                                                 const void* biases, void* y_or_null, int* argmax_dev, int M,
+                                                 int N, int K, int group_size, int bits, void* stream) {
+    return guard([&] {
+        need(x && w && scales && biases && argmax_dev, "pointers");
+        if (group_size != 64 || bits != 4)
+            throw qw::Error(QW_ERR_UNSUPPORTED, "only group_size 64 / bits 4 are supported");
+        need(M >= 1 && M <= 8 && N >= 1 && K >= 64 && K % 64 == 0,
+             "shape (1 <= M <= 8, N >= 1, K a positive multiple of 64)");
+        const long long slots = (long long)M * ((N + 15) / 16);
+        if (slots > QW_STATIC_AMAX_SLOTS)
+            throw qw::Error(QW_ERR_INVALID_ARG, "qw_quantized_matmul_argmax_static: M * ceil(N/16) = " +
+                                                    std::to_string(slots) + " exceeds the static scratch of " +
+                                                    std::to_string(QW_STATIC_AMAX_SLOTS) + " slots");
+        int dev = 0;
+        QW_CUDA(cudaGetDevice(&dev));
+        unsigned long long* scratch = static_amax(dev);
+        qw::QmmArgs a;
+        std::memset(&a, 0, sizeof(a));
+        a.x = (const bf16*)x;
+        a.ldx = K;
+        a.M = M;
+        a.K = K;
+        a.seg[0].w = (const uint32_t*)w;
+        a.seg[0].s = (const bf16*)scales;
+        a.seg[0].b = (const bf16*)biases;
+        a.seg[0].y = y_or_null;
+        a.seg[0].n = N;
+        a.seg[0].ldy = N;
+        a.nseg = 1;
+        a.epi = qw::EPI_LOGITS;
+        a.store_logits = y_or_null ? 1 : 0;
+        a.amax_partial = scratch;
+        cudaStream_t st = (cudaStream_t)stream;
+        QW_CUDA(qw::launch_qgemv(a, st, false, 0));
+        QW_CUDA(qw::launch_amax_finalize(scratch, qw::qgemv_row_blocks(a), M, argmax_dev, nullptr, st));
+    });
+}
+

@@ -127,6 +127,7 @@ SIGNATURES = {
     "qw_spec_generate": [P, P, U32P, I, I, I, ctypes.c_float, ctypes.c_uint64, U32P, I, U32P, I, U32P,
                          ctypes.POINTER(I), ctypes.POINTER(SpecStats)],
     "qw_quantized_matmul": [P, P, P, P, P, I, I, I, I, I, P],
+    "qw_quantized_matmul_argmax_static": [P, P, P, P, P, P, I, I, I, I, I, P],
 }
 
 
@@ -336,3 +337,18 @@ def quantized_matmul(x_ptr: int, w_ptr: int, s_ptr: int, b_ptr: int, y_ptr: int,
                      group_size: int = 64, bits: int = 4, stream: int = 0) -> None:
     """y[M,N] = x[M,K] . dequant(W)^T on device pointers (MLX layout, bf16 x/y)."""
     check(lib().qw_quantized_matmul(x_ptr, w_ptr, s_ptr, b_ptr, y_ptr, M, N, K, group_size, bits, stream or None))
+
+
+STATIC_AMAX_SLOTS = 131072  # QW_STATIC_AMAX_SLOTS
+
+
+def quantized_matmul_argmax_static(x_ptr: int, w_ptr: int, s_ptr: int, b_ptr: int, y_ptr: int, argmax_ptr: int,
+                                   M: int, N: int, K: int, group_size: int = 64, bits: int = 4,
+                                   stream: int = 0) -> None:
+    """Logits head that allocates nothing: y[M,N] (bf16, skipped when y_ptr is 0)
+    = x . dequant(W)^T and argmax[m] (int32) on device pointers.  Its scratch
+    is a static device array of STATIC_AMAX_SLOTS slots (M * ceil(N/16) must
+    fit); concurrent calls on one device race on it.  The first call on a
+    device should come before any stream capture."""
+    check(lib().qw_quantized_matmul_argmax_static(x_ptr, w_ptr, s_ptr, b_ptr, y_ptr or None, argmax_ptr, M, N, K,
+                                                  group_size, bits, stream or None))

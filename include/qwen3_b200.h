@@ -168,6 +168,33 @@ QW_API int qw_spec_generate(qw_model* target, qw_model* draft, const uint32_t* p
 QW_API int qw_quantized_matmul(const void* x, const void* w, const void* scales, const void* biases,
                                void* y, int M, int N, int K, int group_size, int bits, void* stream);
 
+/* ---- standalone op without workspace ------------------------------------ */
+
+/* Scratch of qw_quantized_matmul_argmax_static: 131072 per-CTA maxima of
+ * 8 bytes (1 MiB) in a static device array of the library. */
+#define QW_STATIC_AMAX_SLOTS 131072
+
+/* Greedy logits head that allocates no memory: y[M,N] (bf16, optional) =
+ * x[M,K] . dequant(W)^T as in qw_quantized_matmul, plus argmax_dev[m] (int32,
+ * device) = the lowest index of row m's largest bf16 logit.  No counterpart in
+ * the reference (mlx-rs allocates every intermediate through MLX's allocator);
+ * it serves callers that cannot allocate device memory on the call: a host
+ * whose device memory is fully reserved up front (weights, KV arena), or one
+ * that must not synchronise the device, which cudaMalloc/cudaFree can do.
+ *   - Its per-CTA maxima live in a file-scope device array of
+ *     QW_STATIC_AMAX_SLOTS slots; M (1..8) * ceil(N / 16) must not exceed it,
+ *     otherwise QW_ERR_INVALID_ARG with the sizes in the message
+ *     (Qwen3's 151936-entry vocabulary uses 75968 slots at M = 8).
+ *   - The first call on each device (that device current) looks the array's
+ *     address up once; make that first call before any stream capture.
+ *   - It calls no cudaMalloc, cudaFree or other allocating routine.
+ *   - Calls that overlap on the GPU on one device (two streams, two host
+ *     threads) share the array and race; serialise them.
+ * Only group_size 64 and bits 4 are supported. */
+QW_API int qw_quantized_matmul_argmax_static(const void* x, const void* w, const void* scales,
+                                             const void* biases, void* y_or_null, int* argmax_dev, int M,
+                                             int N, int K, int group_size, int bits, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
