@@ -12,295 +12,25 @@
 // The cache length lives on the device (seq_len) so a captured step graph can
 // be replayed at every position; positions past max_pos raise an error flag
 // instead of being written.
-#include "kernels.h"
+#include "attn_decode.cuh"
 
 namespace qw {
 namespace {
 
-constexpr int D = 128;
-constexpr int HALF = 64;
-constexpr int TILE = 64;
+using namespace attn;
 
-// RMSNorm over one 128-wide head row followed by RoPE at position pos.
-// Lane l handles dims {2l, 2l+1} and {64+2l, 64+2l+1}; returns the 4 bf16
-// results (as floats) in o[0..3] = dims 2l, 2l+1, 64+2l, 64+2l+1.
-QW_DEV void norm_rope_row(const bf16* row, const bf16* nw, float eps, const float* cosr, const float* sinr,
-                          int lane, float (&o)[4]) {
-    const uint32_t lo = *reinterpret_cast<const uint32_t*>(row + 2 * lane);
-    const uint32_t hi = *reinterpret_cast<const uint32_t*>(row + HALF + 2 * lane);
-    float x[4] = {bits_lo_f(lo), bits_hi_f(lo), bits_lo_f(hi), bits_hi_f(hi)};
-    float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
-    ss = warp_sum(ss);
-    const float r = 1.0f / sqrtf(ss / (float)D + eps);
-    const uint32_t wlo = *reinterpret_cast<const uint32_t*>(nw + 2 * lane);
-    const uint32_t whi = *reinterpret_cast<const uint32_t*>(nw + HALF + 2 * lane);
-    const float w[4] = {bits_lo_f(wlo), bits_hi_f(wlo), bits_lo_f(whi), bits_hi_f(whi)};
-    float n[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) n[i] = bfr(__fmul_rn(__fmul_rn(x[i], r), w[i]));
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-        const float c = cosr[2 * lane + e], s = sinr[2 * lane + e];
-        o[e] = bfr(__fsub_rn(__fmul_rn(n[e], c), __fmul_rn(n[2 + e], s)));
-        o[2 + e] = bfr(__fadd_rn(__fmul_rn(n[2 + e], c), __fmul_rn(n[e], s)));
-    }
-}
-
-// ---------------------------------------------------------------------------
-// Decode / verify attention (S <= 8 new rows).  Grid (kv_heads, nsplit): each
-// CTA handles the G = Hq/Hkv query heads of one kv head (R = G*S rows) over one
-// contiguous slice of key positions, writes an unnormalised partial
-// (max, sum, o[128]) per row, and the last CTA of the kv head merges them.
-// Cached K/V rows stream through two 64-key shared-memory tiles with 16-byte
-// asynchronous copies (K chunks XOR-swizzled by row, so a thread-per-key read
-// is bank-conflict free); the new positions' k/v are normalised + rotated by
-// the CTA that owns them, written to the cache and placed into the tile
-// directly.
-// ---------------------------------------------------------------------------
-template <int RMAX>
-struct DecSmem {
-    float qs[RMAX][D];
-    float sc[RMAX][TILE];
-    float mrow[RMAX], lrow[RMAX], alph[RMAX];
-    bf16 kt[2][TILE][D];
-    bf16 vt[2][TILE][D];
-    bf16 nk[8][D], nv[8][D];
-    int last;
+// CUDA-core block barrier for the standalone kernel (128 threads).
+struct CtaSync {
+    QW_DEV void operator()() const { __syncthreads(); }
 };
 
 template <int RMAX>
 __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
     extern __shared__ __align__(16) unsigned char smraw[];
     DecSmem<RMAX>& sm = *reinterpret_cast<DecSmem<RMAX>*>(smraw);
-    const int kvh = blockIdx.x, split = blockIdx.y, nsplit = gridDim.y;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int S = a.S, G = a.Hq / a.Hkv, R = G * S;
-
     pdl_wait();
     pdl_launch_dependents();
-    const int off = *a.seq_len;
-    const int T = off + S;
-    if (T > a.max_pos || R > RMAX) {
-        if (tid == 0) atomicOr(a.err, T > a.max_pos ? QW_DERR_KV_RANGE : QW_DERR_SHAPE);
-        return;
-    }
-    // Keys are cut into fixed 64-key chunks, chunk c handled by CTA c % nsplit
-    // in increasing c.  The summation order of a row therefore does not depend
-    // on T: a verify of S rows and S single-row decodes produce bit-identical
-    // outputs (chunks past a row's causal limit only add exact zeros).
-    const int nchunks = (T + TILE - 1) / TILE;
-    const int ntiles = split < nchunks ? (nchunks - split + nsplit - 1) / nsplit : 0;
-    const bf16* kbase = a.kcache + (size_t)kvh * a.max_pos * D;
-    const bf16* vbase = a.vcache + (size_t)kvh * a.max_pos * D;
-
-    // cached (old) rows of a chunk -> shared memory, asynchronously
-    auto load_tile = [&](int buf, int j0) {
-        const int nold = max(0, min(j0 + TILE, min(T, off)) - j0);
-        for (int idx = tid; idx < nold * 16; idx += 128) {
-            const int r = idx >> 4, c = idx & 15;
-            cp_async16(&sm.kt[buf][r][(c ^ (r & 15)) * 8], kbase + (size_t)(j0 + r) * D + c * 8);
-            cp_async16(&sm.vt[buf][r][c * 8], vbase + (size_t)(j0 + r) * D + c * 8);
-        }
-        cp_async_commit();
-    };
-    if (ntiles > 0) load_tile(0, split * TILE);
-    if (ntiles > 1) load_tile(1, (split + nsplit) * TILE);
-
-    // queries: q_norm + rope
-    for (int r = warp; r < R; r += 4) {
-        const int gi = r / S, i = r - gi * S;
-        const int h = kvh * G + gi, pos = off + i;
-        float o[4];
-        norm_rope_row(a.q + (size_t)i * a.ldq + h * D, a.q_norm_w, a.eps, a.rope_cos + (size_t)pos * HALF,
-                      a.rope_sin + (size_t)pos * HALF, lane, o);
-        sm.qs[r][2 * lane] = o[0];
-        sm.qs[r][2 * lane + 1] = o[1];
-        sm.qs[r][HALF + 2 * lane] = o[2];
-        sm.qs[r][HALF + 2 * lane + 1] = o[3];
-    }
-    // new keys / values of this CTA's chunks: cache write + local copy
-    for (int p = off + warp; p < T; p += 4) {
-        if ((p / TILE) % nsplit != split) continue;
-        const int i = p - off;
-        float o[4];
-        norm_rope_row(a.k + (size_t)i * a.ldk + kvh * D, a.k_norm_w, a.eps, a.rope_cos + (size_t)p * HALF,
-                      a.rope_sin + (size_t)p * HALF, lane, o);
-        const uint32_t k01 = pack_bf16x2(o[0], o[1]), k23 = pack_bf16x2(o[2], o[3]);
-        bf16* kd = a.kcache + ((size_t)kvh * a.max_pos + p) * D;
-        *reinterpret_cast<uint32_t*>(kd + 2 * lane) = k01;
-        *reinterpret_cast<uint32_t*>(kd + HALF + 2 * lane) = k23;
-        *reinterpret_cast<uint32_t*>(&sm.nk[i][2 * lane]) = k01;
-        *reinterpret_cast<uint32_t*>(&sm.nk[i][HALF + 2 * lane]) = k23;
-        const uint2 vv = *reinterpret_cast<const uint2*>(a.v + (size_t)i * a.ldv + kvh * D + 4 * lane);
-        *reinterpret_cast<uint2*>(a.vcache + ((size_t)kvh * a.max_pos + p) * D + 4 * lane) = vv;
-        *reinterpret_cast<uint2*>(&sm.nv[i][4 * lane]) = vv;
-    }
-    if (tid < RMAX) {
-        sm.mrow[tid] = -INFINITY;
-        sm.lrow[tid] = 0.f;
-    }
-    __syncthreads();
-
-    float o_acc[RMAX];
-#pragma unroll
-    for (int r = 0; r < RMAX; ++r) o_acc[r] = 0.f;
-    constexpr int RH = (RMAX + 1) / 2;
-
-    for (int it = 0; it < ntiles; ++it) {
-        const int buf = it & 1, j0 = (split + it * nsplit) * TILE;
-        const int hi = min(T, j0 + TILE);
-        if (it + 1 < ntiles)
-            cp_async_wait<1>();
-        else
-            cp_async_wait<0>();
-        // new positions of this tile come from the locally computed rows
-        for (int idx = tid; idx < TILE * 16; idx += 128) {
-            const int r = idx >> 4, c = idx & 15, j = j0 + r;
-            if (j >= off && j < hi) {
-                *reinterpret_cast<uint4*>(&sm.kt[buf][r][(c ^ (r & 15)) * 8]) =
-                    *reinterpret_cast<const uint4*>(&sm.nk[j - off][c * 8]);
-                *reinterpret_cast<uint4*>(&sm.vt[buf][r][c * 8]) = *reinterpret_cast<const uint4*>(&sm.nv[j - off][c * 8]);
-            }
-        }
-        __syncthreads();
-        // scores: thread -> key (tid & 63), rows of parity (tid >> 6)
-        {
-            const int jj = tid & (TILE - 1), par = tid >> 6;
-            const int j = j0 + jj;
-            float acc[RH];
-#pragma unroll
-            for (int q = 0; q < RH; ++q) acc[q] = 0.f;
-            if (j < hi) {
-#pragma unroll 4
-                for (int dc = 0; dc < D / 8; ++dc) {
-                    const uint4 u = *reinterpret_cast<const uint4*>(&sm.kt[buf][jj][(dc ^ (jj & 15)) * 8]);
-                    const float kf[8] = {bits_lo_f(u.x), bits_hi_f(u.x), bits_lo_f(u.y), bits_hi_f(u.y),
-                                         bits_lo_f(u.z), bits_hi_f(u.z), bits_lo_f(u.w), bits_hi_f(u.w)};
-#pragma unroll
-                    for (int q = 0; q < RH; ++q) {
-                        const int r = par + 2 * q;
-                        if (r < R) {
-                            const float4 q0 = *reinterpret_cast<const float4*>(&sm.qs[r][dc * 8]);
-                            const float4 q1 = *reinterpret_cast<const float4*>(&sm.qs[r][dc * 8 + 4]);
-                            float s = acc[q];
-                            s = fmaf(q0.x, kf[0], s); s = fmaf(q0.y, kf[1], s);
-                            s = fmaf(q0.z, kf[2], s); s = fmaf(q0.w, kf[3], s);
-                            s = fmaf(q1.x, kf[4], s); s = fmaf(q1.y, kf[5], s);
-                            s = fmaf(q1.z, kf[6], s); s = fmaf(q1.w, kf[7], s);
-                            acc[q] = s;
-                        }
-                    }
-                }
-            }
-#pragma unroll
-            for (int q = 0; q < RH; ++q) {
-                const int r = par + 2 * q;
-                if (r < R) {
-                    const int i = r % S;
-                    const bool ok = (j < hi) && (j <= off + i);
-                    sm.sc[r][jj] = ok ? acc[q] * a.scale : -INFINITY;
-                }
-            }
-        }
-        __syncthreads();
-        // online softmax update, one warp per row
-        for (int r = warp; r < R; r += 4) {
-            const float s0 = sm.sc[r][lane], s1 = sm.sc[r][lane + 32];
-            const float mx = warp_max(fmaxf(s0, s1));
-            const float mold = sm.mrow[r];
-            const float mnew = fmaxf(mold, mx);
-            float p0 = 0.f, p1 = 0.f, al = 1.f;
-            if (mnew != -INFINITY) {
-                p0 = expf(s0 - mnew);
-                p1 = expf(s1 - mnew);
-                al = expf(mold - mnew);
-            }
-            sm.sc[r][lane] = p0;
-            sm.sc[r][lane + 32] = p1;
-            const float ps = warp_sum(p0 + p1);
-            if (lane == 0) {
-                sm.lrow[r] = sm.lrow[r] * al + ps;
-                sm.mrow[r] = mnew;
-                sm.alph[r] = al;
-            }
-        }
-        __syncthreads();
-        // o[r][d] = o*alpha + sum_j p[r][j] v[j][d]; thread = dim
-        {
-            const int d = tid;
-#pragma unroll
-            for (int r = 0; r < RMAX; ++r)
-                if (r < R) o_acc[r] *= sm.alph[r];
-            const int nj = min(TILE, hi - j0);
-            for (int jj = 0; jj < nj; ++jj) {
-                const float vv = bf2f(sm.vt[buf][jj][d]);
-#pragma unroll
-                for (int r = 0; r < RMAX; ++r)
-                    if (r < R) o_acc[r] = fmaf(sm.sc[r][jj], vv, o_acc[r]);
-            }
-        }
-        __syncthreads();
-        if (it + 2 < ntiles) load_tile(buf, (split + (it + 2) * nsplit) * TILE);
-    }
-
-    // partial -> global
-    const size_t pbase = ((size_t)kvh * nsplit + split) * RMAX;
-#pragma unroll
-    for (int r = 0; r < RMAX; ++r)
-        if (r < R) a.part[(pbase + r) * (D + 2) + tid] = o_acc[r];
-    if (tid < R) {
-        a.part[(pbase + tid) * (D + 2) + D] = sm.mrow[tid];
-        a.part[(pbase + tid) * (D + 2) + D + 1] = sm.lrow[tid];
-    }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) sm.last = (atomicAdd(&a.counters[kvh], 1u) == (unsigned)(nsplit - 1));
-    __syncthreads();
-    if (!sm.last) return;
-    __threadfence();
-    // merge the splits (fixed order) and write bf16 output.  All split maxima
-    // and sums are gathered in one parallel pass; the tile buffers (no longer
-    // needed) hold them: nsplit * R <= 148 * 64 floats.
-    float* mb = reinterpret_cast<float*>(&sm.kt[0][0][0]);
-    float* lb = mb + nsplit * R;
-    for (int idx = tid; idx < nsplit * R; idx += 128) {
-        const int s2 = idx / R, r = idx - s2 * R;
-        const float* pp = a.part + (((size_t)kvh * nsplit + s2) * RMAX + r) * (D + 2);
-        mb[idx] = __ldcg(pp + D);
-        lb[idx] = __ldcg(pp + D + 1);
-    }
-    __syncthreads();
-    if (tid < R) {
-        // row tid: global max, then split weights e^(m_s - max) (in place of m_s)
-        float mm = -INFINITY;
-        for (int s2 = 0; s2 < nsplit; ++s2) mm = fmaxf(mm, mb[s2 * R + tid]);
-        float Lsum = 0.f;
-        for (int s2 = 0; s2 < nsplit; ++s2) {
-            const float ms = mb[s2 * R + tid];
-            const float f = ms == -INFINITY ? 0.f : expf(ms - mm);
-            mb[s2 * R + tid] = f;
-            Lsum = fmaf(lb[s2 * R + tid], f, Lsum);
-        }
-        sm.lrow[tid] = Lsum;
-    }
-    __syncthreads();
-    for (int r = 0; r < R; ++r) {
-        float O = 0.f;
-        for (int s0 = 0; s0 < nsplit; s0 += 8) {
-            float pv[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                pv[j] = (s0 + j < nsplit && mb[(s0 + j) * R + r] != 0.f)
-                            ? __ldcg(&a.part[(((size_t)kvh * nsplit + s0 + j) * RMAX + r) * (D + 2) + tid])
-                            : 0.f;
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                if (s0 + j < nsplit) O = fmaf(pv[j], mb[(s0 + j) * R + r], O);
-        }
-        const int gi = r / S, i = r - gi * S;
-        a.out[(size_t)i * a.ldo + (kvh * G + gi) * D + tid] = f2bf(O / sm.lrow[r]);
-    }
-    if (tid == 0) a.counters[kvh] = 0u;
+    attn_decode_body<RMAX>(a, sm, blockIdx.x, blockIdx.y, gridDim.y, threadIdx.x, CtaSync{});
 }
 
 // ---------------------------------------------------------------------------

@@ -87,6 +87,7 @@ int qw_model_load(const char* dir, int device, int tp_rank, int tp_size, qw_mode
         qw_model* m = qw::model_create(cfg, device, tp_rank, tp_size);
         try {
             qw::model_load_dir(m, dir);
+            qw::mk_prepare(m);
         } catch (...) {
             delete m;
             throw;
@@ -104,6 +105,7 @@ int qw_model_init_random(const char* config_json, uint64_t seed, int norm_mode, 
         qw_model* m = qw::model_create(cfg, device, tp_rank, tp_size);
         try {
             qw::model_init_random(m, seed, norm_mode);
+            qw::mk_prepare(m);
         } catch (...) {
             delete m;
             throw;

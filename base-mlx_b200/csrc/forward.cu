@@ -67,6 +67,8 @@ void forward_dev(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_m
     const bool decode = S <= 8;
     const bool tp = m->tp_size > 1;
     if (S > w.cap_rows) throw Error(QW_ERR_INFERENCE, "workspace too small for forward");
+    if (decode && !tp && mk_forward(m, c, d_ids, S, logits_mode, store_logits, d_argmax, st, ctl, next_tok, out, gate))
+        return;
 
     QW_CUDA(launch_embed(d_ids, S, m->embed.w, m->embed.s, m->embed.b, H, cf.vocab, w.x, m->d_err, st, true));
 

@@ -470,6 +470,7 @@ qw_model::~qw_model() {
     if (device >= 0) cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
     qw::tp_destroy(this);
+    qw::mk_free(this);
     qw::spec_state_free(spec_state);
     spec_state = nullptr;
     for (qw_cache* c : caches) delete c;

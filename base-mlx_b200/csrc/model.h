@@ -78,6 +78,7 @@ struct Workspace {
 };
 
 struct TpComm;  // tensor-parallel communicator (NCCL), defined in tp.cu
+struct MkState;  // persistent decode kernel: packed weights + sync words, defined in decode_mk.cu
 
 }  // namespace qw
 
@@ -106,6 +107,7 @@ struct qw_model {
     std::vector<qw_cache*> caches;  // live caches (freed with the model)
     qw_cache* gen_cache = nullptr;  // cache used by the generate entry points
     void* spec_state = nullptr;     // speculative-decoding graphs (spec.cu)
+    qw::MkState* mk = nullptr;      // persistent decode kernel state (decode_mk.cu)
     ~qw_model();
 };
 
@@ -136,6 +138,13 @@ void set_cache_len(qw_cache* c, int len);
 void check_device_err(qw_model* m);
 qw_cache* cache_create(qw_model* m, int max_pos);
 qw_cache* cache_for_generate(qw_model* m, int need_pos);
+
+// decode_mk.cu: persistent decode step (S <= 8 rows, one GPU)
+void mk_prepare(qw_model* m);
+void mk_free(qw_model* m);
+// false when the step does not fit the persistent kernel (the caller runs the kernel chain)
+bool mk_forward(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_mode, bool store_logits,
+                int* d_argmax, cudaStream_t st, StepCtl* ctl, int* next_tok, int* out, const int* gate);
 
 // forward.cu
 // logits_mode: 0 = none, 1 = last row, 2 = all rows
