@@ -60,9 +60,42 @@ struct DecSmem {
     int last;
 };
 
+// Cached (old) K/V rows [j0, min(j0 + 64, T, off)) of kv head kvh -> tile buffer
+// `buf`, asynchronously (one commit group).  Old rows do not depend on the
+// current step, so a caller may issue the first two tiles early (`preloaded`).
+template <int RMAX>
+QW_DEV void attn_load_tile(const AttnArgs& a, DecSmem<RMAX>& sm, int kvh, int buf, int j0, int T, int off, int tid) {
+    const bf16* kbase = a.kcache + (size_t)kvh * a.max_pos * D;
+    const bf16* vbase = a.vcache + (size_t)kvh * a.max_pos * D;
+    const int nold = max(0, min(j0 + TILE, min(T, off)) - j0);
+    for (int idx = tid; idx < nold * 16; idx += 128) {
+        const int r = idx >> 4, c = idx & 15;
+        cp_async16(&sm.kt[buf][r][(c ^ (r & 15)) * 8], kbase + (size_t)(j0 + r) * D + c * 8);
+        cp_async16(&sm.vt[buf][r][c * 8], vbase + (size_t)(j0 + r) * D + c * 8);
+    }
+    cp_async_commit();
+}
+
+// Tiles of this split CTA (chunks split, split + nsplit, ... of 64 keys).
+QW_DEV int attn_ntiles(int T, int split, int nsplit) {
+    const int nchunks = (T + TILE - 1) / TILE;
+    return split < nchunks ? (nchunks - split + nsplit - 1) / nsplit : 0;
+}
+
+// Issue the first two tile loads of attn_decode_body ahead of time (128 threads).
+template <int RMAX>
+QW_DEV void attn_decode_preload(const AttnArgs& a, DecSmem<RMAX>& sm, int kvh, int split, int nsplit, int tid) {
+    const int off = *a.seq_len;
+    const int T = off + a.S;
+    if (T > a.max_pos) return;
+    const int ntiles = attn_ntiles(T, split, nsplit);
+    if (ntiles > 0) attn_load_tile<RMAX>(a, sm, kvh, 0, split * TILE, T, off, tid);
+    if (ntiles > 1) attn_load_tile<RMAX>(a, sm, kvh, 1, (split + nsplit) * TILE, T, off, tid);
+}
+
 template <int RMAX, typename Sync>
 QW_DEV void attn_decode_body(const AttnArgs& a, DecSmem<RMAX>& sm, const int kvh, const int split, const int nsplit,
-                             const int tid, Sync sync) {
+                             const int tid, Sync sync, bool preloaded = false) {
     const int lane = tid & 31, warp = tid >> 5;
     const int S = a.S, G = a.Hq / a.Hkv, R = G * S;
     const int off = *a.seq_len;
@@ -75,23 +108,12 @@ QW_DEV void attn_decode_body(const AttnArgs& a, DecSmem<RMAX>& sm, const int kvh
     // in increasing c.  The summation order of a row therefore does not depend
     // on T: a verify of S rows and S single-row decodes produce bit-identical
     // outputs (chunks past a row's causal limit only add exact zeros).
-    const int nchunks = (T + TILE - 1) / TILE;
-    const int ntiles = split < nchunks ? (nchunks - split + nsplit - 1) / nsplit : 0;
-    const bf16* kbase = a.kcache + (size_t)kvh * a.max_pos * D;
-    const bf16* vbase = a.vcache + (size_t)kvh * a.max_pos * D;
-
-    // cached (old) rows of a chunk -> shared memory, asynchronously
-    auto load_tile = [&](int buf, int j0) {
-        const int nold = max(0, min(j0 + TILE, min(T, off)) - j0);
-        for (int idx = tid; idx < nold * 16; idx += 128) {
-            const int r = idx >> 4, c = idx & 15;
-            cp_async16(&sm.kt[buf][r][(c ^ (r & 15)) * 8], kbase + (size_t)(j0 + r) * D + c * 8);
-            cp_async16(&sm.vt[buf][r][c * 8], vbase + (size_t)(j0 + r) * D + c * 8);
-        }
-        cp_async_commit();
-    };
-    if (ntiles > 0) load_tile(0, split * TILE);
-    if (ntiles > 1) load_tile(1, (split + nsplit) * TILE);
+    const int ntiles = attn_ntiles(T, split, nsplit);
+    auto load_tile = [&](int buf, int j0) { attn_load_tile<RMAX>(a, sm, kvh, buf, j0, T, off, tid); };
+    if (!preloaded) {
+        if (ntiles > 0) load_tile(0, split * TILE);
+        if (ntiles > 1) load_tile(1, (split + nsplit) * TILE);
+    }
 
     // queries: q_norm + rope
     for (int r = warp; r < R; r += 4) {

@@ -100,6 +100,7 @@ struct MkArgs {
 };
 
 struct MkMisc {
+    int wft[MK_NW];  // first tile (CTA-local) of each warp's range in the current phase
     float rnorm[8];
     float ssq[MK_NW][8];
     unsigned long long amax[8];
@@ -258,9 +259,109 @@ QW_DEV void load16(const MkArgs& a, const StageSrc& s, int m, int k, float (&v)[
     }
 }
 
-QW_DEV void stage_acts(const MkArgs& a, const StageSrc& s, int K, int Mx, uint32_t* xs, float* seeds, MkMisc& mm) {
+// Convert one unit (16 values of column m, k-step j of group gl) into its
+// fragment words and return the sum of the converted values.
+QW_DEV float stage_unit(const float (&v)[16], int gl, int m, int j, int Mx, uint32_t* xs) {
+    float sum = 0.f;
+    uint32_t h[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const __half2 hh = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+        const float2 back = __half22float2(hh);
+        sum += back.x + back.y;
+        h[i] = *reinterpret_cast<const uint32_t*>(&hh);
+    }
+    uint32_t* blk = xs + (size_t)(gl * Mx + m) * XW;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        blk[t * 8 + 2 * j] = h[t];          // (x[16j+2t], x[16j+2t+1])
+        blk[t * 8 + 2 * j + 1] = h[t + 4];  // (x[16j+2t+8], x[16j+2t+9])
+    }
+    return sum;
+}
+
+// j-quads share (gl, m): lo = steps 0+2, hi = steps 1+3 (every lane of the warp
+// takes part in the shuffles).
+QW_DEV void stage_seeds(float sum, bool valid, int gl, int m, int j, float* seeds) {
+    const float pair = sum + __shfl_xor_sync(0xffffffffu, sum, 2);
+    const float tot = pair + __shfl_xor_sync(0xffffffffu, pair, 1);
+    if (valid && j < 2) {
+        float* e = seeds + (size_t)(gl * 4 + (m >> 1)) * SEEDF;
+        e[2 * j + (m & 1)] = -1024.f * pair;  // j = 0: lo, j = 1: hi
+        if (j == 0) e[4 + (m & 1)] = tot;
+    }
+}
+
+QW_DEV void apply_norm(const StageSrc& s, float r, int k, float (&v)[16]) {
+    const uint4* wp = reinterpret_cast<const uint4*>(s.norm + k);
+    const uint4 w0 = wp[0], w1 = wp[1];
+    const uint32_t W[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        v[2 * i] = bfr(__fmul_rn(__fmul_rn(v[2 * i], r), bits_lo_f(W[i])));
+        v[2 * i + 1] = bfr(__fmul_rn(__fmul_rn(v[2 * i + 1], r), bits_hi_f(W[i])));
+    }
+}
+
+// Unit u -> (group, column, k-step); units are ordered (gl, m, j).
+QW_DEV void unit_coords(int u, int Mx, int& gl, int& m, int& j) {
+    j = u & 3;
+    const int gm = u >> 2;
+    gl = gm / Mx;
+    m = gm - gl * Mx;
+}
+
+QW_DEV void stage_acts(const MkArgs& a, const StageSrc& s, int K, int Mx, uint32_t* xs, float* seeds, float* sq,
+                       MkMisc& mm) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int KG = K / 64;
+    const int units = KG * Mx * 4;
+    if (s.norm && units <= 2 * MK_NT) {
+        // RMSNorm in one pass over x: each thread keeps its (at most two) units
+        // in registers while the per-row sums of squares are reduced
+        float v0[16], v1[16];
+        int gl0 = 0, m0 = 0, j0 = 0, gl1 = 0, m1 = 0, j1 = 0;
+        const int u0 = tid, u1 = tid + MK_NT;
+        if (u0 < units) {
+            unit_coords(u0, Mx, gl0, m0, j0);
+            load16(a, s, m0, gl0 * 64 + 16 * j0, v0);
+            float q = 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) q = fmaf(v0[i], v0[i], q);
+            sq[u0] = q;
+        }
+        if (u1 < units) {
+            unit_coords(u1, Mx, gl1, m1, j1);
+            load16(a, s, m1, gl1 * 64 + 16 * j1, v1);
+            float q = 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) q = fmaf(v1[i], v1[i], q);
+            sq[u1] = q;
+        }
+        __syncthreads();
+        if (warp < Mx) {
+            // row `warp`: its KG*4 units, lane-strided, then a fixed shuffle tree
+            float q = 0.f;
+            for (int i = lane; i < KG * 4; i += 32) q += sq[((i >> 2) * Mx + warp) * 4 + (i & 3)];
+            q = warp_sum(q);
+            if (lane == 0) mm.rnorm[warp] = 1.0f / sqrtf(q / (float)K + a.eps);
+        }
+        __syncthreads();
+        float sum0 = 0.f, sum1 = 0.f;
+        if (u0 < units) {
+            apply_norm(s, mm.rnorm[m0], gl0 * 64 + 16 * j0, v0);
+            sum0 = stage_unit(v0, gl0, m0, j0, Mx, xs);
+        }
+        stage_seeds(sum0, u0 < units, gl0, m0, j0, seeds);
+        if (u1 - lane < units) {  // warp-uniform: some lane of this warp has a unit
+            if (u1 < units) {
+                apply_norm(s, mm.rnorm[m1], gl1 * 64 + 16 * j1, v1);
+                sum1 = stage_unit(v1, gl1, m1, j1, Mx, xs);
+            }
+            stage_seeds(sum1, u1 < units, gl1, m1, j1, seeds);
+        }
+        return;
+    }
     if (s.norm) {
         // RMSNorm statistics: fp32 sum of squares per row
         float ss[8];
@@ -292,53 +393,19 @@ QW_DEV void stage_acts(const MkArgs& a, const StageSrc& s, int K, int Mx, uint32
         }
         __syncthreads();
     }
-    const int units = KG * Mx * 4;
-    for (int u0 = 0; u0 < units; u0 += MK_NT) {
-        const int u = u0 + tid;
+    for (int ub = 0; ub < units; ub += MK_NT) {
+        const int u = ub + tid;
         float sum = 0.f;
         int gl = 0, m = 0, j = 0;
         if (u < units) {
-            j = u & 3;
-            const int gm = u >> 2;
-            gl = gm / Mx;
-            m = gm - gl * Mx;
+            unit_coords(u, Mx, gl, m, j);
             const int k = gl * 64 + 16 * j;
             float v[16];
             load16(a, s, m, k, v);
-            if (s.norm) {
-                const float r = mm.rnorm[m];
-                const uint4* wp = reinterpret_cast<const uint4*>(s.norm + k);
-                const uint4 w0 = wp[0], w1 = wp[1];
-                const uint32_t W[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    v[2 * i] = bfr(__fmul_rn(__fmul_rn(v[2 * i], r), bits_lo_f(W[i])));
-                    v[2 * i + 1] = bfr(__fmul_rn(__fmul_rn(v[2 * i + 1], r), bits_hi_f(W[i])));
-                }
-            }
-            uint32_t h[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const __half2 hh = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-                const float2 back = __half22float2(hh);
-                sum += back.x + back.y;
-                h[i] = *reinterpret_cast<const uint32_t*>(&hh);
-            }
-            uint32_t* blk = xs + (size_t)(gl * Mx + m) * XW;
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                blk[t * 8 + 2 * j] = h[t];          // (x[16j+2t], x[16j+2t+1])
-                blk[t * 8 + 2 * j + 1] = h[t + 4];  // (x[16j+2t+8], x[16j+2t+9])
-            }
+            if (s.norm) apply_norm(s, mm.rnorm[m], k, v);
+            sum = stage_unit(v, gl, m, j, Mx, xs);
         }
-        // j-quads share (gl, m): lo = steps 0+2, hi = steps 1+3
-        const float pair = sum + __shfl_xor_sync(0xffffffffu, sum, 2);
-        const float tot = pair + __shfl_xor_sync(0xffffffffu, pair, 1);
-        if (u < units && j < 2) {
-            float* e = seeds + (size_t)(gl * 4 + (m >> 1)) * SEEDF;
-            e[2 * j + (m & 1)] = -1024.f * pair;  // j = 0: lo, j = 1: hi
-            if (j == 0) e[4 + (m & 1)] = tot;
-        }
+        stage_seeds(sum, u < units, gl, m, j, seeds);
     }
 }
 
@@ -473,6 +540,7 @@ QW_DEV void gemv_phase(const MkArgs& a, const PhaseInfo& P, int Mx, uint32_t* xs
 
     int wa, wb;
     warp_range(P, warp, wa, wb);
+    if (lane == 0) mm.wft[warp] = (wa - P.tg0) / KG;
     int seg = 0;
     for (int tg = wa; tg < wb; ++seg) {
         // one tile segment: tile-groups [tg, se) of tile `tile`
@@ -547,15 +615,17 @@ QW_DEV void gemv_phase(const MkArgs& a, const PhaseInfo& P, int Mx, uint32_t* xs
     const int tfirst = P.tg0 / KG, tlast = (P.tg1 - 1) / KG;
     const int ntl = P.tg1 > P.tg0 ? tlast - tfirst + 1 : 0;
     // CTA partial of tile (tfirst + tl), element (sub, lane slot ln, e): warps in order
+    const int tg0 = P.tg0, nrange = P.tg1 - P.tg0;
     auto cta_part = [&](int tl, int sub, int ln, int e) {
-        const int tile = tfirst + tl;
+        const int lo = (tfirst + tl) * KG - tg0, hi = lo + KG;  // tile's tile-groups, CTA-relative
         float v = 0.f;
+#pragma unroll
         for (int w = 0; w < MK_NW; ++w) {
-            int xa, xb;
-            warp_range(P, w, xa, xb);
-            if (xa >= xb || xa >= (tile + 1) * KG || xb <= tile * KG) continue;
-            const int sg = tile - xa / KG;
-            v += red[((size_t)(w * seg_stride + sg) * R16 + sub) * 32 * 4 + ln * 4 + e];
+            const int xa = (w * nrange) >> 4, xb = ((w + 1) * nrange) >> 4;
+            if (xa < xb && xa < hi && xb > lo) {
+                const int sg = (tfirst + tl) - (tfirst + mm.wft[w]);
+                v += red[((size_t)(w * seg_stride + sg) * R16 + sub) * 32 * 4 + ln * 4 + e];
+            }
         }
         return v;
     };
@@ -686,7 +756,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
             if (l > 0) ok = cta_wait(a, arrivals * C, mm);
             if (!ok) break;
             StageSrc s{l == 0 ? nullptr : a.x, a.H, 0, Ly.in_norm};
-            stage_acts(a, s, a.H, M, xs, seeds, mm);
+            stage_acts(a, s, a.H, M, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
             if (l == 0 && blockIdx.x == 0) {
                 // the residual stream starts as the embedding rows
                 for (int u = tid; u < M * (a.H / 16); u += MK_NT) {
@@ -704,6 +774,16 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
             }
             __syncthreads();
             gemv_phase<K_QKV, DEPTH>(a, tab[4 * l + K_QKV], M, xs, seeds, red, pc, slot, ring, false, mm);
+            // the attention tiles' cached K/V rows do not depend on this step:
+            // start loading them before waiting for the other CTAs' q|k|v
+            __syncthreads();
+            if (warp < 4 && (int)blockIdx.x < a.aa.Hkv * a.aa.nsplit) {
+                AttnArgs aa = a.aa;
+                aa.kcache = a.kc0 + (size_t)l * a.kv_layer_elems;
+                aa.vcache = a.vc0 + (size_t)l * a.kv_layer_elems;
+                attn::attn_decode_preload<RMAX>(aa, *reinterpret_cast<attn::DecSmem<RMAX>*>(uni),
+                                                blockIdx.x / a.aa.nsplit, blockIdx.x % a.aa.nsplit, a.aa.nsplit, tid);
+            }
             cta_arrive(a);
             ++arrivals;
         }
@@ -719,7 +799,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
                 aa.vcache = a.vc0 + (size_t)l * a.kv_layer_elems;
                 attn::DecSmem<RMAX>& asm_ = *reinterpret_cast<attn::DecSmem<RMAX>*>(uni);
                 attn::attn_decode_body<RMAX>(aa, asm_, blockIdx.x / a.aa.nsplit, blockIdx.x % a.aa.nsplit,
-                                             a.aa.nsplit, tid, NamedSync128{});
+                                             a.aa.nsplit, tid, NamedSync128{}, true);
             }
             cta_arrive(a);
             ++arrivals;
@@ -733,7 +813,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
             ok = cta_wait(a, arrivals * C, mm);
             if (!ok) break;
             StageSrc s{a.attn, a.QD, 0, nullptr};
-            stage_acts(a, s, a.QD, M, xs, seeds, mm);
+            stage_acts(a, s, a.QD, M, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
             __syncthreads();
             gemv_phase<K_O, DEPTH>(a, tab[4 * l + K_O], M, xs, seeds, red, pc, slot, ring, false, mm);
             cta_arrive(a);
@@ -748,7 +828,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
             ok = cta_wait(a, arrivals * C, mm);
             if (!ok) break;
             StageSrc s{a.x, a.H, 0, Ly.post_norm};
-            stage_acts(a, s, a.H, M, xs, seeds, mm);
+            stage_acts(a, s, a.H, M, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
             __syncthreads();
             gemv_phase<K_GU, DEPTH>(a, tab[4 * l + K_GU], M, xs, seeds, red, pc, slot, ring, false, mm);
             cta_arrive(a);
@@ -763,7 +843,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
             ok = cta_wait(a, arrivals * C, mm);
             if (!ok) break;
             StageSrc s{a.mlp, a.I, 0, nullptr};
-            stage_acts(a, s, a.I, M, xs, seeds, mm);
+            stage_acts(a, s, a.I, M, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
             __syncthreads();
             gemv_phase<K_DOWN, DEPTH>(a, tab[4 * l + K_DOWN], M, xs, seeds, red, pc, slot, ring, false, mm);
             cta_arrive(a);
@@ -780,7 +860,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
         ok = cta_wait(a, arrivals * C, mm);
         if (ok) {
             StageSrc s{a.x, a.H, M - rows, a.final_norm};
-            stage_acts(a, s, a.H, rows, xs, seeds, mm);
+            stage_acts(a, s, a.H, rows, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
             __syncthreads();
             gemv_phase<K_O, DEPTH>(a, tab[4 * a.L], rows, xs, seeds, red, pc, slot, ring, true, mm);
         }
@@ -1039,12 +1119,13 @@ namespace {
 template <int RMAX>
 size_t mk_union_bytes(const MkState* s, int M, int rows, int C) {
     size_t u = sizeof(attn::DecSmem<RMAX>);
-    auto need = [&](const MkLin& lin, int Mx) {
+    // staged x', seeds, per-warp partials and (RMSNorm phases) per-unit sums of squares
+    auto need = [&](const MkLin& lin, int Mx, bool norm) {
         return (size_t)lin.KG * Mx * XW * 4 + (size_t)lin.KG * 4 * SEEDF * 4 +
-               (size_t)MK_NW * lin.seg_stride * lin.R16 * 512;
+               (size_t)MK_NW * lin.seg_stride * lin.R16 * 512 + (norm ? (size_t)lin.KG * Mx * 4 * 4 : 0);
     };
-    for (int k = 0; k < 4; ++k) u = std::max(u, need(s->layers[0].lin[k], M));
-    if (rows > 0) u = std::max(u, need(s->lm, rows));
+    for (int k = 0; k < 4; ++k) u = std::max(u, need(s->layers[0].lin[k], M, k == K_QKV || k == K_GU));
+    if (rows > 0) u = std::max(u, need(s->lm, rows, true));
     return (u + 127) & ~(size_t)127;
 }
 
