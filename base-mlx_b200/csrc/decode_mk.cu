@@ -428,6 +428,7 @@ QW_DEV bool cta_wait(const MkArgs& a, unsigned target, MkMisc& mm) {
                 }
             }
         }
+        __threadfence();
     }
     __syncthreads();
     return !*reinterpret_cast<volatile int*>(&mm.bad);
@@ -696,7 +697,10 @@ QW_DEV void gemv_phase(const MkArgs& a, const PhaseInfo& P, int Mx, uint32_t* xs
             }
         }
         __syncthreads();
-        if (tid < Mx) a.amax_cta[(size_t)blockIdx.x * 8 + tid] = mm.amax[tid];
+        if (tid < Mx) {
+            a.amax_cta[(size_t)blockIdx.x * 8 + tid] = mm.amax[tid];
+            __threadfence();  // each writer publishes before the final arrival
+        }
     }
 }
 
