@@ -51,6 +51,7 @@ QW_DEV void norm_rope_row(const bf16* row, const bf16* nw, float eps, const floa
 // ---------------------------------------------------------------------------
 template <int RMAX>
 struct DecSmem {
+    uint64_t tbar[2];  // tile buffer b: completes when all 128 threads' copies of a tile have landed
     float qs[RMAX][D];
     float sc[RMAX][TILE];
     float mrow[RMAX], lrow[RMAX], alph[RMAX];
@@ -63,6 +64,9 @@ struct DecSmem {
 // Cached (old) K/V rows [j0, min(j0 + 64, T, off)) of kv head kvh -> tile buffer
 // `buf`, asynchronously (one commit group).  Old rows do not depend on the
 // current step, so a caller may issue the first two tiles early (`preloaded`).
+// Completion is tracked on the buffer's mbarrier (cp.async.mbarrier.arrive.noinc
+// from each of the 128 threads), not on the threads' cp.async groups, so a
+// caller whose threads have other copies in flight does not wait for them.
 template <int RMAX>
 QW_DEV void attn_load_tile(const AttnArgs& a, DecSmem<RMAX>& sm, int kvh, int buf, int j0, int T, int off, int tid) {
     const bf16* kbase = a.kcache + (size_t)kvh * a.max_pos * D;
@@ -73,7 +77,17 @@ QW_DEV void attn_load_tile(const AttnArgs& a, DecSmem<RMAX>& sm, int kvh, int bu
         cp_async16(&sm.kt[buf][r][(c ^ (r & 15)) * 8], kbase + (size_t)(j0 + r) * D + c * 8);
         cp_async16(&sm.vt[buf][r][c * 8], vbase + (size_t)(j0 + r) * D + c * 8);
     }
-    cp_async_commit();
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&sm.tbar[buf])) : "memory");
+}
+
+// (Re)initialise the two tile barriers (128 arrivals each); callers sync after.
+template <int RMAX>
+QW_DEV void attn_init_bars(DecSmem<RMAX>& sm, int tid) {
+    if (tid == 0) {
+        mbar_init(&sm.tbar[0], 128);
+        mbar_init(&sm.tbar[1], 128);
+        fence_mbar_init();
+    }
 }
 
 // Tiles of this split CTA (chunks split, split + nsplit, ... of 64 keys).
@@ -83,8 +97,11 @@ QW_DEV int attn_ntiles(int T, int split, int nsplit) {
 }
 
 // Issue the first two tile loads of attn_decode_body ahead of time (128 threads).
-template <int RMAX>
-QW_DEV void attn_decode_preload(const AttnArgs& a, DecSmem<RMAX>& sm, int kvh, int split, int nsplit, int tid) {
+template <int RMAX, typename Sync>
+QW_DEV void attn_decode_preload(const AttnArgs& a, DecSmem<RMAX>& sm, int kvh, int split, int nsplit, int tid,
+                                Sync sync) {
+    attn_init_bars(sm, tid);
+    sync();
     const int off = *a.seq_len;
     const int T = off + a.S;
     if (T > a.max_pos) return;
@@ -111,6 +128,8 @@ QW_DEV void attn_decode_body(const AttnArgs& a, DecSmem<RMAX>& sm, const int kvh
     const int ntiles = attn_ntiles(T, split, nsplit);
     auto load_tile = [&](int buf, int j0) { attn_load_tile<RMAX>(a, sm, kvh, buf, j0, T, off, tid); };
     if (!preloaded) {
+        attn_init_bars(sm, tid);
+        sync();
         if (ntiles > 0) load_tile(0, split * TILE);
         if (ntiles > 1) load_tile(1, (split + nsplit) * TILE);
     }
@@ -158,10 +177,7 @@ QW_DEV void attn_decode_body(const AttnArgs& a, DecSmem<RMAX>& sm, const int kvh
     for (int it = 0; it < ntiles; ++it) {
         const int buf = it & 1, j0 = (split + it * nsplit) * TILE;
         const int hi = min(T, j0 + TILE);
-        if (it + 1 < ntiles)
-            cp_async_wait<1>();
-        else
-            cp_async_wait<0>();
+        if (!mbar_wait_bounded(&sm.tbar[buf], (it >> 1) & 1) && tid == 0) atomicOr(a.err, QW_DERR_TIMEOUT);
         // new positions of this tile come from the locally computed rows
         for (int idx = tid; idx < TILE * 16; idx += 128) {
             const int r = idx >> 4, c = idx & 15, j = j0 + r;
@@ -261,18 +277,19 @@ QW_DEV void attn_decode_body(const AttnArgs& a, DecSmem<RMAX>& sm, const int kvh
         a.part[(pbase + tid) * (D + 2) + D] = sm.mrow[tid];
         a.part[(pbase + tid) * (D + 2) + D + 1] = sm.lrow[tid];
     }
-    __threadfence();
     sync();
-    if (tid == 0) sm.last = (atomicAdd(&a.counters[kvh], 1u) == (unsigned)(nsplit - 1));
+    if (tid == 0) sm.last = (atom_add_acq_rel(&a.counters[kvh], 1u) == (unsigned)(nsplit - 1));
     sync();
     if (!sm.last) return;
-    __threadfence();
     // merge the splits (fixed order) and write bf16 output.  All split maxima
     // and sums are gathered in one parallel pass; the tile buffers (no longer
     // needed) hold them: nsplit * R <= 148 * 64 floats.
+    // Only splits that own a chunk have data (chunk c -> split c % nsplit);
+    // the others would add exact zeros, so skipping them changes no bit.
+    const int nact = min(nsplit, (T + TILE - 1) / TILE);
     float* mb = reinterpret_cast<float*>(&sm.kt[0][0][0]);
     float* lb = mb + nsplit * R;
-    for (int idx = tid; idx < nsplit * R; idx += 128) {
+    for (int idx = tid; idx < nact * R; idx += 128) {
         const int s2 = idx / R, r = idx - s2 * R;
         const float* pp = a.part + (((size_t)kvh * nsplit + s2) * RMAX + r) * (D + 2);
         mb[idx] = __ldcg(pp + D);
@@ -282,9 +299,9 @@ QW_DEV void attn_decode_body(const AttnArgs& a, DecSmem<RMAX>& sm, const int kvh
     if (tid < R) {
         // row tid: global max, then split weights e^(m_s - max) (in place of m_s)
         float mm = -INFINITY;
-        for (int s2 = 0; s2 < nsplit; ++s2) mm = fmaxf(mm, mb[s2 * R + tid]);
+        for (int s2 = 0; s2 < nact; ++s2) mm = fmaxf(mm, mb[s2 * R + tid]);
         float Lsum = 0.f;
-        for (int s2 = 0; s2 < nsplit; ++s2) {
+        for (int s2 = 0; s2 < nact; ++s2) {
             const float ms = mb[s2 * R + tid];
             const float f = ms == -INFINITY ? 0.f : expf(ms - mm);
             mb[s2 * R + tid] = f;
@@ -293,18 +310,19 @@ QW_DEV void attn_decode_body(const AttnArgs& a, DecSmem<RMAX>& sm, const int kvh
         sm.lrow[tid] = Lsum;
     }
     sync();
+    // thread = dim; per row, up to 16 splits' partials are loaded together
     for (int r = 0; r < R; ++r) {
         float O = 0.f;
-        for (int s0 = 0; s0 < nsplit; s0 += 8) {
-            float pv[8];
+        for (int s0 = 0; s0 < nact; s0 += 16) {
+            float pv[16];
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-                pv[j] = (s0 + j < nsplit && mb[(s0 + j) * R + r] != 0.f)
+            for (int j = 0; j < 16; ++j)
+                pv[j] = (s0 + j < nact && mb[(s0 + j) * R + r] != 0.f)
                             ? __ldcg(&a.part[(((size_t)kvh * nsplit + s0 + j) * RMAX + r) * (D + 2) + tid])
                             : 0.f;
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-                if (s0 + j < nsplit) O = fmaf(pv[j], mb[(s0 + j) * R + r], O);
+            for (int j = 0; j < 16; ++j)
+                if (s0 + j < nact) O = fmaf(pv[j], mb[(s0 + j) * R + r], O);
         }
         const int gi = r / S, i = r - gi * S;
         a.out[(size_t)i * a.ldo + (kvh * G + gi) * D + tid] = f2bf(O / sm.lrow[r]);

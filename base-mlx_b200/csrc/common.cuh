@@ -126,6 +126,18 @@ QW_DEV float warp_max(float v) {
     return v;
 }
 
+// ---- inter-CTA publication ------------------------------------------------
+// atom.add with acquire-release semantics at GPU scope.  Called by one thread
+// after a block barrier, it publishes the whole block's earlier writes (the
+// barrier orders them before the release, and release is cumulative) and,
+// for the CTA that sees the final count, orders the block's later reads
+// (after another block barrier) after every earlier publisher's writes.
+QW_DEV unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 // ---- shared-memory staging: bulk copies (TMA engine) + mbarriers --------
 QW_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 

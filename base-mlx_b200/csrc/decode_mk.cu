@@ -428,17 +428,15 @@ QW_DEV bool cta_wait(const MkArgs& a, unsigned target, MkMisc& mm) {
                 }
             }
         }
-        __threadfence();
     }
-    __syncthreads();
+    __syncthreads();  // the acquire above, then this barrier, orders every thread's reads
     return !*reinterpret_cast<volatile int*>(&mm.bad);
 }
+// Block barrier, then one release-add: publishes every thread's earlier writes
+// (the barrier orders them before the release, which is cumulative).
 QW_DEV void cta_arrive(const MkArgs& a) {
     __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        red_release_add(a.sync, 1u);
-    }
+    if (threadIdx.x == 0) red_release_add(a.sync, 1u);
 }
 
 // Attention uses warps 0-3 (128 threads) with a named barrier.
@@ -659,16 +657,14 @@ QW_DEV void gemv_phase(const MkArgs& a, const PhaseInfo& P, int Mx, uint32_t* xs
             const int sub = i >> 7, ln = (i >> 2) & 31, e = i & 3;
             slotp[i] = cta_part(tl, sub, ln, e);
         }
-        __threadfence();
         __syncthreads();
         // CTAs with a non-empty share of this tile (empty ranges exist when N < C)
         const int cf = cta_of(tile * KG, P.N, C), cl = cta_of((tile + 1) * KG - 1, P.N, C);
         int ncov = 0;
         for (int cc = cf; cc <= cl; ++cc) ncov += range_lo(cc, P.N, C) < range_lo(cc + 1, P.N, C);
-        if (tid == 0) mm.last = atomicAdd(&a.tile_ctr[tile], 1u) == (unsigned)(ncov - 1);
+        if (tid == 0) mm.last = atom_add_acq_rel(&a.tile_ctr[tile], 1u) == (unsigned)(ncov - 1);
         __syncthreads();
         if (mm.last) {
-            __threadfence();
             for (int o = tid; o < 16 * Mx; o += MK_NT) {
                 const int m = o % Mx, r = o / Mx;
                 const int ln = 4 * (r & 7) + (m >> 1), e = 2 * (r >> 3) + (m & 1);
@@ -697,10 +693,7 @@ QW_DEV void gemv_phase(const MkArgs& a, const PhaseInfo& P, int Mx, uint32_t* xs
             }
         }
         __syncthreads();
-        if (tid < Mx) {
-            a.amax_cta[(size_t)blockIdx.x * 8 + tid] = mm.amax[tid];
-            __threadfence();  // each writer publishes before the final arrival
-        }
+        if (tid < Mx) a.amax_cta[(size_t)blockIdx.x * 8 + tid] = mm.amax[tid];
     }
 }
 
@@ -786,7 +779,8 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
                 aa.kcache = a.kc0 + (size_t)l * a.kv_layer_elems;
                 aa.vcache = a.vc0 + (size_t)l * a.kv_layer_elems;
                 attn::attn_decode_preload<RMAX>(aa, *reinterpret_cast<attn::DecSmem<RMAX>*>(uni),
-                                                blockIdx.x / a.aa.nsplit, blockIdx.x % a.aa.nsplit, a.aa.nsplit, tid);
+                                                blockIdx.x / a.aa.nsplit, blockIdx.x % a.aa.nsplit, a.aa.nsplit, tid,
+                                                NamedSync128{});
             }
             cta_arrive(a);
             ++arrivals;
@@ -874,13 +868,9 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
     __syncthreads();
 
     // ---- last CTA: argmax over CTAs, step bookkeeping, counter reset
-    if (tid == 0) {
-        __threadfence();
-        mm.last = atomicAdd(a.sync + 1, 1u) == (unsigned)(C - 1);
-    }
+    if (tid == 0) mm.last = atom_add_acq_rel(a.sync + 1, 1u) == (unsigned)(C - 1);
     __syncthreads();
     if (!mm.last) return;
-    __threadfence();
     const bool aborted = *reinterpret_cast<volatile unsigned*>(a.sync + 2) != 0;
     if (!aborted && a.logits_rows > 0 && warp == 0) {
         for (int m = 0; m < a.logits_rows; ++m) {
@@ -919,8 +909,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
             for (int h = 0; h < a.aa.Hkv; ++h) a.aa.counters[h] = 0u;
         a.sync[0] = 0u;
         a.sync[1] = 0u;
-        a.sync[2] = 0u;
-        __threadfence();
+        a.sync[2] = 0u;  // visible to the next launch at kernel completion
     }
 }
 
