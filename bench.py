@@ -43,6 +43,9 @@ sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "base-mlx_b200"))
 
 PROMPT_LEN, DECODE_TOKENS, KV_PREALLOC, SEED = 512, 300, 4096, 1234
+# DRAM bytes read per launch / algorithmic bytes of decode_step_kernel, from an ncu capture
+# (profiles/decode_step_kernel_traffic.md)
+TRAFFIC_RATIO = 1.0010
 
 # Workload shapes (config.json contents of the random-init models)
 CFG_0_6B = dict(
@@ -240,11 +243,13 @@ def qgemv_roofline(q, torch, info, peak_gbs):
 
 
 def launches_per_generation(info, prompt_len, decode_tokens):
-    """Kernels the library launches for one greedy generation (for gpu_launches)."""
+    """Kernels the library launches for one greedy generation (for gpu_launches):
+    the prefill runs the kernel chain (embed; per layer 2 rmsnorm, 4 qgemm,
+    q/k-norm+RoPE+KV write, attention; lm_head, argmax finalize, step), every
+    decode step is one launch of the persistent decode kernel."""
     L = info.num_layers
-    prefill = 1 + 8 * L + 3   # embed; per layer 2 rmsnorm, 4 qgemm, qk-norm/rope/kv, attention; lm_head, finalize, step
-    decode = 1 + 5 * L + 3    # embed; per layer 4 qgemv + attention; lm_head, finalize, step
-    return prefill + (decode_tokens - 1) * decode
+    prefill = 1 + 8 * L + 3
+    return prefill + (decode_tokens - 1)
 
 
 def run_ours(args):
@@ -323,14 +328,21 @@ def run_ours(args):
         mean_T = PROMPT_LEN + DECODE_TOKENS / 2
         kv_bytes = L * 2 * KD * 2 * mean_T
         step_s = decode_ms / 1e3 / max(dec_tokens, 1)
-        extra["step_roofline"] = {"bound": "hbm", "achieved": round((w_bytes + kv_bytes) / step_s / 1e9, 1),
-                                  "peak": peak, "unit": "GB/s",
-                                  "frac": round((w_bytes + kv_bytes) / step_s / 1e9 / peak, 4),
-                                  "bytes_per_token": int(w_bytes + kv_bytes),
-                                  "note": "whole decode step (weights + KV at mean position 662) / device time"}
-        roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
-                "traffic": None, "kernel": "qgemv (decode quantized GEMV), M=1, 4B layer shapes + lm_head",
-                "bytes_per_launch": int(per_launch), "launches_timed": nl, "peak_source": peak_kind}
+        # the dominant kernel: one decode_step_kernel launch per token (CUDA events
+        # around the decode loop, inside the library)
+        step_gbs = (w_bytes + kv_bytes) / step_s / 1e9
+        roof = {"bound": "hbm", "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(step_gbs / peak, 4), "traffic": int(TRAFFIC_RATIO * (w_bytes + kv_bytes)),
+                "traffic_source": "ncu dram__bytes_read+write on the Qwen3-0.6B step, read/algorithmic ratio "
+                                  "1.0010 applied to these algorithmic bytes (profiles/decode_step_kernel_traffic.md)",
+                "kernel": "decode_step_kernel (persistent decode step: all 36 layers + lm_head in one launch)",
+                "bytes_per_launch": int(w_bytes + kv_bytes), "launches_timed": int(dec_tokens),
+                "bytes_note": "quantized weights (0.5625 B/param) + bf16 K/V read at the mean KV length 662",
+                "peak_source": peak_kind}
+        extra["qgemv_roofline"] = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                                   "frac": round(ach / peak, 4),
+                                   "kernel": "qw_quantized_matmul (standalone op, M=1), 4B layer shapes + lm_head",
+                                   "bytes_per_launch": int(per_launch), "launches_timed": nl}
         if world == 1 and not args.no_cpu:
             v, cores, desc = cpu_sample(args.cpu_tokens, os.cpu_count() or 1)
             cpu = {"value": round(v, 4), "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
@@ -383,18 +395,21 @@ def spec_measure(q, target, prompt, cfg4):
     return out
 
 
-def profile_decode(n: int) -> None:
-    """The bench model's prefill and n decode steps, one qw_forward each (for ncu launch lists)."""
+def profile_decode(n: int, model: str) -> None:
+    """Prefill and n decode steps, one qw_forward each (the ncu workloads): the
+    bench model (Qwen3-4B, 512-token prompt) or, for captures that must stay
+    small, Qwen3-0.6B with a 128-token prompt."""
     import torch
     import qwen3_b200 as q
-    cfg = dict(CFG_4B)
+    cfg = dict(CFG_4B if model == "4b" else CFG_0_6B)
+    plen = PROMPT_LEN if model == "4b" else 128
     m = q.Qwen3.init_random(cfg, SEED, norm_mode="ones", device=0)
     c = m.new_cache(KV_PREALLOC)
-    _, tok = m.forward(prompt_ids(cfg["vocab_size"]).tolist(), c, want_logits=False)
+    _, tok = m.forward(prompt_ids(cfg["vocab_size"])[:plen].tolist(), c, want_logits=False)
     for _ in range(n):
         _, tok = m.forward([tok], c, want_logits=False)
     torch.cuda.synchronize()
-    print(f"profile_decode: prefill {PROMPT_LEN} + {n} decode steps, last token {tok}")
+    print(f"profile_decode: {model} prefill {plen} + {n} decode steps, last token {tok}")
 
 
 def main():
@@ -408,13 +423,14 @@ def main():
     ap.add_argument("--ref-tokens", type=int, default=4)
     ap.add_argument("--no-spec", dest="spec", action="store_false")
     ap.add_argument("--profile-decode", type=int, default=0, metavar="N",
-                    help="profiling workload for ncu: weight init, the 512-token prefill and N greedy decode "
-                         "steps of the bench model through qw_forward; prints no bench line")
+                    help="profiling workload for ncu: weight init, the prefill and N greedy decode steps through "
+                         "qw_forward; prints no bench line")
+    ap.add_argument("--profile-model", choices=["4b", "0.6b"], default="4b")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.profile_decode > 0:
-        profile_decode(args.profile_decode)
+        profile_decode(args.profile_decode, args.profile_model)
     elif args.impl == "reference":
         run_reference(args)
     else:
