@@ -30,7 +30,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
     DecSmem<RMAX>& sm = *reinterpret_cast<DecSmem<RMAX>*>(smraw);
     pdl_wait();
     pdl_launch_dependents();
-    attn_decode_body<RMAX>(a, sm, blockIdx.x, blockIdx.y, gridDim.y, threadIdx.x, CtaSync{});
+    attn_decode_body<RMAX, 128>(a, sm, blockIdx.x, blockIdx.y, gridDim.y, threadIdx.x, CtaSync{});
 }
 
 // ---------------------------------------------------------------------------

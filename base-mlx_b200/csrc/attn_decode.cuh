@@ -62,17 +62,17 @@ struct DecSmem {
 };
 
 // Cached (old) K/V rows [j0, min(j0 + 64, T, off)) of kv head kvh -> tile buffer
-// `buf`, asynchronously (one commit group).  Old rows do not depend on the
-// current step, so a caller may issue the first two tiles early (`preloaded`).
-// Completion is tracked on the buffer's mbarrier (cp.async.mbarrier.arrive.noinc
-// from each of the 128 threads), not on the threads' cp.async groups, so a
-// caller whose threads have other copies in flight does not wait for them.
-template <int RMAX>
+// `buf`, asynchronously.  Old rows do not depend on the current step, so a
+// caller may issue the first two tiles early (`preloaded`).  Completion is
+// tracked on the buffer's mbarrier (cp.async.mbarrier.arrive.noinc from each
+// of the NT threads), not on the threads' cp.async groups, so a caller whose
+// threads have other copies in flight does not wait for them.
+template <int RMAX, int NT>
 QW_DEV void attn_load_tile(const AttnArgs& a, DecSmem<RMAX>& sm, int kvh, int buf, int j0, int T, int off, int tid) {
     const bf16* kbase = a.kcache + (size_t)kvh * a.max_pos * D;
     const bf16* vbase = a.vcache + (size_t)kvh * a.max_pos * D;
     const int nold = max(0, min(j0 + TILE, min(T, off)) - j0);
-    for (int idx = tid; idx < nold * 16; idx += 128) {
+    for (int idx = tid; idx < nold * 16; idx += NT) {
         const int r = idx >> 4, c = idx & 15;
         cp_async16(&sm.kt[buf][r][(c ^ (r & 15)) * 8], kbase + (size_t)(j0 + r) * D + c * 8);
         cp_async16(&sm.vt[buf][r][c * 8], vbase + (size_t)(j0 + r) * D + c * 8);
@@ -80,12 +80,12 @@ QW_DEV void attn_load_tile(const AttnArgs& a, DecSmem<RMAX>& sm, int kvh, int bu
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&sm.tbar[buf])) : "memory");
 }
 
-// (Re)initialise the two tile barriers (128 arrivals each); callers sync after.
-template <int RMAX>
+// (Re)initialise the two tile barriers (NT arrivals each); callers sync after.
+template <int RMAX, int NT>
 QW_DEV void attn_init_bars(DecSmem<RMAX>& sm, int tid) {
     if (tid == 0) {
-        mbar_init(&sm.tbar[0], 128);
-        mbar_init(&sm.tbar[1], 128);
+        mbar_init(&sm.tbar[0], NT);
+        mbar_init(&sm.tbar[1], NT);
         fence_mbar_init();
     }
 }
@@ -96,23 +96,33 @@ QW_DEV int attn_ntiles(int T, int split, int nsplit) {
     return split < nchunks ? (nchunks - split + nsplit - 1) / nsplit : 0;
 }
 
-// Issue the first two tile loads of attn_decode_body ahead of time (128 threads).
-template <int RMAX, typename Sync>
+// Issue the first two tile loads of attn_decode_body ahead of time (NT threads).
+template <int RMAX, int NT, typename Sync>
 QW_DEV void attn_decode_preload(const AttnArgs& a, DecSmem<RMAX>& sm, int kvh, int split, int nsplit, int tid,
                                 Sync sync) {
-    attn_init_bars(sm, tid);
+    attn_init_bars<RMAX, NT>(sm, tid);
     sync();
     const int off = *a.seq_len;
     const int T = off + a.S;
     if (T > a.max_pos) return;
     const int ntiles = attn_ntiles(T, split, nsplit);
-    if (ntiles > 0) attn_load_tile<RMAX>(a, sm, kvh, 0, split * TILE, T, off, tid);
-    if (ntiles > 1) attn_load_tile<RMAX>(a, sm, kvh, 1, (split + nsplit) * TILE, T, off, tid);
+    if (ntiles > 0) attn_load_tile<RMAX, NT>(a, sm, kvh, 0, split * TILE, T, off, tid);
+    if (ntiles > 1) attn_load_tile<RMAX, NT>(a, sm, kvh, 1, (split + nsplit) * TILE, T, off, tid);
 }
 
-template <int RMAX, typename Sync>
+// One (kv head, split) item with NT threads (a multiple of 128).  Work split:
+// scores -- thread = (key, row group of NT/64 groups); softmax -- warp per row;
+// P.V -- thread = (dim, key quarter of NT/128 quarters), each quarter keeping
+// its own rescaled accumulator, the quarters summed in order at the end.  Every
+// per-row quantity is computed in an order that depends on neither R nor T.
+template <int RMAX, int NT, typename Sync>
 QW_DEV void attn_decode_body(const AttnArgs& a, DecSmem<RMAX>& sm, const int kvh, const int split, const int nsplit,
                              const int tid, Sync sync, bool preloaded = false) {
+    constexpr int NW = NT / 32;
+    constexpr int RG = NT / 64;          // row groups in the score pass
+    constexpr int RPT = (RMAX + RG - 1) / RG;
+    constexpr int KQ = NT / 128;         // key quarters in the P.V pass
+    constexpr int KPQ = TILE / KQ;       // keys per quarter
     const int lane = tid & 31, warp = tid >> 5;
     const int S = a.S, G = a.Hq / a.Hkv, R = G * S;
     const int off = *a.seq_len;
@@ -126,16 +136,16 @@ QW_DEV void attn_decode_body(const AttnArgs& a, DecSmem<RMAX>& sm, const int kvh
     // on T: a verify of S rows and S single-row decodes produce bit-identical
     // outputs (chunks past a row's causal limit only add exact zeros).
     const int ntiles = attn_ntiles(T, split, nsplit);
-    auto load_tile = [&](int buf, int j0) { attn_load_tile<RMAX>(a, sm, kvh, buf, j0, T, off, tid); };
+    auto load_tile = [&](int buf, int j0) { attn_load_tile<RMAX, NT>(a, sm, kvh, buf, j0, T, off, tid); };
     if (!preloaded) {
-        attn_init_bars(sm, tid);
+        attn_init_bars<RMAX, NT>(sm, tid);
         sync();
         if (ntiles > 0) load_tile(0, split * TILE);
         if (ntiles > 1) load_tile(1, (split + nsplit) * TILE);
     }
 
     // queries: q_norm + rope
-    for (int r = warp; r < R; r += 4) {
+    for (int r = warp; r < R; r += NW) {
         const int gi = r / S, i = r - gi * S;
         const int h = kvh * G + gi, pos = off + i;
         float o[4];
@@ -147,7 +157,7 @@ QW_DEV void attn_decode_body(const AttnArgs& a, DecSmem<RMAX>& sm, const int kvh
         sm.qs[r][HALF + 2 * lane + 1] = o[3];
     }
     // new keys / values of this CTA's chunks: cache write + local copy
-    for (int p = off + warp; p < T; p += 4) {
+    for (int p = off + warp; p < T; p += NW) {
         if ((p / TILE) % nsplit != split) continue;
         const int i = p - off;
         float o[4];
@@ -169,17 +179,17 @@ QW_DEV void attn_decode_body(const AttnArgs& a, DecSmem<RMAX>& sm, const int kvh
     }
     sync();
 
+    const int d = tid & (D - 1), kq = tid / D;  // P.V: dim and key quarter
     float o_acc[RMAX];
 #pragma unroll
     for (int r = 0; r < RMAX; ++r) o_acc[r] = 0.f;
-    constexpr int RH = (RMAX + 1) / 2;
 
     for (int it = 0; it < ntiles; ++it) {
         const int buf = it & 1, j0 = (split + it * nsplit) * TILE;
         const int hi = min(T, j0 + TILE);
         if (!mbar_wait_bounded(&sm.tbar[buf], (it >> 1) & 1) && tid == 0) atomicOr(a.err, QW_DERR_TIMEOUT);
         // new positions of this tile come from the locally computed rows
-        for (int idx = tid; idx < TILE * 16; idx += 128) {
+        for (int idx = tid; idx < TILE * 16; idx += NT) {
             const int r = idx >> 4, c = idx & 15, j = j0 + r;
             if (j >= off && j < hi) {
                 *reinterpret_cast<uint4*>(&sm.kt[buf][r][(c ^ (r & 15)) * 8]) =
@@ -188,13 +198,13 @@ QW_DEV void attn_decode_body(const AttnArgs& a, DecSmem<RMAX>& sm, const int kvh
             }
         }
         sync();
-        // scores: thread -> key (tid & 63), rows of parity (tid >> 6)
+        // scores: thread -> key (tid & 63), rows par, par + RG, ...
         {
             const int jj = tid & (TILE - 1), par = tid >> 6;
             const int j = j0 + jj;
-            float acc[RH];
+            float acc[RPT];
 #pragma unroll
-            for (int q = 0; q < RH; ++q) acc[q] = 0.f;
+            for (int q = 0; q < RPT; ++q) acc[q] = 0.f;
             if (j < hi) {
 #pragma unroll 4
                 for (int dc = 0; dc < D / 8; ++dc) {
@@ -202,8 +212,8 @@ QW_DEV void attn_decode_body(const AttnArgs& a, DecSmem<RMAX>& sm, const int kvh
                     const float kf[8] = {bits_lo_f(u.x), bits_hi_f(u.x), bits_lo_f(u.y), bits_hi_f(u.y),
                                          bits_lo_f(u.z), bits_hi_f(u.z), bits_lo_f(u.w), bits_hi_f(u.w)};
 #pragma unroll
-                    for (int q = 0; q < RH; ++q) {
-                        const int r = par + 2 * q;
+                    for (int q = 0; q < RPT; ++q) {
+                        const int r = par + RG * q;
                         if (r < R) {
                             const float4 q0 = *reinterpret_cast<const float4*>(&sm.qs[r][dc * 8]);
                             const float4 q1 = *reinterpret_cast<const float4*>(&sm.qs[r][dc * 8 + 4]);
@@ -218,8 +228,8 @@ QW_DEV void attn_decode_body(const AttnArgs& a, DecSmem<RMAX>& sm, const int kvh
                 }
             }
 #pragma unroll
-            for (int q = 0; q < RH; ++q) {
-                const int r = par + 2 * q;
+            for (int q = 0; q < RPT; ++q) {
+                const int r = par + RG * q;
                 if (r < R) {
                     const int i = r % S;
                     const bool ok = (j < hi) && (j <= off + i);
@@ -229,7 +239,7 @@ QW_DEV void attn_decode_body(const AttnArgs& a, DecSmem<RMAX>& sm, const int kvh
         }
         sync();
         // online softmax update, one warp per row
-        for (int r = warp; r < R; r += 4) {
+        for (int r = warp; r < R; r += NW) {
             const float s0 = sm.sc[r][lane], s1 = sm.sc[r][lane + 32];
             const float mx = warp_max(fmaxf(s0, s1));
             const float mold = sm.mrow[r];
@@ -250,14 +260,13 @@ QW_DEV void attn_decode_body(const AttnArgs& a, DecSmem<RMAX>& sm, const int kvh
             }
         }
         sync();
-        // o[r][d] = o*alpha + sum_j p[r][j] v[j][d]; thread = dim
+        // o_q[r][d] = o_q*alpha + sum over this quarter's keys of p[r][j] v[j][d]
         {
-            const int d = tid;
 #pragma unroll
             for (int r = 0; r < RMAX; ++r)
                 if (r < R) o_acc[r] *= sm.alph[r];
-            const int nj = min(TILE, hi - j0);
-            for (int jj = 0; jj < nj; ++jj) {
+            const int jlo = kq * KPQ, jhi = min(jlo + KPQ, hi - j0);
+            for (int jj = jlo; jj < jhi; ++jj) {
                 const float vv = bf2f(sm.vt[buf][jj][d]);
 #pragma unroll
                 for (int r = 0; r < RMAX; ++r)
@@ -268,11 +277,27 @@ QW_DEV void attn_decode_body(const AttnArgs& a, DecSmem<RMAX>& sm, const int kvh
         if (it + 2 < ntiles) load_tile(buf, (split + (it + 2) * nsplit) * TILE);
     }
 
-    // partial -> global
-    const size_t pbase = ((size_t)kvh * nsplit + split) * RMAX;
+    // key quarters -> one accumulator per (row, dim), summed in quarter order
+    float* comb = reinterpret_cast<float*>(&sm.kt[0][0][0]);  // [KQ][R][D], tiles no longer needed
+    if (KQ > 1) {
 #pragma unroll
-    for (int r = 0; r < RMAX; ++r)
-        if (r < R) a.part[(pbase + r) * (D + 2) + tid] = o_acc[r];
+        for (int r = 0; r < RMAX; ++r)
+            if (r < R) comb[((size_t)kq * R + r) * D + d] = o_acc[r];
+        sync();
+    }
+    // partial -> global: thread (dim d, quarter kq) writes rows r = kq, kq + KQ, ...
+    const size_t pbase = ((size_t)kvh * nsplit + split) * RMAX;
+    for (int r = kq; r < R; r += KQ) {
+        float v = 0.f;
+        if (KQ > 1) {
+            for (int q = 0; q < KQ; ++q) v += comb[((size_t)q * R + r) * D + d];
+        } else {
+#pragma unroll
+            for (int rr = 0; rr < RMAX; ++rr)
+                if (rr == r) v = o_acc[rr];
+        }
+        a.part[(pbase + r) * (D + 2) + d] = v;
+    }
     if (tid < R) {
         a.part[(pbase + tid) * (D + 2) + D] = sm.mrow[tid];
         a.part[(pbase + tid) * (D + 2) + D + 1] = sm.lrow[tid];
@@ -281,15 +306,14 @@ QW_DEV void attn_decode_body(const AttnArgs& a, DecSmem<RMAX>& sm, const int kvh
     if (tid == 0) sm.last = (atom_add_acq_rel(&a.counters[kvh], 1u) == (unsigned)(nsplit - 1));
     sync();
     if (!sm.last) return;
-    // merge the splits (fixed order) and write bf16 output.  All split maxima
-    // and sums are gathered in one parallel pass; the tile buffers (no longer
-    // needed) hold them: nsplit * R <= 148 * 64 floats.
-    // Only splits that own a chunk have data (chunk c -> split c % nsplit);
-    // the others would add exact zeros, so skipping them changes no bit.
+    // merge the splits (fixed order) and write bf16 output.  Only splits that
+    // own a chunk have data (chunk c -> split c % nsplit); the others would add
+    // exact zeros, so skipping them changes no bit.  Split maxima and sums go to
+    // the tile buffers (no longer needed): nsplit * R <= 148 * 64 floats.
     const int nact = min(nsplit, (T + TILE - 1) / TILE);
     float* mb = reinterpret_cast<float*>(&sm.kt[0][0][0]);
     float* lb = mb + nsplit * R;
-    for (int idx = tid; idx < nact * R; idx += 128) {
+    for (int idx = tid; idx < nact * R; idx += NT) {
         const int s2 = idx / R, r = idx - s2 * R;
         const float* pp = a.part + (((size_t)kvh * nsplit + s2) * RMAX + r) * (D + 2);
         mb[idx] = __ldcg(pp + D);
@@ -310,26 +334,25 @@ QW_DEV void attn_decode_body(const AttnArgs& a, DecSmem<RMAX>& sm, const int kvh
         sm.lrow[tid] = Lsum;
     }
     sync();
-    // thread = dim; per row, up to 16 splits' partials are loaded together
-    for (int r = 0; r < R; ++r) {
+    // thread = (dim, row group); per row, up to 16 splits' partials are loaded together
+    for (int r = kq; r < R; r += KQ) {
         float O = 0.f;
         for (int s0 = 0; s0 < nact; s0 += 16) {
             float pv[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j)
                 pv[j] = (s0 + j < nact && mb[(s0 + j) * R + r] != 0.f)
-                            ? __ldcg(&a.part[(((size_t)kvh * nsplit + s0 + j) * RMAX + r) * (D + 2) + tid])
+                            ? __ldcg(&a.part[(((size_t)kvh * nsplit + s0 + j) * RMAX + r) * (D + 2) + d])
                             : 0.f;
 #pragma unroll
             for (int j = 0; j < 16; ++j)
                 if (s0 + j < nact) O = fmaf(pv[j], mb[(s0 + j) * R + r], O);
         }
         const int gi = r / S, i = r - gi * S;
-        a.out[(size_t)i * a.ldo + (kvh * G + gi) * D + tid] = f2bf(O / sm.lrow[r]);
+        a.out[(size_t)i * a.ldo + (kvh * G + gi) * D + d] = f2bf(O / sm.lrow[r]);
     }
     if (tid == 0) a.counters[kvh] = 0u;
 }
-
 
 }  // namespace attn
 }  // namespace qw

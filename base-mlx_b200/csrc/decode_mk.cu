@@ -311,6 +311,39 @@ QW_DEV void unit_coords(int u, int Mx, int& gl, int& m, int& j) {
     m = gm - gl * Mx;
 }
 
+// The 16 bf16 values of a unit as 8 packed words (the staged values are exact
+// bf16: rows of a bf16 matrix or bf16-rounded embedding entries).
+QW_DEV void load16_packed(const MkArgs& a, const StageSrc& s, int m, int k, uint32_t (&X)[8]) {
+    if (s.x) {
+        const uint4* p = reinterpret_cast<const uint4*>(s.x + (size_t)(s.row0 + m) * s.ld + k);
+        const uint4 u0 = __ldcg(p), u1 = __ldcg(p + 1);
+        X[0] = u0.x; X[1] = u0.y; X[2] = u0.z; X[3] = u0.w;
+        X[4] = u1.x; X[5] = u1.y; X[6] = u1.z; X[7] = u1.w;
+    } else {
+        float v[16];
+        load16(a, s, m, k, v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) X[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+    }
+}
+QW_DEV float sumsq_packed(const uint32_t (&X)[8]) {
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float lo = bits_lo_f(X[i]), hi = bits_hi_f(X[i]);
+        q = fmaf(lo, lo, q);
+        q = fmaf(hi, hi, q);
+    }
+    return q;
+}
+QW_DEV void unpack16(const uint32_t (&X)[8], float (&v)[16]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        v[2 * i] = bits_lo_f(X[i]);
+        v[2 * i + 1] = bits_hi_f(X[i]);
+    }
+}
+
 QW_DEV void stage_acts(const MkArgs& a, const StageSrc& s, int K, int Mx, uint32_t* xs, float* seeds, float* sq,
                        MkMisc& mm) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -319,24 +352,18 @@ QW_DEV void stage_acts(const MkArgs& a, const StageSrc& s, int K, int Mx, uint32
     if (s.norm && units <= 2 * MK_NT) {
         // RMSNorm in one pass over x: each thread keeps its (at most two) units
         // in registers while the per-row sums of squares are reduced
-        float v0[16], v1[16];
+        uint32_t X0[8], X1[8];
         int gl0 = 0, m0 = 0, j0 = 0, gl1 = 0, m1 = 0, j1 = 0;
         const int u0 = tid, u1 = tid + MK_NT;
         if (u0 < units) {
             unit_coords(u0, Mx, gl0, m0, j0);
-            load16(a, s, m0, gl0 * 64 + 16 * j0, v0);
-            float q = 0.f;
-#pragma unroll
-            for (int i = 0; i < 16; ++i) q = fmaf(v0[i], v0[i], q);
-            sq[u0] = q;
+            load16_packed(a, s, m0, gl0 * 64 + 16 * j0, X0);
+            sq[u0] = sumsq_packed(X0);
         }
         if (u1 < units) {
             unit_coords(u1, Mx, gl1, m1, j1);
-            load16(a, s, m1, gl1 * 64 + 16 * j1, v1);
-            float q = 0.f;
-#pragma unroll
-            for (int i = 0; i < 16; ++i) q = fmaf(v1[i], v1[i], q);
-            sq[u1] = q;
+            load16_packed(a, s, m1, gl1 * 64 + 16 * j1, X1);
+            sq[u1] = sumsq_packed(X1);
         }
         __syncthreads();
         if (warp < Mx) {
@@ -349,14 +376,18 @@ QW_DEV void stage_acts(const MkArgs& a, const StageSrc& s, int K, int Mx, uint32
         __syncthreads();
         float sum0 = 0.f, sum1 = 0.f;
         if (u0 < units) {
-            apply_norm(s, mm.rnorm[m0], gl0 * 64 + 16 * j0, v0);
-            sum0 = stage_unit(v0, gl0, m0, j0, Mx, xs);
+            float v[16];
+            unpack16(X0, v);
+            apply_norm(s, mm.rnorm[m0], gl0 * 64 + 16 * j0, v);
+            sum0 = stage_unit(v, gl0, m0, j0, Mx, xs);
         }
         stage_seeds(sum0, u0 < units, gl0, m0, j0, seeds);
         if (u1 - lane < units) {  // warp-uniform: some lane of this warp has a unit
             if (u1 < units) {
-                apply_norm(s, mm.rnorm[m1], gl1 * 64 + 16 * j1, v1);
-                sum1 = stage_unit(v1, gl1, m1, j1, Mx, xs);
+                float v[16];
+                unpack16(X1, v);
+                apply_norm(s, mm.rnorm[m1], gl1 * 64 + 16 * j1, v);
+                sum1 = stage_unit(v, gl1, m1, j1, Mx, xs);
             }
             stage_seeds(sum1, u1 < units, gl1, m1, j1, seeds);
         }
@@ -439,9 +470,9 @@ QW_DEV void cta_arrive(const MkArgs& a) {
     if (threadIdx.x == 0) red_release_add(a.sync, 1u);
 }
 
-// Attention uses warps 0-3 (128 threads) with a named barrier.
-struct NamedSync128 {
-    QW_DEV void operator()() const { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Attention items run on the whole CTA (taken by whole CTAs only).
+struct BlockSync {
+    QW_DEV void operator()() const { __syncthreads(); }
 };
 
 // Staged activations of one group for this lane: B fragments of the four
@@ -774,13 +805,13 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
             // the attention tiles' cached K/V rows do not depend on this step:
             // start loading them before waiting for the other CTAs' q|k|v
             __syncthreads();
-            if (warp < 4 && (int)blockIdx.x < a.aa.Hkv * a.aa.nsplit) {
+            if ((int)blockIdx.x < a.aa.Hkv * a.aa.nsplit) {
                 AttnArgs aa = a.aa;
                 aa.kcache = a.kc0 + (size_t)l * a.kv_layer_elems;
                 aa.vcache = a.vc0 + (size_t)l * a.kv_layer_elems;
-                attn::attn_decode_preload<RMAX>(aa, *reinterpret_cast<attn::DecSmem<RMAX>*>(uni),
-                                                blockIdx.x / a.aa.nsplit, blockIdx.x % a.aa.nsplit, a.aa.nsplit, tid,
-                                                NamedSync128{});
+                attn::attn_decode_preload<RMAX, MK_NT>(aa, *reinterpret_cast<attn::DecSmem<RMAX>*>(uni),
+                                                       blockIdx.x / a.aa.nsplit, blockIdx.x % a.aa.nsplit,
+                                                       a.aa.nsplit, tid, BlockSync{});
             }
             cta_arrive(a);
             ++arrivals;
@@ -789,15 +820,15 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
         {
             ok = cta_wait(a, arrivals * C, mm);
             if (!ok) break;
-            if (warp < 4 && (int)blockIdx.x < a.aa.Hkv * a.aa.nsplit) {
+            if ((int)blockIdx.x < a.aa.Hkv * a.aa.nsplit) {
                 AttnArgs aa = a.aa;
                 aa.q_norm_w = Ly.q_norm;
                 aa.k_norm_w = Ly.k_norm;
                 aa.kcache = a.kc0 + (size_t)l * a.kv_layer_elems;
                 aa.vcache = a.vc0 + (size_t)l * a.kv_layer_elems;
                 attn::DecSmem<RMAX>& asm_ = *reinterpret_cast<attn::DecSmem<RMAX>*>(uni);
-                attn::attn_decode_body<RMAX>(aa, asm_, blockIdx.x / a.aa.nsplit, blockIdx.x % a.aa.nsplit,
-                                             a.aa.nsplit, tid, NamedSync128{}, true);
+                attn::attn_decode_body<RMAX, MK_NT>(aa, asm_, blockIdx.x / a.aa.nsplit, blockIdx.x % a.aa.nsplit,
+                                                    a.aa.nsplit, tid, BlockSync{}, true);
             }
             cta_arrive(a);
             ++arrivals;
