@@ -2,6 +2,7 @@
 // exceptions into a status code plus a thread-local message, mirroring the
 // Result<T, Error> convention of crates/base-mlx-core/src/error.rs:6-32.
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <map>
@@ -352,6 +353,12 @@ int qw_spec_generate(qw_model* target, qw_model* draft, const uint32_t* prompt, 
     });
 }
 
+// QW_PREFILL_GEMM=legacy keeps multi-row matmuls on the mma.sync kernel.
+static bool legacy_prefill_gemm() {
+    const char* e = std::getenv("QW_PREFILL_GEMM");
+    return e && std::strcmp(e, "legacy") == 0;
+}
+
 int qw_quantized_matmul(const void* x, const void* w, const void* scales, const void* biases, void* y, int M,
                         int N, int K, int group_size, int bits, void* stream) {
     return guard([&] {
@@ -377,10 +384,19 @@ int qw_quantized_matmul(const void* x, const void* w, const void* scales, const 
         a.nseg = 1;
         a.epi = qw::EPI_STORE;
         cudaStream_t st = (cudaStream_t)stream;
-        if (M <= 8)
+        if (M <= 8) {
             QW_CUDA(qw::launch_qgemv(a, st, false, sms));
-        else
+        } else if (qw::qgemm_tc_supported(a) && !legacy_prefill_gemm()) {
+            // fp16 copy of x for the tensor-core kernel, stream-ordered
+            const size_t bytes = qw::qgemm_tc_scratch_bytes(M, K);
+            void* scratch = nullptr;
+            QW_CUDA(cudaMallocAsync(&scratch, bytes, st));
+            const cudaError_t e = qw::launch_qgemm_tc(a, scratch, bytes, st);
+            cudaFreeAsync(scratch, st);
+            QW_CUDA(e);
+        } else {
             QW_CUDA(qw::launch_qgemm(a, st, sms));
+        }
     });
 }
 

@@ -16,6 +16,7 @@
 // on the device, which lets one captured CUDA graph serve every decode step.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 
 #include "model.h"
@@ -50,9 +51,20 @@ QmmArgs qmm_base(qw_model* m, const bf16* x, int ldx, int M, int K) {
     return a;
 }
 
+// QW_PREFILL_GEMM=legacy keeps the multi-row matmuls on the mma.sync kernel.
+bool tc_gemm_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("QW_PREFILL_GEMM");
+        return !(e && std::strcmp(e, "legacy") == 0);
+    }();
+    return on;
+}
+
 void qmm(qw_model* m, QmmArgs a, cudaStream_t st) {
     if (a.M <= 8)
         QW_CUDA(launch_qgemv(a, st, true, m->num_sms));
+    else if (tc_gemm_enabled() && qgemm_tc_supported(a) && m->ws.xh_bytes >= qgemm_tc_scratch_bytes(a.M, a.K))
+        QW_CUDA(launch_qgemm_tc(a, m->ws.xh, m->ws.xh_bytes, st));
     else
         QW_CUDA(launch_qgemm(a, st, m->num_sms));
 }

@@ -54,6 +54,13 @@ cudaError_t launch_amax_finalize(const unsigned long long* partial, int nrb, int
                                  unsigned long long* keys_out, cudaStream_t st);
 // Prefill path: M > 8 (no norm prologue, no argmax; EPI_STORE/RESID/SWIGLU/F32).
 cudaError_t launch_qgemm(QmmArgs a, cudaStream_t st, int num_sms);
+// Prefill path on the tcgen05 tensor cores (qgemm_tc.cu): M > 8, K a multiple
+// of 128, no norm prologue, no argmax.  `scratch` holds the fp16 copy of x
+// (qgemm_tc_scratch_bytes).  Callers fall back to launch_qgemm when
+// qgemm_tc_supported is false.
+bool qgemm_tc_supported(const QmmArgs& a);
+size_t qgemm_tc_scratch_bytes(int M, int K);
+cudaError_t launch_qgemm_tc(QmmArgs a, void* scratch, size_t scratch_bytes, cudaStream_t st);
 
 // ---- other kernels ------------------------------------------------------
 struct AttnArgs {

@@ -383,6 +383,11 @@ void ensure_workspace(qw_model* m, int rows, int logits_rows) {
     w.mlp = (bf16*)alloc(rows * (size_t)m->inter_l * 2);
     w.logits = (bf16*)alloc((size_t)logits_rows * m->vocab_l * 2);
     w.f32 = (float*)alloc(rows * H * 4);
+    {
+        const int kmax = std::max<int>((int)std::max(H, QD), m->inter_l);
+        w.xh_bytes = qgemm_tc_scratch_bytes(rows, kmax);
+        w.xh = alloc(w.xh_bytes);
+    }
     w.ids = (int*)alloc(rows * 4);
     w.argmax = (int*)alloc(rows * 4);
     const size_t nrb_max = (size_t)m->vocab_l / 16 + 64;

@@ -63,6 +63,8 @@ struct Workspace {
     bf16 *x = nullptr, *h = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *qr = nullptr, *attn = nullptr,
          *mlp = nullptr, *logits = nullptr;
     float* f32 = nullptr;        // tensor-parallel partial sums [rows, hidden]
+    void* xh = nullptr;          // fp16 activations for the tcgen05 prefill GEMM
+    size_t xh_bytes = 0;
     int* ids = nullptr;          // input token ids [rows]
     int* argmax = nullptr;       // [rows]
     unsigned long long* amax_partial = nullptr;  // lm_head per-CTA maxima [row blocks, rows]

@@ -26,6 +26,7 @@
 #include <cuda_fp16.h>
 
 #include "kernels.h"
+#include "qmm_epi.cuh"
 
 namespace qw {
 namespace {
@@ -120,28 +121,6 @@ QW_DEV void stage16_f16(const bf16* src, const bf16* normw, float r, uint32_t* d
                        prmt(F[5], F[7], 0x5410));
     d4[1] = make_uint4(prmt(F[0], F[2], 0x7632), prmt(F[1], F[3], 0x7632), prmt(F[4], F[6], 0x7632),
                        prmt(F[5], F[7], 0x7632));
-}
-
-// Final per-element epilogue shared by both kernels (not EPI_LOGITS).
-QW_DEV void store_out(const QmmArgs& a, int si, int epi, int row, int feat, int col, float v0, float v1) {
-    if (epi == EPI_SWIGLU) {
-        const float g = bfr(v0), u = bfr(v1);
-        const float sg = bfr(1.0f / (1.0f + expf(-g)));
-        const float act = bfr(__fmul_rn(g, sg));
-        bf16* y = reinterpret_cast<bf16*>(a.seg[0].y);
-        y[(size_t)col * a.seg[0].ldy + feat] = f2bf(__fmul_rn(act, u));
-        return;
-    }
-    const QSeg& sg = a.seg[si];
-    const size_t idx = (size_t)col * sg.ldy + row;
-    if (epi == EPI_F32) {
-        reinterpret_cast<float*>(sg.y)[idx] = v0;
-    } else if (epi == EPI_RESID) {
-        bf16* y = reinterpret_cast<bf16*>(sg.y);
-        y[idx] = f2bf(__fadd_rn(bf2f(y[idx]), bfr(v0)));
-    } else {
-        reinterpret_cast<bf16*>(sg.y)[idx] = f2bf(v0);
-    }
 }
 
 // ===========================================================================
