@@ -6,35 +6,41 @@
 //
 // Tile: 128 output features (the MMA M) x 128 activation rows (the MMA N), fp32
 // accumulators in tensor memory (TMEM), K walked one 64-wide quantization group
-// per pipeline stage.  Operands are fp16, K-major, in the no-swizzle canonical
-// layout (8 rows x 16 bytes per core matrix, core matrices of one 8-row block
-// contiguous along K: LBO 128 B between the two K halves of an MMA, SBO 1 KB
-// between 8-row blocks).
+// per stage.  Operands are fp16, K-major, in the 128-byte-swizzled canonical
+// layout (one 128-byte row per tile row, its eight 16-byte chunks XOR-permuted
+// by row % 8, 1 KB per 8 rows).
 //
 //   * activations: converted once per call from bf16 to fp16 by
-//     x_to_f16p_kernel (exact for |x| in fp16 range), with the eight elements
-//     of every 8-wide K chunk stored in the order (0,4,1,5,2,6,3,7) and rows
-//     zero-padded to a multiple of 128; 16-byte cp.async copies then place
-//     each chunk directly in its core-matrix row.
-//   * weights: 16-byte cp.async copies of the packed words and 4-byte copies of
-//     the (scale, bias) pairs into a raw stage; each producer thread then
-//     dequantizes its own 32 weights: nibble pairs (j, j+4) of a word become
-//     the fp16 pair 1024+q with one LOP3, 1024 is subtracted exactly, and
-//     w = q*s + b is one fused half2 FMA (single rounding to fp16).  The
-//     pair order matches the activation permutation above.
+//     x_to_f16p_kernel (exact for |x| in fp16 range), the eight elements of
+//     every 8-wide K chunk stored in the order (0,4,1,5,2,6,3,7), rows
+//     zero-padded to a multiple of 128; one TMA tensor load (128B swizzle)
+//     per stage brings the 128 x 64 tile.
+//   * weights: one TMA tensor load per stage of the packed words (128 rows x
+//     32 bytes, rows past N zero-filled) and, every 8 stages, of the scales and
+//     biases (128 rows x 8 groups); producer threads dequantize: nibble pairs
+//     (j, j+4) of a word become the fp16 pair 1024+q with one LOP3, 1024 is
+//     subtracted exactly, and w = q*s + b is one fused half2 FMA (a single
+//     rounding to fp16).  The pair order matches the activation permutation.
 //
-// Roles (288 threads): warps 0-7 are producers (copies, dequantization) and
-// afterwards the epilogue; lane 0 of warp 8 issues tcgen05.mma (4 per stage
-// per 128-row weight tile) and signals stage release / completion through
-// tcgen05.commit on mbarriers; warp 8 owns the TMEM allocation.  Every wait
-// is bounded: a lost arrival sets QW_DERR_TIMEOUT and the CTA still releases
-// its TMEM and exits.
+// Roles (320 threads): warps 0-7 dequantize into a two-deep operand ring and
+// then run the epilogue; lane 0 of warp 8 issues tcgen05.mma (4 per stage per
+// 128-row weight tile) and releases stages with tcgen05.commit; lane 0 of
+// warp 9 issues the TMA loads into an L-deep load ring.  Warp 8 owns the TMEM
+// allocation.  Producers only touch shared memory, so the proxy fence that
+// publishes their operand tile never waits on an outstanding global copy.
+// Every wait is bounded: a lost arrival sets QW_DERR_TIMEOUT and the CTA
+// still releases its TMEM and exits.
 //
 // RT = 2 runs the gate and up projections of the MLP in one CTA (two TMEM
 // accumulators) for the fused SiLU(gate) * up epilogue.
+#include <cuda.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "kernels.h"
 #include "qmm_epi.cuh"
@@ -44,21 +50,36 @@ namespace {
 
 constexpr int TC_BM = 128;            // output features per tile (MMA M)
 constexpr int TC_BN = 128;            // activation rows per tile (MMA N)
-constexpr int TC_PT = 256;            // producer threads
-constexpr int TC_NT = TC_PT + 32;     // + the MMA warp
+constexpr int TC_PT = 256;            // producer threads (warps 0-7)
+constexpr int TC_NT = TC_PT + 64;     // + MMA warp + TMA warp
+constexpr int TC_LMAX = 8;            // deepest load ring
+constexpr int TC_SMEM_MAX = 232448;   // opt-in shared memory per block
 constexpr unsigned long long TC_TIMEOUT_NS = 2000000000ull;
 
+// Shared-memory plan (bytes from the 1 KB-aligned base; every tile 1 KB aligned):
+//   [0, 1024)            mbarriers + TMEM address
+//   A ring   2 x RT x 16 KB   dequantized weights (fp16, swizzled)
+//   SB ring  2 x RT x 4 KB    scales [128][8] bf16 then biases [128][8] bf16
+//   load ring L x (16 KB activations + RT x 4 KB packed words)
 template <int RT>
-struct TcCfg {
-    static constexpr int A_BYTES = RT * TC_BM * 64 * 2;   // fp16 weight operand
-    static constexpr int B_BYTES = TC_BN * 64 * 2;        // fp16 activation operand
-    static constexpr int W_BYTES = RT * TC_BM * 32;       // packed words of one group
-    static constexpr int SB_BYTES = RT * 2 * TC_BM * 8;   // (scale pair, bias pair) per row and half
-    static constexpr int STAGE = A_BYTES + B_BYTES + W_BYTES + SB_BYTES;
-    static constexpr int S = RT == 1 ? 4 : 3;             // pipeline depth
-    static constexpr int CTRL = 256;                      // mbarriers + TMEM address
-    static constexpr int SMEM = CTRL + S * STAGE + 128;   // + alignment slack
+struct TcPlan {
+    static constexpr int A_TILE = TC_BM * 128;
+    static constexpr int A_OFF = 1024;
+    static constexpr int SB_OFF = A_OFF + 2 * RT * A_TILE;
+    static constexpr int SB_SLOT = RT * 4096;
+    static constexpr int LD_OFF = SB_OFF + 2 * SB_SLOT;
+    static constexpr int LD_SLOT = TC_BN * 128 + RT * 4096;
+    static constexpr int L = (TC_SMEM_MAX - 1024 - LD_OFF) / LD_SLOT > TC_LMAX ? TC_LMAX
+                                                                                : (TC_SMEM_MAX - 1024 - LD_OFF) / LD_SLOT;
+    static constexpr int SMEM = LD_OFF + L * LD_SLOT + 1024;  // + base alignment slack
     static constexpr uint32_t TMEM_COLS = RT * TC_BN;
+};
+
+// TMA tensor maps of one launch: activations, then per segment the packed
+// words, scales and biases.
+struct TcMaps {
+    CUtensorMap x;
+    CUtensorMap w[3], s[3], b[3];
 };
 
 // Instruction descriptor (kind::f16): fp32 accumulate, fp16 A and B, both
@@ -66,10 +87,12 @@ struct TcCfg {
 constexpr uint32_t TC_IDESC = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(TC_BN >> 3) << 17) |
                               ((uint32_t)(TC_BM >> 4) << 24);
 
-// Shared-memory matrix descriptor, no swizzle, K-major (descriptor version 1).
-QW_DEV uint64_t tc_sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
-    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 1 KB between
+// 8-row groups, descriptor version 1.  A K-step of 16 elements inside the
+// 128-byte row advances the start address by 32 bytes.
+QW_DEV uint64_t tc_sdesc_sw128(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)(1024u >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
 }
 
 QW_DEV unsigned long long tc_clock() {
@@ -90,8 +113,14 @@ QW_DEV bool tc_wait(uint64_t* bar, uint32_t parity) {
 QW_DEV void tc_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-QW_DEV void cp_async4(void* dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+// 2-D TMA tensor load into this CTA's shared memory (no multicast: the source
+// is this GPU's own memory), completion counted on `bar` in bytes.
+QW_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
 }
 QW_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 QW_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -127,18 +156,22 @@ QW_DEV void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "me
 QW_DEV uint32_t nib_f16x2(uint32_t w) { return (w & 0x000F000Fu) | 0x64006400u; }
 
 template <int RT>
-__global__ void __launch_bounds__(TC_NT, 1) qgemm_tc_kernel(const QmmArgs a, const __half* __restrict__ xh) {
-    using C = TcCfg<RT>;
+__global__ void __launch_bounds__(TC_NT, 1) qgemm_tc_kernel(const QmmArgs a, const __grid_constant__ TcMaps maps) {
+    using P = TcPlan<RT>;
+    constexpr int L = P::L;
     extern __shared__ unsigned char tc_smem_raw[];
-    unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)tc_smem_raw + 127) & ~(uintptr_t)127);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);   // [S] producers -> MMA
-    uint64_t* empty = full + 4;                           // [S] MMA -> producers
-    uint64_t* done = full + 8;                            // accumulators final
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full + 12);
-    unsigned char* stages = smem + C::CTRL;
+    unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)tc_smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* ld_full = reinterpret_cast<uint64_t*>(smem);   // [L] TMA -> producers, MMA
+    uint64_t* ld_empty = ld_full + TC_LMAX;                   // [L] MMA -> TMA
+    uint64_t* a_full = ld_empty + TC_LMAX;                    // [2] producers -> MMA
+    uint64_t* a_empty = a_full + 2;                           // [2] MMA -> producers
+    uint64_t* sb_full = a_empty + 2;                          // [2] TMA -> producers
+    uint64_t* sb_empty = sb_full + 2;                         // [2] producers -> TMA
+    uint64_t* done = sb_empty + 2;                            // accumulators final
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int K = a.K, KG = K / 64, KW = K / 8;
+    const int KG = a.K / 64;
     const int rb = blockIdx.x, t0 = blockIdx.y * TC_BN;
 
     // segment of this row block (q | k | v of the fused qkv launch, or one)
@@ -148,17 +181,28 @@ __global__ void __launch_bounds__(TC_NT, 1) qgemm_tc_kernel(const QmmArgs a, con
         if (RT == 1 && i < a.nseg && rb >= a.seg[i].rb0) si = i;
     const int n0 = (rb - a.seg[si].rb0) * TC_BM;
 
+    auto A_of = [&](int slot, int rt) { return smem + P::A_OFF + (slot * RT + rt) * P::A_TILE; };
+    auto SB_of = [&](int slot, int rt) { return smem + P::SB_OFF + slot * P::SB_SLOT + rt * 4096; };
+    auto X_of = [&](int slot) { return smem + P::LD_OFF + slot * P::LD_SLOT; };
+    auto W_of = [&](int slot, int rt) { return smem + P::LD_OFF + slot * P::LD_SLOT + TC_BN * 128 + rt * 4096; };
+
     if (tid == 0) {
-        for (int s = 0; s < C::S; ++s) {
-            mbar_init(full + s, TC_PT);
-            mbar_init(empty + s, 1);
+        for (int s = 0; s < L; ++s) {
+            mbar_init(ld_full + s, 1);
+            mbar_init(ld_empty + s, 1);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(a_full + s, TC_PT);
+            mbar_init(a_empty + s, 1);
+            mbar_init(sb_full + s, 1);
+            mbar_init(sb_empty + s, TC_PT);
         }
         mbar_init(done, 1);
         fence_mbar_init();
     }
     if (warp == 8) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(C::TMEM_COLS)
+                     "r"(P::TMEM_COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -169,133 +213,112 @@ __global__ void __launch_bounds__(TC_NT, 1) qgemm_tc_kernel(const QmmArgs a, con
 
     pdl_wait();
 
-    auto A_of = [&](int slot, int rt) { return stages + (size_t)slot * C::STAGE + rt * (TC_BM * 64 * 2); };
-    auto B_of = [&](int slot) { return stages + (size_t)slot * C::STAGE + C::A_BYTES; };
-    auto W_of = [&](int slot, int rt) {
-        return stages + (size_t)slot * C::STAGE + C::A_BYTES + C::B_BYTES + rt * (TC_BM * 32);
-    };
-    auto SB_of = [&](int slot, int rt) {
-        return stages + (size_t)slot * C::STAGE + C::A_BYTES + C::B_BYTES + C::W_BYTES + rt * (2 * TC_BM * 8);
-    };
-
     bool ok = true;
     if (warp < 8) {
-        // ---- producers -------------------------------------------------------
+        // ---- producers: packed words -> fp16 operand tile --------------------------
         const int row = tid & 127, half = tid >> 7;
-        const uint32_t* wrow[RT];
-        const bf16* srow[RT];
-        const bf16* brow[RT];
-        bool valid[RT];
-#pragma unroll
-        for (int rt = 0; rt < RT; ++rt) {
-            const QSeg& sg = a.seg[RT == 2 ? rt : si];
-            const int n = n0 + row;
-            valid[rt] = n < sg.n;
-            const int nn = valid[rt] ? n : 0;
-            wrow[rt] = sg.w + (size_t)nn * KW + 4 * half;
-            srow[rt] = sg.s + (size_t)nn * KG;
-            brow[rt] = sg.b + (size_t)nn * KG;
-        }
-        const __half* xrow = xh + (size_t)t0 * K;
-
-        auto issue = [&](int gi) {
-            const int slot = gi % C::S;
-#pragma unroll
-            for (int rt = 0; rt < RT; ++rt) {
-                unsigned char* wd = W_of(slot, rt) + row * 32 + half * 16;
-                unsigned char* sd = SB_of(slot, rt) + (half * TC_BM + row) * 8;
-                if (valid[rt]) {
-                    cp_async16(wd, wrow[rt] + (size_t)gi * 8);
-                    cp_async4(sd, srow[rt] + (gi & ~1));
-                    cp_async4(sd + 4, brow[rt] + (gi & ~1));
-                } else {
-                    *reinterpret_cast<uint4*>(wd) = make_uint4(0u, 0u, 0u, 0u);
-                    *reinterpret_cast<uint2*>(sd) = make_uint2(0u, 0u);
-                }
-            }
-            unsigned char* bd = B_of(slot);
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int q = tid + TC_PT * u;
-                const int tt = (q & 7) + 8 * (q >> 6), j = (q >> 3) & 7;
-                cp_async16(bd + (tt >> 3) * 1024 + j * 128 + (tt & 7) * 16, xrow + (size_t)tt * K + gi * 64 + j * 8);
-            }
-        };
-
-#pragma unroll
-        for (int i = 0; i < C::S - 1; ++i) {
-            if (i < KG) issue(i);
-            cp_async_commit();
-        }
         const __half2 k1024 = __float2half2_rn(1024.f);
         for (int gi = 0; gi < KG; ++gi) {
-            const int ni = gi + C::S - 1;
-            if (ni < KG) {
-                // slot of stage ni last held stage gi-1: its MMAs must have finished
-                if (gi >= 1 && ok && !tc_wait(empty + (gi - 1) % C::S, ((gi - 1) / C::S) & 1)) ok = false;
-                issue(ni);
-            }
-            cp_async_commit();
-            cp_async_wait<C::S - 1>();
-            const int slot = gi % C::S;
+            const int ls = gi % L, as = gi & 1, c = gi >> 3;
+            if (ok && (gi & 7) == 0 && !tc_wait(sb_full + (c & 1), (c >> 1) & 1)) ok = false;
+            if (ok && !tc_wait(ld_full + ls, (gi / L) & 1)) ok = false;
+            if (ok && gi >= 2 && !tc_wait(a_empty + as, ((gi - 2) >> 1) & 1)) ok = false;
 #pragma unroll
             for (int rt = 0; rt < RT; ++rt) {
-                const uint4 wr = *reinterpret_cast<const uint4*>(W_of(slot, rt) + row * 32 + half * 16);
-                const uint2 sbp = *reinterpret_cast<const uint2*>(SB_of(slot, rt) + (half * TC_BM + row) * 8);
-                const uint32_t sh = (gi & 1) ? 16u : 0u;
-                const float sf = __uint_as_float(((sbp.x >> sh) & 0xFFFFu) << 16);
-                const float bf = __uint_as_float(((sbp.y >> sh) & 0xFFFFu) << 16);
+                const uint4 wr = *reinterpret_cast<const uint4*>(W_of(ls, rt) + row * 32 + half * 16);
+                const unsigned short* sbp = reinterpret_cast<const unsigned short*>(SB_of(c & 1, rt));
+                const float sf = __uint_as_float((uint32_t)sbp[row * 8 + (gi & 7)] << 16);
+                const float bf = __uint_as_float((uint32_t)sbp[1024 + row * 8 + (gi & 7)] << 16);
                 const __half2 s2 = __float2half2_rn(sf), b2 = __float2half2_rn(bf);
                 const uint32_t wv[4] = {wr.x, wr.y, wr.z, wr.w};
-                unsigned char* ad = A_of(slot, rt) + (row >> 3) * 1024 + (row & 7) * 16;
+                unsigned char* ad = A_of(as, rt) + row * 128;
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     uint32_t o[4];
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         uint32_t h = nib_f16x2(wv[u] >> (4 * j));
-                        __half2 q = __hsub2(*reinterpret_cast<__half2*>(&h), k1024);
-                        __half2 r = __hfma2(q, s2, b2);
-                        o[j] = *reinterpret_cast<uint32_t*>(&r);
+                        const __half2 q = __hsub2(*reinterpret_cast<const __half2*>(&h), k1024);
+                        const __half2 r = __hfma2(q, s2, b2);
+                        o[j] = *reinterpret_cast<const uint32_t*>(&r);
                     }
-                    *reinterpret_cast<uint4*>(ad + (half * 4 + u) * 128) = make_uint4(o[0], o[1], o[2], o[3]);
+                    *reinterpret_cast<uint4*>(ad + (((half * 4 + u) ^ (row & 7)) << 4)) =
+                        make_uint4(o[0], o[1], o[2], o[3]);
                 }
             }
             fence_proxy_async();
-            tc_arrive(full + slot);
+            tc_arrive(a_full + as);
+            if ((gi & 7) == 7) tc_arrive(sb_empty + (c & 1));
         }
-        cp_async_wait<0>();
+    } else if (warp == 8) {
+        if (lane == 0) {
+            // ---- MMA issuer ------------------------------------------------------------
+            for (int gi = 0; gi < KG; ++gi) {
+                const int ls = gi % L, as = gi & 1;
+                if (!tc_wait(a_full + as, (gi >> 1) & 1) || !tc_wait(ld_full + ls, (gi / L) & 1)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t xb = smem_u32(X_of(ls));
+#pragma unroll
+                for (int rt = 0; rt < RT; ++rt) {
+                    const uint32_t ab = smem_u32(A_of(as, rt));
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        tc_mma(tmem + rt * TC_BN, tc_sdesc_sw128(ab + 32 * j), tc_sdesc_sw128(xb + 32 * j),
+                               (gi | j) != 0 ? 1u : 0u);
+                }
+                tc_commit(a_empty + as);
+                tc_commit(ld_empty + ls);
+            }
+            tc_commit(done);
+        }
     } else if (lane == 0) {
-        // ---- MMA issuer ----------------------------------------------------------
+        // ---- TMA issuer ----------------------------------------------------------------
+        const CUtensorMap* wmap[RT];
+        const CUtensorMap* smap[RT];
+        const CUtensorMap* bmap[RT];
+#pragma unroll
+        for (int rt = 0; rt < RT; ++rt) {
+            const int sg = RT == 2 ? rt : si;
+            wmap[rt] = &maps.w[sg];
+            smap[rt] = &maps.s[sg];
+            bmap[rt] = &maps.b[sg];
+        }
         for (int gi = 0; gi < KG; ++gi) {
-            const int slot = gi % C::S;
-            if (!tc_wait(full + slot, (gi / C::S) & 1)) {
+            const int ls = gi % L;
+            if ((gi & 7) == 0) {
+                const int c = gi >> 3;
+                if (c >= 2 && !tc_wait(sb_empty + (c & 1), ((c - 2) >> 1) & 1)) {
+                    ok = false;
+                    break;
+                }
+                mbar_arrive_expect_tx(sb_full + (c & 1), RT * 4096);
+#pragma unroll
+                for (int rt = 0; rt < RT; ++rt) {
+                    tma_load_2d(SB_of(c & 1, rt), smap[rt], c * 8, n0, sb_full + (c & 1));
+                    tma_load_2d(SB_of(c & 1, rt) + 2048, bmap[rt], c * 8, n0, sb_full + (c & 1));
+                }
+            }
+            if (gi >= L && !tc_wait(ld_empty + ls, ((gi - L) / L) & 1)) {
                 ok = false;
                 break;
             }
-            tc_fence_after();
-            const uint32_t bbase = smem_u32(B_of(slot));
+            mbar_arrive_expect_tx(ld_full + ls, TC_BN * 128 + RT * 4096);
+            tma_load_2d(X_of(ls), &maps.x, gi * 64, t0, ld_full + ls);
 #pragma unroll
-            for (int rt = 0; rt < RT; ++rt) {
-                const uint32_t abase = smem_u32(A_of(slot, rt));
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    tc_mma(tmem + rt * TC_BN, tc_sdesc(abase + j * 256, 128, 1024), tc_sdesc(bbase + j * 256, 128, 1024),
-                           (gi | j) != 0 ? 1u : 0u);
-            }
-            tc_commit(empty + slot);
+            for (int rt = 0; rt < RT; ++rt) tma_load_2d(W_of(ls, rt), wmap[rt], gi * 8, n0, ld_full + ls);
         }
-        tc_commit(done);
     }
     pdl_launch_dependents();
 
-    // ---- epilogue: TMEM -> registers -> outputs --------------------------------
+    // ---- epilogue: TMEM -> registers -> outputs --------------------------------------
     if (warp < 8) {
         if (!tc_wait(done, 0)) ok = false;
         tc_fence_after();
         const int lq = warp & 3, ch = warp >> 2;
-        const int r = 32 * lq + lane;
-        const int n = n0 + r;
+        const int n = n0 + 32 * lq + lane;
         const bool nvalid = n < a.seg[RT == 2 ? 0 : si].n;
 #pragma unroll 1
         for (int cc = 0; cc < 4; ++cc) {
@@ -322,7 +345,7 @@ __global__ void __launch_bounds__(TC_NT, 1) qgemm_tc_kernel(const QmmArgs a, con
     __syncthreads();
     if (warp == 8) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(P::TMEM_COLS)
                      : "memory");
     }
 }
@@ -370,16 +393,72 @@ cudaError_t launch_pdl(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStre
     return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
+// cuTensorMapEncodeTiled, resolved through the runtime (no link-time libcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return (EncodeTiledFn) nullptr;
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+// 2-D map over a row-major [rows, cols] tensor with a (box_cols x box_rows) box.
+bool make_map(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* base, long long cols, long long rows,
+              int box_cols, int box_rows, CUtensorMapSwizzle sw) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * esize};
+    const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Weight-side maps depend only on (pointer, rows, K): cached across calls.
+struct SegMaps {
+    CUtensorMap w, s, b;
+};
+bool seg_maps(const QSeg& sg, int K, SegMaps& out) {
+    static std::mutex mu;
+    static std::map<std::tuple<const void*, int, int>, SegMaps> cache;
+    const auto key = std::make_tuple((const void*)sg.w, sg.n, K);
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        out = it->second;
+        return true;
+    }
+    SegMaps m;
+    const int KW = K / 8, KG = K / 64;
+    if (!make_map(&m.w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, sg.w, KW, sg.n, 8, TC_BM, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map(&m.s, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, sg.s, KG, sg.n, 8, TC_BM, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map(&m.b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, sg.b, KG, sg.n, 8, TC_BM, CU_TENSOR_MAP_SWIZZLE_NONE))
+        return false;
+    if (cache.size() > 4096) cache.clear();
+    cache.emplace(key, m);
+    out = m;
+    return true;
+}
+
 template <int RT>
-cudaError_t launch_tc_t(const QmmArgs& a, const __half* xh, dim3 grid, cudaStream_t st) {
+cudaError_t launch_tc_t(const QmmArgs& a, const TcMaps& maps, dim3 grid, cudaStream_t st) {
     static bool set = false;
     if (!set) {
         const cudaError_t e =
-            cudaFuncSetAttribute(qgemm_tc_kernel<RT>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<RT>::SMEM);
+            cudaFuncSetAttribute(qgemm_tc_kernel<RT>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcPlan<RT>::SMEM);
         if (e != cudaSuccess) return e;
         set = true;
     }
-    return launch_pdl(qgemm_tc_kernel<RT>, grid, dim3(TC_NT), (size_t)TcCfg<RT>::SMEM, st, a, xh);
+    return launch_pdl(qgemm_tc_kernel<RT>, grid, dim3(TC_NT), (size_t)TcPlan<RT>::SMEM, st, a, maps);
 }
 
 }  // namespace
@@ -391,10 +470,12 @@ bool qgemm_tc_supported(const QmmArgs& a) {
     if (a.epi == EPI_LOGITS || a.norm_w) return false;
     if (a.ldx % 8 != 0) return false;
     if (a.epi == EPI_SWIGLU && (a.nseg < 2 || a.seg[0].n != a.seg[1].n)) return false;
-    if ((uintptr_t)a.x % 16 != 0) return false;
+    // TMA: 16-byte aligned bases, row strides a multiple of 16 bytes (K/64
+    // groups of bf16 scales per row -> K a multiple of 512)
+    if (a.K % 512 != 0 || (uintptr_t)a.x % 16 != 0 || !encode_fn()) return false;
     const int ns = a.epi == EPI_SWIGLU ? 2 : a.nseg;
-    for (int i = 0; i < ns; ++i)  // 16-byte word copies, 4-byte scale / bias pair copies
-        if ((uintptr_t)a.seg[i].w % 16 != 0 || (uintptr_t)a.seg[i].s % 4 != 0 || (uintptr_t)a.seg[i].b % 4 != 0)
+    for (int i = 0; i < ns; ++i)
+        if ((uintptr_t)a.seg[i].w % 16 != 0 || (uintptr_t)a.seg[i].s % 16 != 0 || (uintptr_t)a.seg[i].b % 16 != 0)
             return false;
     return true;
 }
@@ -420,9 +501,20 @@ cudaError_t launch_qgemm_tc(QmmArgs a, void* scratch, size_t scratch_bytes, cuda
     const int cblocks = (int)std::min<long long>((chunks + 255) / 256, 148 * 8);
     cudaError_t e = launch_pdl(x_to_f16p_kernel, dim3(cblocks), dim3(256), 0, st, a.x, a.ldx, a.M, Mpad, a.K, xh);
     if (e != cudaSuccess) return e;
+    TcMaps maps;
+    std::memset(&maps, 0, sizeof(maps));
+    if (!make_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh, a.K, Mpad, 64, TC_BN, CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    for (int i = 0; i < a.nseg; ++i) {
+        SegMaps sm;
+        if (!seg_maps(a.seg[i], a.K, sm)) return cudaErrorInvalidValue;
+        maps.w[i] = sm.w;
+        maps.s[i] = sm.s;
+        maps.b[i] = sm.b;
+    }
     const dim3 grid(nrb, Mpad / TC_BN);
-    if (a.epi == EPI_SWIGLU) return launch_tc_t<2>(a, xh, grid, st);
-    return launch_tc_t<1>(a, xh, grid, st);
+    if (a.epi == EPI_SWIGLU) return launch_tc_t<2>(a, maps, grid, st);
+    return launch_tc_t<1>(a, maps, grid, st);
 }
 
 }  // namespace qw
