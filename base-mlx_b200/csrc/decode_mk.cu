@@ -35,6 +35,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 
 #include "attn_decode.cuh"
@@ -47,6 +48,11 @@ namespace {
 constexpr int MK_NW = 16;
 constexpr int MK_NT = MK_NW * 32;
 constexpr int GR_BYTES = 576;  // one granule: 512 B nibbles + 64 B scales/biases
+// The GEMV phases stage their activations past the head of the shared union,
+// which holds the attention tile mbarriers (attn::DecSmem::tbar, written by
+// asynchronous cp.async arrivals): staged data never shares bytes with a
+// barrier that an arrival could still update.
+constexpr size_t MK_UNI_RESERVED = 128;
 constexpr int XW = 36;         // words per (group, column) block of staged activations (32 + 4 pad)
 constexpr int SEEDF = 8;       // floats per (group, quad t) seed entry
 constexpr unsigned long long MK_TIMEOUT_NS = 2000000000ull;
@@ -778,8 +784,8 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
         // ---- q|k|v (x = embedding rows at layer 0)
         {
             const MkLin lin = Ly.lin[K_QKV];
-            uint32_t* xs = reinterpret_cast<uint32_t*>(uni);
-            float* seeds = reinterpret_cast<float*>(uni + (size_t)lin.KG * M * XW * 4);
+            uint32_t* xs = reinterpret_cast<uint32_t*>(uni + MK_UNI_RESERVED);
+            float* seeds = reinterpret_cast<float*>(uni + MK_UNI_RESERVED + (size_t)lin.KG * M * XW * 4);
             float* red = seeds + (size_t)lin.KG * 4 * SEEDF;
             if (l > 0) ok = cta_wait(a, arrivals * C, mm);
             if (!ok) break;
@@ -836,8 +842,8 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
         // ---- o_proj + residual
         {
             const MkLin lin = Ly.lin[K_O];
-            uint32_t* xs = reinterpret_cast<uint32_t*>(uni);
-            float* seeds = reinterpret_cast<float*>(uni + (size_t)lin.KG * M * XW * 4);
+            uint32_t* xs = reinterpret_cast<uint32_t*>(uni + MK_UNI_RESERVED);
+            float* seeds = reinterpret_cast<float*>(uni + MK_UNI_RESERVED + (size_t)lin.KG * M * XW * 4);
             float* red = seeds + (size_t)lin.KG * 4 * SEEDF;
             ok = cta_wait(a, arrivals * C, mm);
             if (!ok) break;
@@ -851,8 +857,8 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
         // ---- gate|up + SwiGLU
         {
             const MkLin lin = Ly.lin[K_GU];
-            uint32_t* xs = reinterpret_cast<uint32_t*>(uni);
-            float* seeds = reinterpret_cast<float*>(uni + (size_t)lin.KG * M * XW * 4);
+            uint32_t* xs = reinterpret_cast<uint32_t*>(uni + MK_UNI_RESERVED);
+            float* seeds = reinterpret_cast<float*>(uni + MK_UNI_RESERVED + (size_t)lin.KG * M * XW * 4);
             float* red = seeds + (size_t)lin.KG * 4 * SEEDF;
             ok = cta_wait(a, arrivals * C, mm);
             if (!ok) break;
@@ -866,8 +872,8 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
         // ---- down + residual
         {
             const MkLin lin = Ly.lin[K_DOWN];
-            uint32_t* xs = reinterpret_cast<uint32_t*>(uni);
-            float* seeds = reinterpret_cast<float*>(uni + (size_t)lin.KG * M * XW * 4);
+            uint32_t* xs = reinterpret_cast<uint32_t*>(uni + MK_UNI_RESERVED);
+            float* seeds = reinterpret_cast<float*>(uni + MK_UNI_RESERVED + (size_t)lin.KG * M * XW * 4);
             float* red = seeds + (size_t)lin.KG * 4 * SEEDF;
             ok = cta_wait(a, arrivals * C, mm);
             if (!ok) break;
@@ -883,8 +889,8 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
     if (ok && a.logits_rows > 0) {
         const MkLin lin = a.lm;
         const int rows = a.logits_rows;
-        uint32_t* xs = reinterpret_cast<uint32_t*>(uni);
-        float* seeds = reinterpret_cast<float*>(uni + (size_t)lin.KG * rows * XW * 4);
+        uint32_t* xs = reinterpret_cast<uint32_t*>(uni + MK_UNI_RESERVED);
+        float* seeds = reinterpret_cast<float*>(uni + MK_UNI_RESERVED + (size_t)lin.KG * rows * XW * 4);
         float* red = seeds + (size_t)lin.KG * 4 * SEEDF;
         ok = cta_wait(a, arrivals * C, mm);
         if (ok) {
@@ -1140,6 +1146,9 @@ void mk_prepare(qw_model* m) {
 
 namespace {
 
+static_assert(offsetof(attn::DecSmem<8>, tbar) + sizeof(uint64_t) * 2 <= MK_UNI_RESERVED,
+              "attention mbarriers must sit in the reserved head of the union");
+
 template <int RMAX>
 size_t mk_union_bytes(const MkState* s, int M, int rows, int C) {
     size_t u = sizeof(attn::DecSmem<RMAX>);
@@ -1148,8 +1157,8 @@ size_t mk_union_bytes(const MkState* s, int M, int rows, int C) {
         return (size_t)lin.KG * Mx * XW * 4 + (size_t)lin.KG * 4 * SEEDF * 4 +
                (size_t)MK_NW * lin.seg_stride * lin.R16 * 512 + (norm ? (size_t)lin.KG * Mx * 4 * 4 : 0);
     };
-    for (int k = 0; k < 4; ++k) u = std::max(u, need(s->layers[0].lin[k], M, k == K_QKV || k == K_GU));
-    if (rows > 0) u = std::max(u, need(s->lm, rows, true));
+    for (int k = 0; k < 4; ++k) u = std::max(u, MK_UNI_RESERVED + need(s->layers[0].lin[k], M, k == K_QKV || k == K_GU));
+    if (rows > 0) u = std::max(u, MK_UNI_RESERVED + need(s->lm, rows, true));
     return (u + 127) & ~(size_t)127;
 }
 
@@ -1185,7 +1194,10 @@ bool mk_launch_t(qw_model* m, MkArgs& a, cudaStream_t st, int slot_idx) {
     const size_t misc = misc_struct + (((size_t)np * sizeof(PhaseInfo) + 127) & ~(size_t)127);
     const long long room = (long long)max_smem - (long long)uni - (long long)misc;
     const long long per_depth = (long long)MK_NW * GR_BYTES;
-    const int depth = room >= 16 * per_depth ? 16 : (room >= 8 * per_depth ? 8 : 0);
+    int depth = room >= 16 * per_depth ? 16 : (room >= 8 * per_depth ? 8 : 0);
+    // QW_MK_DEPTH=8 caps the ring depth (profiling / testing both kernel forms)
+    if (const char* e = std::getenv("QW_MK_DEPTH"))
+        if (std::atoi(e) == 8 && depth == 16) depth = 8;
     if (depth == 0) return false;
     a.depth = depth;
     a.off_union = (unsigned)((size_t)MK_NW * depth * GR_BYTES);  // a multiple of 128

@@ -69,6 +69,16 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def tensor_peak():
+    """Dense bf16 tensor peak for a kernel timed in isolation (burst figure)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled during the timed region."""
 
@@ -242,6 +252,50 @@ def qgemv_roofline(q, torch, info, peak_gbs):
     return achieved, len(launches), total_bytes / len(launches)
 
 
+def qgemm_roofline(q, torch, info, M=2048):
+    """Time the multi-row quantized matmul (the tcgen05 prefill GEMM, with its
+    bf16 -> fp16 activation conversion) over one layer's Qwen3-4B shapes at
+    M = 2048 rows; the four shapes' operands (~220 MB) exceed L2.  Returns
+    achieved TFLOP/s (2*M*N*K per matmul) and the per-shape times."""
+    lib = q.lib()
+    dev = torch.device("cuda")
+    H, I = info.hidden, info.intermediate
+    QD, KD = info.num_heads * info.head_dim, info.num_kv_heads * info.head_dim
+    shapes = [(H, QD + 2 * KD), (QD, H), (H, I), (I, H)]
+    bufs = []
+    for K, N in shapes:
+        w = torch.randint(-2 ** 31, 2 ** 31 - 1, (N, K // 8), dtype=torch.int32, device=dev)
+        s = (torch.rand(N, K // 64, device=dev) * 0.01).to(torch.bfloat16)
+        b = (torch.rand(N, K // 64, device=dev) * -0.01).to(torch.bfloat16)
+        x = torch.randn(M, K, device=dev).to(torch.bfloat16)
+        y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        bufs.append((x, w, s, b, y, N, K))
+    st = torch.cuda.Stream()
+    per = []
+    with torch.cuda.stream(st):
+        def one(x, w, s, b, y, N, K):
+            q.check(lib.qw_quantized_matmul(x.data_ptr(), w.data_ptr(), s.data_ptr(), b.data_ptr(), y.data_ptr(),
+                                            M, N, K, 64, 4, st.cuda_stream))
+        for bb in bufs:
+            for _ in range(3):
+                one(*bb)
+        torch.cuda.synchronize()
+        reps = 5
+        for bb in bufs:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(reps):
+                one(*bb)
+            e1.record(st)
+            torch.cuda.synchronize()
+            per.append(e0.elapsed_time(e1) / reps)
+    flops = sum(2.0 * M * N * K for (K, N) in shapes)
+    sec = sum(per) / 1e3
+    del bufs
+    torch.cuda.empty_cache()
+    return flops / sec / 1e12, per, shapes
+
+
 def launches_per_generation(info, prompt_len, decode_tokens):
     """Kernels the library launches for one greedy generation (for gpu_launches):
     the prefill runs the kernel chain (embed; per layer 2 rmsnorm, 4 qgemm,
@@ -339,6 +393,13 @@ def run_ours(args):
                 "bytes_per_launch": int(w_bytes + kv_bytes), "launches_timed": int(dec_tokens),
                 "bytes_note": "quantized weights (0.5625 B/param) + bf16 K/V read at the mean KV length 662",
                 "peak_source": peak_kind}
+        tf, per_ms, shp = qgemm_roofline(q, torch, info)
+        tpk, tpk_kind = tensor_peak()
+        extra["qgemm_roofline"] = {"bound": "tensor", "achieved": round(tf, 1), "peak": tpk, "unit": "TFLOP/s",
+                                   "frac": round(tf / tpk, 4), "peak_source": tpk_kind,
+                                   "kernel": "qgemm_tc_kernel (tcgen05 prefill GEMM) + x_to_f16p_kernel, "
+                                             "qw_quantized_matmul M=2048 over the 4B layer shapes",
+                                   "ms_per_shape": {f"K{K}xN{N}": round(t, 4) for (K, N), t in zip(shp, per_ms)}}
         extra["qgemv_roofline"] = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
                                    "frac": round(ach / peak, 4),
                                    "kernel": "qw_quantized_matmul (standalone op, M=1), 4B layer shapes + lm_head",
@@ -395,6 +456,25 @@ def spec_measure(q, target, prompt, cfg4):
     return out
 
 
+def profile_qmm(spec: str) -> None:
+    """ncu workload: three qw_quantized_matmul calls of one shape "M,K,N"."""
+    import torch
+    import qwen3_b200 as q
+    M, K, N = (int(v) for v in spec.split(","))
+    dev = torch.device("cuda")
+    g = torch.Generator(device="cpu").manual_seed(SEED)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(dev)
+    w = torch.randint(-2 ** 31, 2 ** 31 - 1, (N, K // 8), dtype=torch.int64, generator=g).to(torch.int32).to(dev)
+    s = (torch.rand(N, K // 64, generator=g) * 0.01 + 0.001).to(torch.bfloat16).to(dev)
+    b = (-torch.rand(N, K // 64, generator=g) * 0.05).to(torch.bfloat16).to(dev)
+    y = torch.zeros(M, N, dtype=torch.bfloat16, device=dev)
+    st = torch.cuda.current_stream().cuda_stream
+    for _ in range(3):
+        q.quantized_matmul(x.data_ptr(), w.data_ptr(), s.data_ptr(), b.data_ptr(), y.data_ptr(), M, N, K, stream=st)
+    torch.cuda.synchronize()
+    print(f"profile_qmm: M={M} K={K} N={N} max|y| {float(y.float().abs().max())}")
+
+
 def profile_decode(n: int, model: str) -> None:
     """Prefill and n decode steps, one qw_forward each (the ncu workloads): the
     bench model (Qwen3-4B, 512-token prompt) or, for captures that must stay
@@ -426,10 +506,14 @@ def main():
                     help="profiling workload for ncu: weight init, the prefill and N greedy decode steps through "
                          "qw_forward; prints no bench line")
     ap.add_argument("--profile-model", choices=["4b", "0.6b"], default="4b")
+    ap.add_argument("--profile-qmm", default="", metavar="M,K,N",
+                    help="profiling workload for ncu: three quantized matmuls of one shape; prints no bench line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.profile_decode > 0:
+    if args.profile_qmm:
+        profile_qmm(args.profile_qmm)
+    elif args.profile_decode > 0:
         profile_decode(args.profile_decode, args.profile_model)
     elif args.impl == "reference":
         run_reference(args)
