@@ -161,6 +161,13 @@ int qw_model_stream(const qw_model* m, void** s) {
     });
 }
 
+int qw_tp_unique_id(void* out, size_t bytes) {
+    return guard([&] {
+        need(out, "out");
+        qw::tp_unique_id(out, bytes);
+    });
+}
+
 int qw_model_tp_attach(qw_model* m, const void* uid, int rank, int size) {
     return guard([&] {
         need(m && uid, "model/id");

@@ -150,8 +150,8 @@ QW_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 // global -> shared bulk copy (16-byte aligned addresses, size a multiple of 16),
-// completion counted on `bar` in bytes.  Non-multicast: the source is always
-// this GPU's own memory.
+// completion counted on `bar` in bytes.  One destination CTA; the source is
+// always this GPU's own memory.
 QW_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),

@@ -170,6 +170,7 @@ void spec_generate_dev(qw_model* target, qw_model* draft, const SpecRequest& r, 
                        qw_spec_stats* stats);
 
 // tp.cu
+void tp_unique_id(void* out, size_t bytes);
 void tp_attach(qw_model* m, const void* unique_id, int rank, int size);
 void tp_allreduce_sum_f32(qw_model* m, float* buf, size_t count, cudaStream_t st);
 void tp_allreduce_max_u64(qw_model* m, unsigned long long* buf, size_t count, cudaStream_t st);

@@ -113,8 +113,8 @@ QW_DEV bool tc_wait(uint64_t* bar, uint32_t parity) {
 QW_DEV void tc_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-// 2-D TMA tensor load into this CTA's shared memory (no multicast: the source
-// is this GPU's own memory), completion counted on `bar` in bytes.
+// 2-D TMA tensor load into this CTA's own shared memory only, from this GPU's
+// own memory; completion counted on `bar` in bytes.
 QW_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(

@@ -25,16 +25,31 @@ struct TpComm {
     const char* (*errstr)(ncclResult_t) = nullptr;
 };
 
+static void* nccl_lib() {
+    const char* names[] = {"libnccl.so.2", "libnccl.so"};
+    for (const char* n : names)
+        if (void* h = dlopen(n, RTLD_NOW | RTLD_GLOBAL)) return h;
+    return nullptr;
+}
+
+void tp_unique_id(void* out, size_t bytes) {
+    if (bytes < sizeof(ncclUniqueId)) throw Error(QW_ERR_INVALID_ARG, "unique id buffer smaller than 128 bytes");
+    void* lib = nccl_lib();
+    if (!lib) throw Error(QW_ERR_CUDA, "cannot dlopen libnccl.so.2");
+    auto get = (ncclResult_t(*)(ncclUniqueId*))dlsym(lib, "ncclGetUniqueId");
+    if (!get) throw Error(QW_ERR_CUDA, "libnccl is missing ncclGetUniqueId");
+    ncclUniqueId id;
+    const ncclResult_t r = get(&id);
+    if (r != ncclSuccess) throw Error(QW_ERR_CUDA, "ncclGetUniqueId failed");
+    std::memcpy(out, &id, sizeof(id));
+}
+
 void tp_attach(qw_model* m, const void* unique_id, int rank, int size) {
     if (size != m->tp_size || rank != m->tp_rank)
         throw Error(QW_ERR_INVALID_ARG, "tp rank/size differ from the ones the model was loaded with");
     if (m->tp) throw Error(QW_ERR_INVALID_ARG, "communicator already attached");
     auto* t = new TpComm();
-    const char* names[] = {"libnccl.so.2", "libnccl.so"};
-    for (const char* n : names) {
-        t->lib = dlopen(n, RTLD_NOW | RTLD_GLOBAL);
-        if (t->lib) break;
-    }
+    t->lib = nccl_lib();
     if (!t->lib) {
         delete t;
         throw Error(QW_ERR_CUDA, "cannot dlopen libnccl.so.2");

@@ -114,6 +114,7 @@ SIGNATURES = {
     "qw_model_export_tensor": [P, ctypes.c_char_p, P, ctypes.c_size_t],
     "qw_model_stream": [P, ctypes.POINTER(P)],
     "qw_model_tp_attach": [P, P, I, I],
+    "qw_tp_unique_id": [P, ctypes.c_size_t],
     "qw_check_compatible": [P, P],
     "qw_cache_new": [P, I, ctypes.POINTER(P)],
     "qw_cache_free": [P],
@@ -303,6 +304,33 @@ class Qwen3:
                                        ctypes.byref(st)))
         return GenerationResult([int(t) for t in out[:n.value]], st.prompt_tokens, st.completion_tokens,
                                 "stop" if st.finish_reason == 1 else "length", st.prefill_ms, st.decode_ms)
+
+
+def tp_unique_id() -> bytes:
+    """A fresh NCCL unique id (128 bytes) for a tensor-parallel group."""
+    buf = ctypes.create_string_buffer(128)
+    check(lib().qw_tp_unique_id(ctypes.cast(buf, P), 128))
+    return buf.raw
+
+
+def tp_share_unique_id(rank: int, group=None, make_id=None) -> bytes:
+    """Rank 0 creates the group's NCCL id, every rank returns it: the host-side
+    exchange through an initialised torch.distributed process group (any
+    backend; gloo suffices, the tensor traffic itself goes through NCCL inside
+    the library).  `make_id` replaces tp_unique_id (tests without NCCL)."""
+    import torch.distributed as dist
+    obj = [(make_id or tp_unique_id)() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0, group=group)
+    uid = obj[0]
+    if not isinstance(uid, (bytes, bytearray)) or len(uid) != 128:
+        raise Inference(-1, "tensor-parallel unique id exchange returned a malformed id")
+    return bytes(uid)
+
+
+def tp_init(model: "Qwen3", rank: int, size: int, group=None) -> None:
+    """Attach the NCCL communicator of a tensor-parallel group of `size` ranks
+    (one process per GPU, model loaded with tp_rank=rank, tp_size=size)."""
+    model.tp_attach(tp_share_unique_id(rank, group), rank, size)
 
 
 def check_compatible(target: Qwen3, draft: Qwen3) -> None:

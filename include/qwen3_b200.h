@@ -111,6 +111,11 @@ QW_API int qw_model_export_tensor(const qw_model* m, const char* name, void* dst
 /* The CUDA stream the model's work runs on (cudaStream_t as void*). */
 QW_API int qw_model_stream(const qw_model* m, void** stream_out);
 
+/* Tensor parallel (no reference counterpart: base-mlx has no distributed path).
+ * qw_tp_unique_id writes a fresh NCCL unique id (128 bytes) for rank 0 to share
+ * with the other ranks (any host channel: torch.distributed, a file, MPI). */
+QW_API int qw_tp_unique_id(void* out, size_t bytes);
+
 /* Tensor parallel: attach an NCCL communicator (ncclUniqueId bytes, 128) to a
  * model loaded with tp_size > 1.  Must be called on every rank before forward. */
 QW_API int qw_model_tp_attach(qw_model* m, const void* nccl_unique_id, int rank, int size);
