@@ -31,7 +31,9 @@
 // boundaries, since weights never depend on activations -- through a private
 // ring of shared-memory slots with 16-byte cp.async copies, `depth` granules
 // ahead of the one it computes, so HBM keeps streaming while the CTA waits at
-// a phase barrier.
+// a phase barrier.  Copies are committed two granules per group: the fixed
+// cost of a commit/wait pair per granule held a copy-only stream near half
+// the HBM rate.
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -214,13 +216,17 @@ struct Cursor {
     }
 };
 
-// Issue the copies of the producer cursor's granule into `slot` (one commit
-// group per granule; an empty group once the stream has ended).
-QW_DEV void issue_granule(Cursor& pc, int warp, int lane, unsigned char* slot) {
-    if (!pc.done()) {
-        cp_async16(slot + 16 * lane, pc.p + 16 * lane);
-        if (lane < 4) cp_async16(slot + 512 + 16 * lane, pc.p + 512 + 16 * lane);
-        pc.advance(warp);
+// Issue the copies of the producer cursor's next two granules into the slot
+// pair at `dst` (one commit group per pair; fewer granules, or an empty group,
+// once the stream has ended).  Every lane walks the cursor in lockstep.
+QW_DEV void issue_pair(Cursor& pc, int warp, int lane, unsigned char* dst) {
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        if (!pc.done()) {
+            cp_async16(dst + u * GR_BYTES + 16 * lane, pc.p + 16 * lane);
+            if (lane < 4) cp_async16(dst + u * GR_BYTES + 512 + 16 * lane, pc.p + 512 + 16 * lane);
+            pc.advance(warp);
+        }
     }
     cp_async_commit();
 }
@@ -561,8 +567,9 @@ QW_DEV void store_elem(const MkArgs& a, bool lm, int row, int m, const float (&v
 // CTA that finishes a split tile.
 template <int KIND, int DEPTH>
 QW_DEV void gemv_phase(const MkArgs& a, const PhaseInfo& P, int Mx, uint32_t* xs, float* seeds, float* red,
-                       Cursor& pc, int& slot, unsigned char* ring, bool lm, MkMisc& mm) {
+                       Cursor& pc, unsigned& gpos, unsigned char* ring, bool lm, MkMisc& mm) {
     constexpr int R16 = KIND == K_GU ? 2 : 1;
+    constexpr int NS = DEPTH / 2;  // slot pairs per warp, one commit group each
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int KG = P.KG;
@@ -572,7 +579,9 @@ QW_DEV void gemv_phase(const MkArgs& a, const PhaseInfo& P, int Mx, uint32_t* xs
     const uint32_t* xs_lane = xs + (size_t)mcol * XW + t * 8;
     const float* seeds_lane = seeds + (size_t)t * SEEDF;
     unsigned char* wring = ring + (size_t)warp * DEPTH * GR_BYTES;
-    auto gptr = [&](int u) { return wring + (size_t)((slot + u) & (DEPTH - 1)) * GR_BYTES; };
+    auto gptr = [&](int u) { return wring + (size_t)((gpos + u) & (DEPTH - 1)) * GR_BYTES; };
+    // refill the slot pair of chunk c (granules 2c, 2c+1) with the chunk NS ahead
+    auto refill = [&](unsigned c) { issue_pair(pc, warp, lane, wring + (size_t)(c % NS) * 2 * GR_BYTES); };
 
     int wa, wb;
     warp_range(P, warp, wa, wb);
@@ -590,7 +599,11 @@ QW_DEV void gemv_phase(const MkArgs& a, const PhaseInfo& P, int Mx, uint32_t* xs
         int gi = 0;
         // four granules per step: independent mma chains in flight
         for (; gi + 4 <= ng; gi += 4) {
-            cp_async_wait<DEPTH - 4>();
+            // groups newer than the last pair these four granules touch may stay pending
+            if ((gpos & 1) == 0)
+                cp_async_wait<NS - 2>();
+            else
+                cp_async_wait<NS - 3>();
             __syncwarp();
             if (R16 == 1) {
                 const int gl = gl0 + gi;
@@ -612,13 +625,18 @@ QW_DEV void gemv_phase(const MkArgs& a, const PhaseInfo& P, int Mx, uint32_t* xs
                 granule_mma(gptr(3), lane, x1, acc[3]);
             }
             __syncwarp();
-            // refill the four slots with the granules `DEPTH` ahead
-#pragma unroll
-            for (int u = 0; u < 4; ++u) issue_granule(pc, warp, lane, gptr(u));
-            slot = (slot + 4) & (DEPTH - 1);
+            // refill the two pairs whose second granule was just consumed
+            if ((gpos & 1) == 0) {
+                refill(gpos / 2);
+                refill(gpos / 2 + 1);
+            } else {
+                refill((gpos - 1) / 2);
+                refill((gpos + 1) / 2);
+            }
+            gpos += 4;
         }
         for (; gi < ng; ++gi) {
-            cp_async_wait<DEPTH - 1>();
+            if ((gpos & 1) == 0) cp_async_wait<NS - 1>();
             __syncwarp();
             const GAct x0 = load_act(xs_lane, seeds_lane, gl0 + gi / R16, col_stride);
             if ((gi & 3) == 0) granule_mma(gptr(0), lane, x0, acc[0]);
@@ -626,8 +644,8 @@ QW_DEV void gemv_phase(const MkArgs& a, const PhaseInfo& P, int Mx, uint32_t* xs
             else if ((gi & 3) == 2) granule_mma(gptr(0), lane, x0, acc[2]);
             else granule_mma(gptr(0), lane, x0, acc[3]);
             __syncwarp();
-            issue_granule(pc, warp, lane, gptr(0));
-            slot = (slot + 1) & (DEPTH - 1);
+            if (gpos & 1) refill((gpos - 1) / 2);
+            gpos += 1;
         }
         // partial accumulators combined in a fixed order (sub-tile = granule parity)
         float* r0 = red + ((size_t)(warp * seg_stride + seg) * R16 * 32 + lane) * 4;
@@ -772,8 +790,8 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
     // prime the ring: `depth` granules per warp in flight
     Cursor pc;
     pc.init(tab, np, warp);
-    for (int i = 0; i < DEPTH; ++i) issue_granule(pc, warp, lane, ring + ((size_t)warp * DEPTH + i) * GR_BYTES);
-    int slot = 0;
+    for (int i = 0; i < DEPTH / 2; ++i) issue_pair(pc, warp, lane, ring + ((size_t)warp * DEPTH + 2 * i) * GR_BYTES);
+    unsigned gpos = 0;
     __syncthreads();
 
     const int M = a.M;
@@ -807,7 +825,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
                 }
             }
             __syncthreads();
-            gemv_phase<K_QKV, DEPTH>(a, tab[4 * l + K_QKV], M, xs, seeds, red, pc, slot, ring, false, mm);
+            gemv_phase<K_QKV, DEPTH>(a, tab[4 * l + K_QKV], M, xs, seeds, red, pc, gpos, ring, false, mm);
             // the attention tiles' cached K/V rows do not depend on this step:
             // start loading them before waiting for the other CTAs' q|k|v
             __syncthreads();
@@ -850,7 +868,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
             StageSrc s{a.attn, a.QD, 0, nullptr};
             stage_acts(a, s, a.QD, M, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
             __syncthreads();
-            gemv_phase<K_O, DEPTH>(a, tab[4 * l + K_O], M, xs, seeds, red, pc, slot, ring, false, mm);
+            gemv_phase<K_O, DEPTH>(a, tab[4 * l + K_O], M, xs, seeds, red, pc, gpos, ring, false, mm);
             cta_arrive(a);
             ++arrivals;
         }
@@ -865,7 +883,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
             StageSrc s{a.x, a.H, 0, Ly.post_norm};
             stage_acts(a, s, a.H, M, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
             __syncthreads();
-            gemv_phase<K_GU, DEPTH>(a, tab[4 * l + K_GU], M, xs, seeds, red, pc, slot, ring, false, mm);
+            gemv_phase<K_GU, DEPTH>(a, tab[4 * l + K_GU], M, xs, seeds, red, pc, gpos, ring, false, mm);
             cta_arrive(a);
             ++arrivals;
         }
@@ -880,7 +898,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
             StageSrc s{a.mlp, a.I, 0, nullptr};
             stage_acts(a, s, a.I, M, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
             __syncthreads();
-            gemv_phase<K_DOWN, DEPTH>(a, tab[4 * l + K_DOWN], M, xs, seeds, red, pc, slot, ring, false, mm);
+            gemv_phase<K_DOWN, DEPTH>(a, tab[4 * l + K_DOWN], M, xs, seeds, red, pc, gpos, ring, false, mm);
             cta_arrive(a);
             ++arrivals;
         }
@@ -897,7 +915,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
             StageSrc s{a.x, a.H, M - rows, a.final_norm};
             stage_acts(a, s, a.H, rows, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
             __syncthreads();
-            gemv_phase<K_O, DEPTH>(a, tab[4 * a.L], rows, xs, seeds, red, pc, slot, ring, true, mm);
+            gemv_phase<K_O, DEPTH>(a, tab[4 * a.L], rows, xs, seeds, red, pc, gpos, ring, true, mm);
         }
     }
     // no copy may still be landing in shared memory when the CTA exits
