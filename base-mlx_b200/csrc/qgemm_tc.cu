@@ -4,7 +4,7 @@
 // 64, 4) as called from crates/base-mlx-core/src/model/qwen3.rs:30-41 and
 // model/kernels.rs:42-44,69-76 during prefill and forward_multi).
 //
-// Tile: 128 output features (the MMA M) x 128 activation rows (the MMA N), fp32
+// Tile: 128 output features (the MMA M) x 128 or 256 activation rows (the MMA N), fp32
 // accumulators in tensor memory (TMEM), K walked one 64-wide quantization group
 // per stage.  Operands are fp16, K-major, in the 128-byte-swizzled canonical
 // layout (one 128-byte row per tile row, its eight 16-byte chunks XOR-permuted
@@ -37,6 +37,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -49,7 +50,7 @@ namespace qw {
 namespace {
 
 constexpr int TC_BM = 128;            // output features per tile (MMA M)
-constexpr int TC_BN = 128;            // activation rows per tile (MMA N)
+constexpr int TC_BN_MAX = 256;        // activation rows per tile (MMA N): 128 or 256
 constexpr int TC_PT = 256;            // producer threads (warps 0-7)
 constexpr int TC_NT = TC_PT + 64;     // + MMA warp + TMA warp
 constexpr int TC_LMAX = 8;            // deepest load ring
@@ -61,18 +62,18 @@ constexpr unsigned long long TC_TIMEOUT_NS = 2000000000ull;
 //   A ring   2 x RT x 16 KB   dequantized weights (fp16, swizzled)
 //   SB ring  2 x RT x 4 KB    scales [128][8] bf16 then biases [128][8] bf16
 //   load ring L x (16 KB activations + RT x 4 KB packed words)
-template <int RT>
+template <int RT, int BN>
 struct TcPlan {
     static constexpr int A_TILE = TC_BM * 128;
     static constexpr int A_OFF = 1024;
     static constexpr int SB_OFF = A_OFF + 2 * RT * A_TILE;
     static constexpr int SB_SLOT = RT * 4096;
     static constexpr int LD_OFF = SB_OFF + 2 * SB_SLOT;
-    static constexpr int LD_SLOT = TC_BN * 128 + RT * 4096;
+    static constexpr int LD_SLOT = BN * 128 + RT * 4096;
     static constexpr int L = (TC_SMEM_MAX - 1024 - LD_OFF) / LD_SLOT > TC_LMAX ? TC_LMAX
                                                                                 : (TC_SMEM_MAX - 1024 - LD_OFF) / LD_SLOT;
     static constexpr int SMEM = LD_OFF + L * LD_SLOT + 1024;  // + base alignment slack
-    static constexpr uint32_t TMEM_COLS = RT * TC_BN;
+    static constexpr uint32_t TMEM_COLS = RT * BN;
 };
 
 // TMA tensor maps of one launch: activations, then per segment the packed
@@ -83,9 +84,11 @@ struct TcMaps {
 };
 
 // Instruction descriptor (kind::f16): fp32 accumulate, fp16 A and B, both
-// K-major, N = TC_BN, M = TC_BM.
-constexpr uint32_t TC_IDESC = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(TC_BN >> 3) << 17) |
-                              ((uint32_t)(TC_BM >> 4) << 24);
+// K-major, N = BN, M = TC_BM.
+template <int BN>
+__host__ __device__ constexpr uint32_t tc_idesc() {
+    return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
+}
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 1 KB between
 // 8-row groups, descriptor version 1.  A K-step of 16 elements inside the
@@ -126,13 +129,14 @@ QW_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" 
 QW_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 QW_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
+template <int BN>
 QW_DEV void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
     const uint32_t z = 0u;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(TC_IDESC), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z)
+        "l"(adesc), "l"(bdesc), "r"(tc_idesc<BN>()), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z)
         : "memory");
 }
 QW_DEV void tc_commit(uint64_t* bar) {
@@ -155,9 +159,9 @@ QW_DEV void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "me
 // (1024 + q_j, 1024 + q_{j+4}) as an fp16 pair, q_j = nibble j of w
 QW_DEV uint32_t nib_f16x2(uint32_t w) { return (w & 0x000F000Fu) | 0x64006400u; }
 
-template <int RT>
+template <int RT, int BN>
 __global__ void __launch_bounds__(TC_NT, 1) qgemm_tc_kernel(const QmmArgs a, const __grid_constant__ TcMaps maps) {
-    using P = TcPlan<RT>;
+    using P = TcPlan<RT, BN>;
     constexpr int L = P::L;
     extern __shared__ unsigned char tc_smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)tc_smem_raw + 1023) & ~(uintptr_t)1023);
@@ -172,7 +176,7 @@ __global__ void __launch_bounds__(TC_NT, 1) qgemm_tc_kernel(const QmmArgs a, con
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int KG = a.K / 64;
-    const int rb = blockIdx.x, t0 = blockIdx.y * TC_BN;
+    const int rb = blockIdx.x, t0 = blockIdx.y * BN;
 
     // segment of this row block (q | k | v of the fused qkv launch, or one)
     int si = 0;
@@ -184,7 +188,7 @@ __global__ void __launch_bounds__(TC_NT, 1) qgemm_tc_kernel(const QmmArgs a, con
     auto A_of = [&](int slot, int rt) { return smem + P::A_OFF + (slot * RT + rt) * P::A_TILE; };
     auto SB_of = [&](int slot, int rt) { return smem + P::SB_OFF + slot * P::SB_SLOT + rt * 4096; };
     auto X_of = [&](int slot) { return smem + P::LD_OFF + slot * P::LD_SLOT; };
-    auto W_of = [&](int slot, int rt) { return smem + P::LD_OFF + slot * P::LD_SLOT + TC_BN * 128 + rt * 4096; };
+    auto W_of = [&](int slot, int rt) { return smem + P::LD_OFF + slot * P::LD_SLOT + BN * 128 + rt * 4096; };
 
     if (tid == 0) {
         for (int s = 0; s < L; ++s) {
@@ -266,7 +270,7 @@ __global__ void __launch_bounds__(TC_NT, 1) qgemm_tc_kernel(const QmmArgs a, con
                     const uint32_t ab = smem_u32(A_of(as, rt));
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
-                        tc_mma(tmem + rt * TC_BN, tc_sdesc_sw128(ab + 32 * j), tc_sdesc_sw128(xb + 32 * j),
+                        tc_mma<BN>(tmem + rt * BN, tc_sdesc_sw128(ab + 32 * j), tc_sdesc_sw128(xb + 32 * j),
                                (gi | j) != 0 ? 1u : 0u);
                 }
                 tc_commit(a_empty + as);
@@ -305,7 +309,7 @@ __global__ void __launch_bounds__(TC_NT, 1) qgemm_tc_kernel(const QmmArgs a, con
                 ok = false;
                 break;
             }
-            mbar_arrive_expect_tx(ld_full + ls, TC_BN * 128 + RT * 4096);
+            mbar_arrive_expect_tx(ld_full + ls, BN * 128 + RT * 4096);
             tma_load_2d(X_of(ls), &maps.x, gi * 64, t0, ld_full + ls);
 #pragma unroll
             for (int rt = 0; rt < RT; ++rt) tma_load_2d(W_of(ls, rt), wmap[rt], gi * 8, n0, ld_full + ls);
@@ -321,11 +325,11 @@ __global__ void __launch_bounds__(TC_NT, 1) qgemm_tc_kernel(const QmmArgs a, con
         const int n = n0 + 32 * lq + lane;
         const bool nvalid = n < a.seg[RT == 2 ? 0 : si].n;
 #pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
-            const int c0 = ch * 64 + cc * 16;
+        for (int cc = 0; cc < BN / 32; ++cc) {
+            const int c0 = ch * (BN / 2) + cc * 16;
             float v[RT][16];
 #pragma unroll
-            for (int rt = 0; rt < RT; ++rt) tc_ld16(tmem + ((uint32_t)(32 * lq) << 16) + rt * TC_BN + c0, v[rt]);
+            for (int rt = 0; rt < RT; ++rt) tc_ld16(tmem + ((uint32_t)(32 * lq) << 16) + rt * BN + c0, v[rt]);
             tc_wait_ld();
             if (ok && nvalid) {
 #pragma unroll
@@ -449,21 +453,21 @@ bool seg_maps(const QSeg& sg, int K, SegMaps& out) {
     return true;
 }
 
-template <int RT>
+template <int RT, int BN>
 cudaError_t launch_tc_t(const QmmArgs& a, const TcMaps& maps, dim3 grid, cudaStream_t st) {
     static bool set = false;
     if (!set) {
-        const cudaError_t e =
-            cudaFuncSetAttribute(qgemm_tc_kernel<RT>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcPlan<RT>::SMEM);
+        const cudaError_t e = cudaFuncSetAttribute(qgemm_tc_kernel<RT, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   TcPlan<RT, BN>::SMEM);
         if (e != cudaSuccess) return e;
         set = true;
     }
-    return launch_pdl(qgemm_tc_kernel<RT>, grid, dim3(TC_NT), (size_t)TcPlan<RT>::SMEM, st, a, maps);
+    return launch_pdl(qgemm_tc_kernel<RT, BN>, grid, dim3(TC_NT), (size_t)TcPlan<RT, BN>::SMEM, st, a, maps);
 }
 
 }  // namespace
 
-size_t qgemm_tc_scratch_bytes(int M, int K) { return (size_t)((M + TC_BN - 1) / TC_BN) * TC_BN * K * 2; }
+size_t qgemm_tc_scratch_bytes(int M, int K) { return (size_t)((M + TC_BN_MAX - 1) / TC_BN_MAX) * TC_BN_MAX * K * 2; }
 
 bool qgemm_tc_supported(const QmmArgs& a) {
     if (a.M < 9 || a.K < 128 || a.K % 128 != 0 || a.nseg < 1 || a.nseg > 3) return false;
@@ -482,7 +486,9 @@ bool qgemm_tc_supported(const QmmArgs& a) {
 
 cudaError_t launch_qgemm_tc(QmmArgs a, void* scratch, size_t scratch_bytes, cudaStream_t st) {
     if (!qgemm_tc_supported(a)) return cudaErrorInvalidValue;
-    const int Mpad = (a.M + TC_BN - 1) / TC_BN * TC_BN;
+    // 256 activation rows per tile when that still gives every SM a tile, else 128
+    // (QW_TC_BN=128|256 forces one); x is padded to a multiple of 256 rows either way
+    const int Mpad = (a.M + TC_BN_MAX - 1) / TC_BN_MAX * TC_BN_MAX;
     if (!scratch || scratch_bytes < qgemm_tc_scratch_bytes(a.M, a.K)) return cudaErrorInvalidValue;
     __half* xh = static_cast<__half*>(scratch);
     int nrb = 0;
@@ -501,9 +507,11 @@ cudaError_t launch_qgemm_tc(QmmArgs a, void* scratch, size_t scratch_bytes, cuda
     const int cblocks = (int)std::min<long long>((chunks + 255) / 256, 148 * 8);
     cudaError_t e = launch_pdl(x_to_f16p_kernel, dim3(cblocks), dim3(256), 0, st, a.x, a.ldx, a.M, Mpad, a.K, xh);
     if (e != cudaSuccess) return e;
+    int BN = (long long)nrb * (Mpad / 256) >= 148 ? 256 : 128;
+    if (const char* e = std::getenv("QW_TC_BN")) BN = std::atoi(e) == 256 ? 256 : 128;
     TcMaps maps;
     std::memset(&maps, 0, sizeof(maps));
-    if (!make_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh, a.K, Mpad, 64, TC_BN, CU_TENSOR_MAP_SWIZZLE_128B))
+    if (!make_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh, a.K, Mpad, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
     for (int i = 0; i < a.nseg; ++i) {
         SegMaps sm;
@@ -512,9 +520,13 @@ cudaError_t launch_qgemm_tc(QmmArgs a, void* scratch, size_t scratch_bytes, cuda
         maps.s[i] = sm.s;
         maps.b[i] = sm.b;
     }
-    const dim3 grid(nrb, Mpad / TC_BN);
-    if (a.epi == EPI_SWIGLU) return launch_tc_t<2>(a, maps, grid, st);
-    return launch_tc_t<1>(a, maps, grid, st);
+    const dim3 grid(nrb, (a.M + BN - 1) / BN);
+    if (BN == 256) {
+        if (a.epi == EPI_SWIGLU) return launch_tc_t<2, 256>(a, maps, grid, st);
+        return launch_tc_t<1, 256>(a, maps, grid, st);
+    }
+    if (a.epi == EPI_SWIGLU) return launch_tc_t<2, 128>(a, maps, grid, st);
+    return launch_tc_t<1, 128>(a, maps, grid, st);
 }
 
 }  // namespace qw

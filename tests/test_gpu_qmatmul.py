@@ -67,3 +67,13 @@ def test_qmatmul_lm_head_m1():
     x, w, s, b = _case(1, 2560, 151936, seed=5)
     ref = nm.bf16_round(x @ nm.dequantize(w, s, b).T)
     _check(_run_gpu(x, w, s, b), ref)
+
+
+@pytest.mark.parametrize("bn", ["128", "256"])
+@pytest.mark.parametrize("M,K,N", [(300, 1024, 384), (513, 2560, 200)])
+def test_qmatmul_tc_tile_widths(bn, M, K, N, monkeypatch):
+    """Both activation tile widths of the tcgen05 prefill GEMM (ragged M and N)."""
+    monkeypatch.setenv("QW_TC_BN", bn)
+    x, w, s, b = _case(M, K, N, seed=31 + M + N)
+    ref = nm.bf16_round(x @ nm.dequantize(w, s, b).T)
+    _check(_run_gpu(x, w, s, b), ref)
