@@ -325,6 +325,64 @@ int qw_generate_greedy(qw_model* m, const uint32_t* prompt, int n_prompt, int ma
     });
 }
 
+int qw_generate_sampled(qw_model* m, const uint32_t* prompt, int n_prompt, int max_new, float temperature,
+                        float top_p, uint64_t seed, int same_draw, const uint32_t* eos, int n_eos, uint32_t* out,
+                        int* n_out, qw_gen_stats* stats) {
+    if (!(temperature > 0.f))  // engine.rs:197: greedy when temperature <= 0
+        return qw_generate_greedy(m, prompt, n_prompt, max_new, eos, n_eos, out, n_out, stats);
+    return guard([&] {
+        need(m && prompt && out && n_out, "model/prompt/out");
+        need(n_prompt >= 1, "empty prompt");
+        need(top_p == top_p, "top_p is NaN");
+        check_ids(m, prompt, n_prompt);
+        const int mn = std::max(max_new, 1);
+        QW_CUDA(cudaSetDevice(m->device));
+        qw_cache* c = qw::cache_for_generate(m, n_prompt + mn);
+        qw::ensure_workspace(m, n_prompt, 8);
+        cudaStream_t st = m->stream;
+        std::vector<int> h(prompt, prompt + n_prompt);
+        QW_CUDA(cudaMemcpyAsync(m->ws.ids, h.data(), (size_t)n_prompt * 4, cudaMemcpyHostToDevice, st));
+        qw::SampleCfg cfg;
+        std::memset(&cfg, 0, sizeof(cfg));
+        cfg.temperature = temperature;
+        cfg.top_p = top_p;
+        cfg.seed = seed;
+        cfg.same_draw = same_draw ? 1 : 0;
+        qw_gen_stats s;
+        std::memset(&s, 0, sizeof(s));
+        qw::generate_sampled_dev(m, c, n_prompt, mn, eos_list(m, eos, n_eos), cfg, &s, st);
+        const int cnt = std::min(s.completion_tokens, mn);
+        const int written = cnt - (s.finish_reason == 1 ? 1 : 0);
+        std::vector<int> o((size_t)std::max(written, 1));
+        if (written > 0) QW_CUDA(cudaMemcpy(o.data(), m->ws.out, (size_t)written * 4, cudaMemcpyDeviceToHost));
+        for (int i = 0; i < written; ++i) out[i] = (uint32_t)o[i];
+        *n_out = written;
+        if (stats) *stats = s;
+        qw::set_cache_len(c, 0);
+        qw::check_device_err(m);
+    });
+}
+
+int qw_sample_topp(const void* logits, int vocab, float temperature, float top_p, uint64_t seed, uint64_t counter,
+                   void* probs, int32_t* token_out, void* stream) {
+    return guard([&] {
+        need(logits && probs && token_out, "logits/probs/token_out");
+        need(vocab >= 1, "vocab must be positive");
+        need(top_p == top_p && temperature == temperature, "NaN parameter");
+        qw::SampleArgs a;
+        std::memset(&a, 0, sizeof(a));
+        a.logits = (const bf16*)logits;
+        a.V = vocab;
+        a.cfg.temperature = temperature;
+        a.cfg.top_p = top_p;
+        a.cfg.seed = seed;
+        a.probs = (float*)probs;
+        a.counter = counter;
+        a.token_out = token_out;
+        QW_CUDA(qw::launch_sample(a, (cudaStream_t)stream, false));
+    });
+}
+
 int qw_spec_generate(qw_model* target, qw_model* draft, const uint32_t* prompt, int n_prompt, int max_new, int k,
                      float force_p, uint64_t seed, const uint32_t* forced, int n_forced, const uint32_t* eos,
                      int n_eos, uint32_t* out, int* n_out, qw_spec_stats* stats) {

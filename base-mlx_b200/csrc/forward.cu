@@ -273,3 +273,93 @@ void generate_greedy_dev(qw_model* m, qw_cache* c, int n_prompt, int max_new, co
 }
 
 }  // namespace qw
+
+namespace qw {
+
+// LoadedModel::generate_text with temperature > 0 (engine.rs:149-201, pick_next
+// :203-263) as a device loop: prefill with the last row's logits stored, pick
+// on the device, then a captured step {forward of the picked token with its
+// logits stored, pick} replayed max_new - 1 times.  The pick kernel does the
+// loop bookkeeping (EOS, token budget, output list); once it sets `done` the
+// replays' forward steps see the gate and do nothing.
+void generate_sampled_dev(qw_model* m, qw_cache* c, int n_prompt, int max_new, const std::vector<int>& eos,
+                          const SampleCfg& cfg, qw_gen_stats* stats, cudaStream_t st) {
+    Workspace& w = m->ws;
+    if (m->vocab_l != m->cfg.vocab)
+        throw Error(QW_ERR_UNSUPPORTED, "sampled generation needs the whole vocabulary on one rank (untied lm_head "
+                                        "is split under tensor parallelism)");
+    if (n_prompt + max_new > c->max_pos)
+        throw Error(QW_ERR_KV_EXHAUSTED, "KV cache exhausted: requested " + std::to_string(n_prompt + max_new) +
+                                             " positions, max " + std::to_string(c->max_pos));
+    if (max_new > w.out_cap) throw Error(QW_ERR_INVALID_ARG, "max_new too large");
+    StepCtl ctl;
+    std::memset(&ctl, 0, sizeof(ctl));
+    ctl.max_new = max_new;
+    ctl.n_eos = (int)std::min<size_t>(eos.size(), 8);
+    for (int i = 0; i < ctl.n_eos; ++i) ctl.eos[i] = eos[i];
+    QW_CUDA(cudaMemcpyAsync(w.ctl, &ctl, sizeof(ctl), cudaMemcpyHostToDevice, st));
+    QW_CUDA(cudaMemcpyAsync(w.scfg, &cfg, sizeof(cfg), cudaMemcpyHostToDevice, st));
+    int zero = 0;
+    QW_CUDA(cudaMemcpyAsync(c->d_seq_len, &zero, sizeof(int), cudaMemcpyHostToDevice, st));
+    c->seq_len = 0;
+
+    SampleArgs sa;
+    std::memset(&sa, 0, sizeof(sa));
+    sa.logits = w.logits;
+    sa.V = m->vocab_l;
+    sa.cfg_dev = w.scfg;
+    sa.probs = w.probs;
+    sa.ctl = w.ctl;
+    sa.next_tok = w.next_tok;
+    sa.out = w.out;
+
+    cudaEvent_t e0, e1, e2;
+    QW_CUDA(cudaEventCreate(&e0));
+    QW_CUDA(cudaEventCreate(&e1));
+    QW_CUDA(cudaEventCreate(&e2));
+    QW_CUDA(cudaEventRecord(e0, st));
+    forward_dev(m, c, w.ids, n_prompt, 1, true, w.argmax, st, nullptr, nullptr, nullptr);
+    QW_CUDA(launch_sample(sa, st, true));
+    QW_CUDA(cudaEventRecord(e1, st));
+    if (max_new > 1) {
+        if (!c->sample_graph || c->sample_graph_gen != w.generation) {
+            if (c->sample_graph) {
+                cudaGraphExecDestroy(c->sample_graph);
+                c->sample_graph = nullptr;
+            }
+            cudaGraph_t g;
+            QW_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+            try {
+                forward_dev(m, c, w.next_tok, 1, 1, true, w.argmax, st, nullptr, nullptr, nullptr, &w.ctl->done);
+                QW_CUDA(launch_sample(sa, st, true));
+            } catch (...) {
+                cudaStreamEndCapture(st, &g);
+                throw;
+            }
+            QW_CUDA(cudaStreamEndCapture(st, &g));
+            QW_CUDA(cudaGraphInstantiate(&c->sample_graph, g, 0));
+            cudaGraphDestroy(g);
+            c->sample_graph_gen = w.generation;
+        }
+        for (int i = 1; i < max_new; ++i) QW_CUDA(cudaGraphLaunch(c->sample_graph, st));
+    }
+    QW_CUDA(cudaEventRecord(e2, st));
+    QW_CUDA(cudaStreamSynchronize(st));
+    QW_CUDA(cudaMemcpy(&ctl, w.ctl, sizeof(ctl), cudaMemcpyDeviceToHost));
+    float pf = 0, dc = 0;
+    cudaEventElapsedTime(&pf, e0, e1);
+    cudaEventElapsedTime(&dc, e1, e2);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaEventDestroy(e2);
+    QW_CUDA(cudaMemcpy(&c->seq_len, c->d_seq_len, sizeof(int), cudaMemcpyDeviceToHost));
+    if (stats) {
+        stats->prompt_tokens = n_prompt;
+        stats->completion_tokens = ctl.produced;
+        stats->finish_reason = ctl.finish;
+        stats->prefill_ms = pf;
+        stats->decode_ms = dc;
+    }
+}
+
+}  // namespace qw

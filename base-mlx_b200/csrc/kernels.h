@@ -109,6 +109,33 @@ struct StepCtl {
     int n_eos;
     int eos[8];
 };
+// Temperature / top-p sampling parameters (SamplingParams fields that
+// engine.rs:195-263 pick_next reads).  seed drives a counter-based draw:
+// u = top 24 bits of splitmix64(seed ^ splitmix64(counter)) / 2^24, counter =
+// tokens already picked, or 0 for every token when same_draw != 0 (the
+// reference re-seeds its generator from the same seed at every token).
+struct SampleCfg {
+    float temperature;
+    float top_p;
+    unsigned long long seed;
+    int same_draw;
+};
+struct SampleArgs {
+    const bf16* logits;        // [V] bf16 (row of the last position)
+    int V;
+    const SampleCfg* cfg_dev;  // device copy (generation loop), else `cfg`
+    SampleCfg cfg;
+    float* probs;              // scratch [V]
+    StepCtl* ctl;              // generation loop bookkeeping, or null (standalone)
+    int* next_tok;
+    int* out;
+    unsigned long long counter;  // standalone: the draw's counter
+    int* token_out;              // standalone: the picked token
+};
+// One block: softmax(logits / t), nucleus of cumulative mass >= top_p in
+// descending-probability order (ties by index), categorical draw inside it.
+cudaError_t launch_sample(const SampleArgs& a, cudaStream_t st, bool pdl);
+
 // After a forward of S rows: seq_len += S (skipped while *gate != 0); greedy
 // loop bookkeeping when ctl != null.
 cudaError_t launch_step_finish(int* seq_len, int S, const int* argmax, StepCtl* ctl, int* next_tok,

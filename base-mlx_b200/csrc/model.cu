@@ -400,6 +400,8 @@ void ensure_workspace(qw_model* m, int rows, int logits_rows) {
     w.out_cap = std::max(w.out_cap, 65536);
     w.out = (int*)alloc((size_t)w.out_cap * 4);
     w.ctl = (StepCtl*)alloc(sizeof(StepCtl));
+    w.probs = (float*)alloc((size_t)m->vocab_l * 4);
+    w.scfg = (SampleCfg*)alloc(sizeof(SampleCfg));
     QW_CUDA(cudaMemset(w.attn_counters, 0, (size_t)std::max(m->hkv_l, 8) * 4));
     QW_CUDA(cudaMemset(w.next_tok, 0, 64));
     w.cap_rows = rows;
@@ -490,6 +492,7 @@ qw_model::~qw_model() {
 
 qw_cache::~qw_cache() {
     if (step_graph) cudaGraphExecDestroy(step_graph);
+    if (sample_graph) cudaGraphExecDestroy(sample_graph);
     if (k) cudaFree(k);
     if (v) cudaFree(v);
     if (d_seq_len) cudaFree(d_seq_len);

@@ -75,6 +75,8 @@ struct Workspace {
     int* out = nullptr;          // generated tokens
     int out_cap = 0;
     StepCtl* ctl = nullptr;
+    float* probs = nullptr;      // sampling: softmax probabilities [vocab]
+    SampleCfg* scfg = nullptr;   // sampling parameters of the running generation
     int generation = 0;          // bumped on reallocation (invalidates graphs)
     std::vector<void*> allocs;
 };
@@ -123,6 +125,9 @@ struct qw_cache {
     // captured decode-step graph (greedy device loop)
     cudaGraphExec_t step_graph = nullptr;
     int step_graph_gen = -1;
+    // captured decode-step graph of the sampled device loop
+    cudaGraphExec_t sample_graph = nullptr;
+    int sample_graph_gen = -1;
     ~qw_cache();
     bf16* kl(int layer) const;
     bf16* vl(int layer) const;
@@ -154,6 +159,8 @@ void forward_dev(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_m
                  int* d_argmax, cudaStream_t st, StepCtl* ctl, int* next_tok, int* out, const int* gate = nullptr);
 void generate_greedy_dev(qw_model* m, qw_cache* c, int n_prompt, int max_new, const std::vector<int>& eos,
                          qw_gen_stats* stats, cudaStream_t st);
+void generate_sampled_dev(qw_model* m, qw_cache* c, int n_prompt, int max_new, const std::vector<int>& eos,
+                          const SampleCfg& cfg, qw_gen_stats* stats, cudaStream_t st);
 
 // spec.cu
 struct SpecRequest {

@@ -125,6 +125,9 @@ SIGNATURES = {
     "qw_kv_read": [P, I, I, U16P, I, I],
     "qw_forward": [P, P, U32P, I, I, U16P, U32P],
     "qw_generate_greedy": [P, U32P, I, I, U32P, I, U32P, ctypes.POINTER(I), ctypes.POINTER(GenStats)],
+    "qw_generate_sampled": [P, U32P, I, I, ctypes.c_float, ctypes.c_float, ctypes.c_uint64, I, U32P, I, U32P,
+                            ctypes.POINTER(I), ctypes.POINTER(GenStats)],
+    "qw_sample_topp": [P, I, ctypes.c_float, ctypes.c_float, ctypes.c_uint64, ctypes.c_uint64, P, P, P],
     "qw_spec_generate": [P, P, U32P, I, I, I, ctypes.c_float, ctypes.c_uint64, U32P, I, U32P, I, U32P,
                          ctypes.POINTER(I), ctypes.POINTER(SpecStats)],
     "qw_quantized_matmul": [P, P, P, P, P, I, I, I, I, I, P],
@@ -304,6 +307,33 @@ class Qwen3:
                                        ctypes.byref(st)))
         return GenerationResult([int(t) for t in out[:n.value]], st.prompt_tokens, st.completion_tokens,
                                 "stop" if st.finish_reason == 1 else "length", st.prefill_ms, st.decode_ms)
+
+    def generate_sampled(self, prompt, max_new: int, temperature: float = 0.7, top_p: float = 0.95, seed: int = 0,
+                         same_draw_each_token: bool = False, eos=None) -> GenerationResult:
+        """LoadedModel::generate_text with SamplingParams {temperature, top_p, seed}
+        (engine.rs:149-263); temperature <= 0 is greedy."""
+        p, pp = _u32(prompt)
+        out = np.empty(max(max_new, 1), np.uint32)
+        n = ctypes.c_int()
+        st = GenStats()
+        if eos is not None:
+            e, ep = _u32(eos)
+            ne = len(e)
+        else:
+            ep, ne = None, 0
+        check(lib().qw_generate_sampled(self.h, pp, len(p), max_new, temperature, top_p, seed & ((1 << 64) - 1),
+                                        1 if same_draw_each_token else 0, ep, ne, out.ctypes.data_as(U32P),
+                                        ctypes.byref(n), ctypes.byref(st)))
+        return GenerationResult([int(t) for t in out[:n.value]], st.prompt_tokens, st.completion_tokens,
+                                "stop" if st.finish_reason == 1 else "length", st.prefill_ms, st.decode_ms)
+
+
+def sample_topp(logits_ptr: int, vocab: int, temperature: float, top_p: float, seed: int, counter: int,
+                probs_ptr: int, token_ptr: int, stream: int = 0) -> None:
+    """LoadedModel::pick_next on one device bf16 logits row (engine.rs:195-263);
+    writes the picked id to the device int32 at token_ptr."""
+    check(lib().qw_sample_topp(logits_ptr, vocab, temperature, top_p, seed & ((1 << 64) - 1),
+                               counter & ((1 << 64) - 1), probs_ptr, token_ptr, stream or None))
 
 
 def tp_unique_id() -> bytes:

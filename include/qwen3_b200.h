@@ -13,6 +13,8 @@
  *   qw_kv_slice_update       mlx_ext::slice_update on a cache tensor mlx_ext.rs:36-64
  *   qw_quantized_matmul      mlx_rs::ops::quantized_matmul(transpose=true, 64, 4) model/qwen3.rs:30-41
  *   qw_generate_greedy       LoadedModel::generate_text (greedy)   engine.rs:149-201
+ *   qw_generate_sampled      LoadedModel::generate_text, temperature/top-p pick_next engine.rs:149-201,203-263
+ *   qw_sample_topp           LoadedModel::pick_next on one logits row (device)         engine.rs:195-263
  *   qw_spec_generate         speculative::generate                 speculative.rs:57-286
  *   qw_check_compatible      speculative::check_compatible         speculative.rs:40-54
  *
@@ -164,6 +166,26 @@ QW_API int qw_spec_generate(qw_model* target, qw_model* draft, const uint32_t* p
                             int max_new, int k, float force_p, uint64_t seed,
                             const uint32_t* forced_seq_host, int n_forced, const uint32_t* eos, int n_eos,
                             uint32_t* out_host, int* n_out, qw_spec_stats* stats);
+
+/* Sampled generation (engine.rs:149-263 with SamplingParams temperature,
+ * top_p, seed; top_k and repetition_penalty are not read by the reference's
+ * pick_next either).  temperature <= 0 is greedy, as in the reference.  Each
+ * pick draws u = top 24 bits of splitmix64(seed ^ splitmix64(i)) / 2^24 with i
+ * the number of tokens already picked, or i = 0 for every pick when
+ * same_draw_each_token != 0 (the reference seeds a fresh generator from the
+ * same seed at every token, so it reuses one draw).  Outputs as in
+ * qw_generate_greedy.  Needs the whole vocabulary on the rank (no untied
+ * vocab-parallel lm_head). */
+QW_API int qw_generate_sampled(qw_model* m, const uint32_t* prompt_host, int n_prompt, int max_new,
+                               float temperature, float top_p, uint64_t seed, int same_draw_each_token,
+                               const uint32_t* eos, int n_eos, uint32_t* out_host, int* n_out, qw_gen_stats* stats);
+
+/* One pick from a device bf16 logits row of `vocab` entries with the draw
+ * counter `counter` (same generator as qw_generate_sampled); probs_scratch is
+ * a device float[vocab] the call overwrites; *token_out (device int32).
+ * stream may be NULL. */
+QW_API int qw_sample_topp(const void* logits, int vocab, float temperature, float top_p, uint64_t seed,
+                          uint64_t counter, void* probs_scratch, int32_t* token_out, void* stream);
 
 /* ---- standalone op ----------------------------------------------------- */
 

@@ -11,6 +11,14 @@
   drafted token is replaced by the plain-greedy target token for that
   position, ``forced_seq[len(emitted) + slot]``; the uniform draw is
   ``numerics.uniform01(seed, iteration, slot)``.
+* ``pick_topp`` restates the temperature / top-p branch of ``pick_next``
+  (``engine.rs:203-263``) literally -- fp32 division by the temperature,
+  softmax with sequential fp32 sums, a stable descending sort, sequential fp32
+  cumulative sums for the top-p cutoff, the renormalising sum and the draw
+  walk -- with the reference's ``rand::StdRng`` draw (rand 0.8, ChaCha12 seeded
+  by ``seed_from_u64``; not vendored) replaced by ``sample_u(seed, counter)``,
+  the counter-based generator the CUDA path shares.  ``generate_sampled`` is
+  ``generate_text`` with that pick.
 """
 from __future__ import annotations
 
@@ -135,3 +143,59 @@ def spec_generate(target: Qwen3Ref, draft: Qwen3Ref, prompt, max_new: int, k: in
         leader = bonus
         dlog = draft.forward([leader], dc)
     return GenResult(emitted, len(emitted), finish), stats
+
+
+def sample_u(seed: int, counter: int) -> np.float32:
+    """Uniform draw in [0, 1): top 24 bits of splitmix64(seed ^ splitmix64(counter)) / 2^24."""
+    h = nm.splitmix64_int((seed & nm.MASK64) ^ nm.splitmix64_int(counter & nm.MASK64))
+    return np.float32(h >> 40) * np.float32(1.0 / 16777216.0)
+
+
+def pick_topp(logits: np.ndarray, temperature: float, top_p: float, u: float, exact: bool = False) -> int:
+    """engine.rs:203-263 on one row of (bf16-valued) logits, draw u in [0, 1).
+
+    exact=False is the reference's arithmetic: every sum sequential in fp32
+    (which over a long flat tail drifts by up to ~1e-4 of probability mass and
+    drops addends below half an ulp).  exact=True keeps the same fp32
+    probabilities but sums in fp64 -- the arithmetic of the CUDA path."""
+    if not temperature > 0.0:
+        return int(argmax_first(np.asarray(logits, np.float32)))
+    t = np.float32(max(np.float32(temperature), np.float32(1e-5)))
+    p = (np.asarray(logits, np.float32) / t).astype(np.float32)
+    mx = np.float32(p.max())
+    p = np.exp(p - mx).astype(np.float32)
+    acc_t = np.float64 if exact else np.float32
+    total = np.float32(np.add.accumulate(p, dtype=acc_t)[-1])  # sequential sum
+    p = (p / total).astype(np.float32)
+    order = np.argsort(-p, kind="stable")
+    top_pf = np.float32(min(max(top_p, 0.0), 1.0))
+    cum = np.add.accumulate(p[order], dtype=acc_t)
+    hit = np.nonzero(cum >= top_pf)[0]
+    cutoff = int(hit[0]) + 1 if len(hit) else len(order)
+    top = order[:cutoff]
+    acc = np.add.accumulate(p[top], dtype=acc_t)
+    renorm = np.float32(acc[-1])
+    r = np.float32(np.float32(u) * renorm)
+    pos = np.nonzero(acc >= r)[0]
+    return int(top[pos[0]]) if len(pos) else int(top[-1])
+
+
+def generate_sampled(model: Qwen3Ref, prompt, max_new: int, temperature: float, top_p: float, seed: int,
+                     same_draw: bool = False, max_pos: int = 4096) -> GenResult:
+    """generate_text with the sampled pick; pick i uses sample_u(seed, 0 if same_draw else i)."""
+    cache = model.new_cache(max_pos)
+    logits = model.forward(list(prompt), cache)
+    out = []
+    produced = 0
+    finish = "length"
+    while True:
+        nxt = pick_topp(logits, temperature, top_p, sample_u(seed, 0 if same_draw else produced))
+        produced += 1
+        if model.is_eos(nxt):
+            finish = "stop"
+            break
+        out.append(nxt)
+        if produced >= max_new:
+            break
+        logits = model.forward([nxt], cache)
+    return GenResult(out, produced, finish)
