@@ -409,6 +409,11 @@ def run_ours(args):
             cpu = {"value": round(v, 4), "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
         if args.spec:
             extra["spec"] = spec_measure(q, m, prompt, cfg)
+        # sampled decode (temperature 0.7, top-p 0.95: the reference's SamplingParams defaults):
+        # the device pick after every step on the same model and prompt
+        rs = m.generate_sampled(prompt, DECODE_TOKENS, temperature=0.7, top_p=0.95, seed=SEED, eos=[1 << 30])
+        extra["sampled_decode"] = {"tok_s": round((rs.completion_tokens - 1) / (rs.decode_ms / 1e3), 2),
+                                   "temperature": 0.7, "top_p": 0.95, "tokens": rs.completion_tokens}
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(region_max * 1e3 / args.steps, 3),
