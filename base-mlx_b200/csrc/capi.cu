@@ -364,9 +364,9 @@ int qw_generate_sampled(qw_model* m, const uint32_t* prompt, int n_prompt, int m
 }
 
 int qw_sample_topp(const void* logits, int vocab, float temperature, float top_p, uint64_t seed, uint64_t counter,
-                   void* probs, int32_t* token_out, void* stream) {
+                   void* scratch, int32_t* token_out, void* stream) {
     return guard([&] {
-        need(logits && probs && token_out, "logits/probs/token_out");
+        need(logits && scratch && token_out, "logits/scratch/token_out");
         need(vocab >= 1, "vocab must be positive");
         need(top_p == top_p && temperature == temperature, "NaN parameter");
         qw::SampleArgs a;
@@ -376,10 +376,11 @@ int qw_sample_topp(const void* logits, int vocab, float temperature, float top_p
         a.cfg.temperature = temperature;
         a.cfg.top_p = top_p;
         a.cfg.seed = seed;
-        a.probs = (float*)probs;
+        a.ctrl = scratch;
+        a.probs = (float*)((char*)scratch + qw::QW_SAMPLE_CTRL_BYTES);
         a.counter = counter;
         a.token_out = token_out;
-        QW_CUDA(qw::launch_sample(a, (cudaStream_t)stream, false));
+        QW_CUDA(qw::launch_sample(a, (cudaStream_t)stream));
     });
 }
 
@@ -418,6 +419,27 @@ int qw_spec_generate(qw_model* target, qw_model* draft, const uint32_t* prompt, 
     });
 }
 
+// The multi-row qw_quantized_matmul keeps one fp16 activation buffer per
+// (device, stream), grown on demand and kept until exit: calls on one stream
+// are ordered, so they can share it, and no call pays an allocation.
+static void* qmm_scratch(int dev, cudaStream_t st, size_t bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<int, cudaStream_t>, std::pair<void*, size_t>> bufs;
+    std::lock_guard<std::mutex> lk(mu);
+    auto& b = bufs[{dev, st}];
+    if (b.second < bytes) {
+        if (b.first) {
+            QW_CUDA(cudaStreamSynchronize(st));  // the old buffer may still be read by earlier work
+            cudaFree(b.first);
+            b = {nullptr, 0};
+        }
+        void* p = nullptr;
+        QW_CUDA(cudaMalloc(&p, bytes));
+        b = {p, bytes};
+    }
+    return b.first;
+}
+
 // QW_PREFILL_GEMM=legacy keeps multi-row matmuls on the mma.sync kernel.
 static bool legacy_prefill_gemm() {
     const char* e = std::getenv("QW_PREFILL_GEMM");
@@ -452,13 +474,9 @@ int qw_quantized_matmul(const void* x, const void* w, const void* scales, const 
         if (M <= 8) {
             QW_CUDA(qw::launch_qgemv(a, st, false, sms));
         } else if (qw::qgemm_tc_supported(a) && !legacy_prefill_gemm()) {
-            // fp16 copy of x for the tensor-core kernel, stream-ordered
+            // fp16 copy of x for the tensor-core kernel
             const size_t bytes = qw::qgemm_tc_scratch_bytes(M, K);
-            void* scratch = nullptr;
-            QW_CUDA(cudaMallocAsync(&scratch, bytes, st));
-            const cudaError_t e = qw::launch_qgemm_tc(a, scratch, bytes, st);
-            cudaFreeAsync(scratch, st);
-            QW_CUDA(e);
+            QW_CUDA(qw::launch_qgemm_tc(a, qmm_scratch(dev, st, bytes), bytes, st));
         } else {
             QW_CUDA(qw::launch_qgemm(a, st, sms));
         }

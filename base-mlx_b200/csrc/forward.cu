@@ -312,6 +312,8 @@ void generate_sampled_dev(qw_model* m, qw_cache* c, int n_prompt, int max_new, c
     sa.ctl = w.ctl;
     sa.next_tok = w.next_tok;
     sa.out = w.out;
+    sa.ctrl = w.sctrl;
+    sa.err = m->d_err;
 
     cudaEvent_t e0, e1, e2;
     QW_CUDA(cudaEventCreate(&e0));
@@ -319,7 +321,7 @@ void generate_sampled_dev(qw_model* m, qw_cache* c, int n_prompt, int max_new, c
     QW_CUDA(cudaEventCreate(&e2));
     QW_CUDA(cudaEventRecord(e0, st));
     forward_dev(m, c, w.ids, n_prompt, 1, true, w.argmax, st, nullptr, nullptr, nullptr);
-    QW_CUDA(launch_sample(sa, st, true));
+    QW_CUDA(launch_sample(sa, st));
     QW_CUDA(cudaEventRecord(e1, st));
     if (max_new > 1) {
         if (!c->sample_graph || c->sample_graph_gen != w.generation) {
@@ -331,7 +333,7 @@ void generate_sampled_dev(qw_model* m, qw_cache* c, int n_prompt, int max_new, c
             QW_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
             try {
                 forward_dev(m, c, w.next_tok, 1, 1, true, w.argmax, st, nullptr, nullptr, nullptr, &w.ctl->done);
-                QW_CUDA(launch_sample(sa, st, true));
+                QW_CUDA(launch_sample(sa, st));
             } catch (...) {
                 cudaStreamEndCapture(st, &g);
                 throw;

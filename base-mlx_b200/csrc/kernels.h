@@ -114,6 +114,7 @@ struct StepCtl {
 // u = top 24 bits of splitmix64(seed ^ splitmix64(counter)) / 2^24, counter =
 // tokens already picked, or 0 for every token when same_draw != 0 (the
 // reference re-seeds its generator from the same seed at every token).
+constexpr size_t QW_SAMPLE_CTRL_BYTES = 16384;  // sampling control block (grid barrier, partials, histograms)
 struct SampleCfg {
     float temperature;
     float top_p;
@@ -131,10 +132,13 @@ struct SampleArgs {
     int* out;
     unsigned long long counter;  // standalone: the draw's counter
     int* token_out;              // standalone: the picked token
+    void* ctrl;                  // QW_SAMPLE_CTRL_BYTES control block, zero before its first use
+    int* err;                    // device error flags (timeouts), may be null
 };
-// One block: softmax(logits / t), nucleus of cumulative mass >= top_p in
-// descending-probability order (ties by index), categorical draw inside it.
-cudaError_t launch_sample(const SampleArgs& a, cudaStream_t st, bool pdl);
+// softmax(logits / t), nucleus of cumulative mass >= top_p in descending-
+// probability order (ties by index), categorical draw inside it: one
+// cooperative grid (sample.cu).
+cudaError_t launch_sample(const SampleArgs& a, cudaStream_t st);
 
 // After a forward of S rows: seq_len += S (skipped while *gate != 0); greedy
 // loop bookkeeping when ctl != null.

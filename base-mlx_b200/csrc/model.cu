@@ -402,6 +402,8 @@ void ensure_workspace(qw_model* m, int rows, int logits_rows) {
     w.ctl = (StepCtl*)alloc(sizeof(StepCtl));
     w.probs = (float*)alloc((size_t)m->vocab_l * 4);
     w.scfg = (SampleCfg*)alloc(sizeof(SampleCfg));
+    w.sctrl = alloc(QW_SAMPLE_CTRL_BYTES);
+    QW_CUDA(cudaMemset(w.sctrl, 0, QW_SAMPLE_CTRL_BYTES));
     QW_CUDA(cudaMemset(w.attn_counters, 0, (size_t)std::max(m->hkv_l, 8) * 4));
     QW_CUDA(cudaMemset(w.next_tok, 0, 64));
     w.cap_rows = rows;

@@ -77,6 +77,7 @@ struct Workspace {
     StepCtl* ctl = nullptr;
     float* probs = nullptr;      // sampling: softmax probabilities [vocab]
     SampleCfg* scfg = nullptr;   // sampling parameters of the running generation
+    void* sctrl = nullptr;       // sampling control block (zeroed at allocation)
     int generation = 0;          // bumped on reallocation (invalidates graphs)
     std::vector<void*> allocs;
 };

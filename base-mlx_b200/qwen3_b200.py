@@ -328,12 +328,17 @@ class Qwen3:
                                 "stop" if st.finish_reason == 1 else "length", st.prefill_ms, st.decode_ms)
 
 
+def sample_scratch_bytes(vocab: int) -> int:
+    """Size of the device scratch qw_sample_topp needs (zero it before first use)."""
+    return 16384 + 4 * vocab
+
+
 def sample_topp(logits_ptr: int, vocab: int, temperature: float, top_p: float, seed: int, counter: int,
-                probs_ptr: int, token_ptr: int, stream: int = 0) -> None:
+                scratch_ptr: int, token_ptr: int, stream: int = 0) -> None:
     """LoadedModel::pick_next on one device bf16 logits row (engine.rs:195-263);
     writes the picked id to the device int32 at token_ptr."""
     check(lib().qw_sample_topp(logits_ptr, vocab, temperature, top_p, seed & ((1 << 64) - 1),
-                               counter & ((1 << 64) - 1), probs_ptr, token_ptr, stream or None))
+                               counter & ((1 << 64) - 1), scratch_ptr, token_ptr, stream or None))
 
 
 def tp_unique_id() -> bytes:

@@ -181,11 +181,15 @@ QW_API int qw_generate_sampled(qw_model* m, const uint32_t* prompt_host, int n_p
                                const uint32_t* eos, int n_eos, uint32_t* out_host, int* n_out, qw_gen_stats* stats);
 
 /* One pick from a device bf16 logits row of `vocab` entries with the draw
- * counter `counter` (same generator as qw_generate_sampled); probs_scratch is
- * a device float[vocab] the call overwrites; *token_out (device int32).
- * stream may be NULL. */
+ * counter `counter` (same generator as qw_generate_sampled); *token_out
+ * (device int32).  `scratch` is a device buffer of QW_SAMPLE_SCRATCH_BYTES(vocab)
+ * bytes, zero before its first use, that the call leaves ready for the next
+ * one (its head is the control block of the grid the pick runs on); calls that
+ * share a scratch buffer must not overlap on the GPU.  logits and scratch must
+ * be 16-byte aligned.  stream may be NULL. */
+#define QW_SAMPLE_SCRATCH_BYTES(vocab) (16384u + 4u * (size_t)(vocab))
 QW_API int qw_sample_topp(const void* logits, int vocab, float temperature, float top_p, uint64_t seed,
-                          uint64_t counter, void* probs_scratch, int32_t* token_out, void* stream);
+                          uint64_t counter, void* scratch, int32_t* token_out, void* stream);
 
 /* ---- standalone op ----------------------------------------------------- */
 

@@ -26,7 +26,7 @@ NOEOS = 1 << 30  # an end-of-sequence id no vocabulary produces: runs go to max_
 def _dev_pick(torch, q, lg_bits, t, top_p, seed, counter):
     dev = torch.device("cuda:0")
     x = torch.from_numpy(lg_bits.view(np.int16).copy()).to(dev)
-    probs = torch.empty(lg_bits.size, dtype=torch.float32, device=dev)
+    probs = torch.zeros(q.sample_scratch_bytes(lg_bits.size) // 4, dtype=torch.float32, device=dev)
     tok = torch.full((1,), -7, dtype=torch.int32, device=dev)
     q.sample_topp(x.data_ptr(), lg_bits.size, t, top_p, seed, counter, probs.data_ptr(), tok.data_ptr(),
                   torch.cuda.current_stream().cuda_stream)
