@@ -39,6 +39,8 @@ def _free_port() -> int:
 
 def _worker(rank, world, port, cfg, plen, out_dir):
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    # single-node boxes without a routable network: NCCL's own bootstrap on loopback
+    os.environ.setdefault("NCCL_SOCKET_IFNAME", "lo")
     import torch
     import torch.distributed as dist
     import qwen3_b200 as q
@@ -86,7 +88,7 @@ def test_tp2_matches_single_gpu(case, tmp_path):
     for p in procs:
         p.start()
     for p in procs:
-        p.join(600)
+        p.join(240)
     for p in procs:
         if p.exitcode is None:
             p.kill()
