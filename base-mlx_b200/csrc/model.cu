@@ -478,12 +478,14 @@ void check_device_err(qw_model* m) {
 qw_model::~qw_model() {
     if (device >= 0) cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
-    qw::tp_destroy(this);
-    qw::mk_free(this);
+    // graphs that captured NCCL calls (the caches' step graphs, the spec graphs)
+    // go before the communicator they use
     qw::spec_state_free(spec_state);
     spec_state = nullptr;
     for (qw_cache* c : caches) delete c;
     caches.clear();
+    qw::tp_destroy(this);
+    qw::mk_free(this);
     for (void* p : ws.allocs) cudaFree(p);
     if (arena) cudaFree(arena);
     if (rope_cos) cudaFree(rope_cos);
