@@ -480,6 +480,20 @@ def profile_qmm(spec: str) -> None:
     print(f"profile_qmm: M={M} K={K} N={N} max|y| {float(y.float().abs().max())}")
 
 
+def profile_sampled(n: int, model: str) -> None:
+    """ncu workload: one sampled generation of n tokens (temperature 0.7, top-p
+    0.95) after the prefill, through qw_generate_sampled."""
+    import torch
+    import qwen3_b200 as q
+    cfg = dict(CFG_4B if model == "4b" else CFG_0_6B)
+    plen = PROMPT_LEN if model == "4b" else 128
+    m = q.Qwen3.init_random(cfg, SEED, norm_mode="ones", device=0)
+    r = m.generate_sampled(prompt_ids(cfg["vocab_size"])[:plen].tolist(), n, temperature=0.7, top_p=0.95, seed=SEED,
+                           eos=[1 << 30])
+    torch.cuda.synchronize()
+    print(f"profile_sampled: {model} prefill {plen} + {len(r.tokens)} sampled tokens")
+
+
 def profile_decode(n: int, model: str) -> None:
     """Prefill and n decode steps, one qw_forward each (the ncu workloads): the
     bench model (Qwen3-4B, 512-token prompt) or, for captures that must stay
@@ -511,6 +525,8 @@ def main():
                     help="profiling workload for ncu: weight init, the prefill and N greedy decode steps through "
                          "qw_forward; prints no bench line")
     ap.add_argument("--profile-model", choices=["4b", "0.6b"], default="4b")
+    ap.add_argument("--profile-sampled", type=int, default=0, metavar="N",
+                    help="profiling workload for ncu: a sampled generation of N tokens; prints no bench line")
     ap.add_argument("--profile-qmm", default="", metavar="M,K,N",
                     help="profiling workload for ncu: three quantized matmuls of one shape; prints no bench line")
     args = ap.parse_args()
@@ -518,6 +534,8 @@ def main():
         args.warmup = 3
     if args.profile_qmm:
         profile_qmm(args.profile_qmm)
+    elif args.profile_sampled > 0:
+        profile_sampled(args.profile_sampled, args.profile_model)
     elif args.profile_decode > 0:
         profile_decode(args.profile_decode, args.profile_model)
     elif args.impl == "reference":
