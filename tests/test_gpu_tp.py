@@ -47,14 +47,22 @@ def _worker(rank, world, port, cfg, plen, out_dir):
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=120))
+    def step(what):  # progress on stdout (pytest -s): shows where a stalled rank stopped
+        print(f"[tp rank {rank}] {what}", flush=True)
+
     try:
+        step("process group up")
         m = q.Qwen3.init_random(cfg, 77, norm_mode="random", device=rank, tp_rank=rank, tp_size=world)
+        step("shard loaded")
         q.tp_init(m, rank, world)
+        step("communicator attached")
         prompt = np.random.default_rng(3).integers(0, cfg["vocab_size"], plen).tolist()
         c = m.new_cache(256)
         lg, am = m.forward_multi(prompt, c)
         c.close()
+        step("prefill done")
         gen = m.generate_greedy(prompt, 24)
+        step("generation done")
         res = {"argmax": np.asarray(am).tolist(), "last_logits": lg[-1].copy(), "tokens": list(gen.tokens)}
         m.close()
         dist.barrier()
