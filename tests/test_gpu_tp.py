@@ -4,10 +4,17 @@ untied lm_head vocabulary rows), the NCCL sum all-reduces after o_proj and
 down_proj and the u64 max all-reduce of the vocab-parallel argmax keys,
 against the single-GPU model of the same seed on the same inputs.
 
-Tolerances: logits within 2e-2 max-abs (tiny models) / 0.1 (4-layer 0.6B
-shapes) -- the split only changes the fp32 summation order of o_proj and
-down_proj -- and identical prefill argmaxes and greedy tokens.  Skipped with
-fewer than two GPUs.  The NCCL id travels over a gloo process group
+Tolerances: logits of every prefill row within 2e-2 max-abs (tiny models) /
+0.1 (4-layer 0.6B shapes).  The split only changes the fp32 summation order of
+o_proj and down_proj, but a partial sum that lands on the other side of a bf16
+rounding boundary of the hidden state moves later logits by more than fp32
+noise, so a row whose two best logits are closer than that can flip its
+argmax.  Every pick (prefill argmax and each greedy token, the latter against
+the single-GPU model run teacher-forced on the tensor-parallel tokens) must
+therefore lie within 2 x tol of the single-GPU maximum of its row -- which is
+exact equality wherever the top-2 gap exceeds 2 x tol -- and the two ranks
+must agree bit for bit on argmaxes and tokens.  Skipped with fewer than two
+GPUs.  The NCCL id travels over a gloo process group
 (qwen3_b200.tp_init); ranks rendezvous on 127.0.0.1.
 """
 import datetime
@@ -63,7 +70,7 @@ def _worker(rank, world, port, cfg, plen, out_dir):
         step("prefill done")
         gen = m.generate_greedy(prompt, 24)
         step("generation done")
-        res = {"argmax": np.asarray(am).tolist(), "last_logits": lg[-1].copy(), "tokens": list(gen.tokens)}
+        res = {"argmax": np.asarray(am).tolist(), "logits": np.asarray(lg).copy(), "tokens": list(gen.tokens)}
         m.close()
         dist.barrier()
         if rank == 0:
@@ -72,7 +79,13 @@ def _worker(rank, world, port, cfg, plen, out_dir):
             lg1, am1 = m1.forward_multi(prompt, c1)
             c1.close()
             g1 = m1.generate_greedy(prompt, 24)
-            res.update(ref_argmax=np.asarray(am1).tolist(), ref_last_logits=lg1[-1].copy(), ref_tokens=list(g1.tokens))
+            # the single-GPU model teacher-forced on the tensor-parallel tokens:
+            # row plen-1+j scores the choice of token j
+            c2 = m1.new_cache(256)
+            lg2, _ = m1.forward_multi(prompt + list(gen.tokens[:-1]), c2)
+            c2.close()
+            res.update(ref_argmax=np.asarray(am1).tolist(), ref_logits=np.asarray(lg1).copy(),
+                       ref_tokens=list(g1.tokens), ref_forced=np.asarray(lg2)[plen - 1:].copy())
             m1.close()
         np.save(os.path.join(out_dir, f"r{rank}.npy"), res, allow_pickle=True)
     finally:
@@ -103,16 +116,28 @@ def test_tp2_matches_single_gpu(case, tmp_path):
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     r0 = np.load(os.path.join(tmp_path, "r0.npy"), allow_pickle=True).item()
     r1 = np.load(os.path.join(tmp_path, "r1.npy"), allow_pickle=True).item()
-    ref = r0["ref_last_logits"]
+    ref = r0["ref_logits"]
     V = cfg["vocab_size"]
     if cfg["tie_word_embeddings"]:
-        # replicated lm_head: every rank holds the full row
-        shards = [(r0["last_logits"], 0), (r1["last_logits"], 0)]
+        # replicated lm_head: every rank holds the full rows
+        shards = [(r0["logits"], 0), (r1["logits"], 0)]
     else:
-        shards = [(r0["last_logits"], 0), (r1["last_logits"], V // 2)]
-    for lg, off in shards:
-        d = np.abs(lg - ref[off:off + len(lg)])
-        assert d.max() <= tol, (case, float(d.max()))
-    for r in (r0, r1):
-        assert r["argmax"] == r0["ref_argmax"], case
-        assert r["tokens"] == r0["ref_tokens"], case
+        shards = [(r0["logits"], 0), (r1["logits"], V // 2)]
+    diffs = [float(np.abs(lg - ref[:, off:off + lg.shape[1]]).max()) for lg, off in shards]
+    am, toks = r0["argmax"], r0["tokens"]
+    am_exact = sum(a == b for a, b in zip(am, r0["ref_argmax"]))
+    tok_exact = sum(a == b for a, b in zip(toks, r0["ref_tokens"]))
+    print(f"[tp {case}] logits max-abs diff per rank {diffs}; prefill argmax exact {am_exact}/{len(am)}; "
+          f"greedy tokens equal to the single-GPU run {tok_exact}/{len(toks)}")
+    assert max(diffs) <= tol, (case, diffs)
+    # both ranks hold the same all-reduced state: identical picks
+    assert r1["argmax"] == am and r1["tokens"] == toks, case
+
+    def within(rows, picks):
+        rows = np.asarray(rows, np.float64)
+        got = rows[np.arange(len(picks)), np.asarray(picks)]
+        return got >= rows.max(axis=1) - 2 * tol
+
+    assert len(am) == len(ref) and within(ref, am).all(), case
+    forced = r0["ref_forced"]
+    assert len(toks) == 24 and len(forced) == len(toks) and within(forced, toks).all(), case
