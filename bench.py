@@ -56,6 +56,9 @@ CFG_0_6B = dict(
     quantization=dict(group_size=64, bits=4))
 CFG_4B = dict(CFG_0_6B, hidden_size=2560, intermediate_size=9728, num_hidden_layers=36,
               num_attention_heads=32, num_key_value_heads=8)
+CFG_32B = dict(CFG_0_6B, hidden_size=5120, intermediate_size=25600, num_hidden_layers=64,
+               num_attention_heads=64, num_key_value_heads=8, tie_word_embeddings=False)
+TP_PROMPT_LEN, TP_DECODE_TOKENS = 2048, 256  # config 5: 2048-token prompt, greedy decode of 256
 REF_TOK_S = 32.75  # reference on M2-class Apple Silicon, 300-token greedy decode
 METRIC = "Qwen3-4B 4-bit batch-1 decode tok/s (plain & spec k=4); qmatmul HBM GB/s"
 
@@ -511,6 +514,102 @@ def profile_decode(n: int, model: str) -> None:
     print(f"profile_decode: {model} prefill {plen} + {n} decode steps, last token {tok}")
 
 
+def run_tp_decode(args):
+    """Qwen3-32B tensor-parallel batch-1 greedy decode (config 5): ONE sequence
+    served by all N ranks, one process per GPU (launched by torchrun; N=1 runs
+    the unsplit model).  Each rank loads its shard (q/k/v, gate/up rows;
+    o_proj/down_proj columns; lm_head vocabulary rows), the library's own NCCL
+    communicator carries the two sum all-reduces per layer and the argmax key
+    all-reduce; a gloo group only exchanges the NCCL id and the timings.
+
+    value = decode tok/s of the sequence, (n-1) / decode time, the decode time
+    taken from the library's CUDA events and maxed over ranks (strong scaling:
+    the work is fixed, N splits it).  roofline: per-rank algorithmic bytes per
+    token (its weight shard + its K/V heads at the mean KV length) over the
+    per-token time, against the measured HBM copy bandwidth.  NVLS is left off
+    (NCCL_NVLS_ENABLE=0): the all-reduces carry 20 KB each, where latency, not
+    bandwidth, sets their cost."""
+    import datetime
+    import torch
+    import qwen3_b200 as q
+    rank, world, local = dist_env()
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    os.environ.setdefault("NCCL_SOCKET_IFNAME", "lo")
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    torch.cuda.set_device(local)
+    cfg = dict(CFG_32B)
+    m = q.Qwen3.init_random(cfg, SEED, norm_mode="ones", device=local, tp_rank=rank, tp_size=world)
+    if world > 1:
+        q.tp_init(m, rank, world)
+    prompt = np.random.default_rng(SEED).integers(0, cfg["vocab_size"], TP_PROMPT_LEN).astype(np.uint32)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        m.generate_greedy(prompt, TP_DECODE_TOKENS)
+    barrier()
+    results = []
+    with ClockSampler(local) as clk:
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            results.append(m.generate_greedy(prompt, TP_DECODE_TOKENS))
+        barrier()
+        region = time.perf_counter() - t0
+    decode_ms = sum(r.decode_ms for r in results)
+    prefill_ms = sum(r.prefill_ms for r in results)
+    dec_tokens = sum(max(r.completion_tokens - 1, 0) for r in results)
+    toks = results[-1].tokens
+    vals = torch.tensor([decode_ms, prefill_ms, region], dtype=torch.float64)
+    agree = True
+    if dist is not None:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        got = [None] * world
+        dist.all_gather_object(got, toks)
+        agree = all(g == toks for g in got)
+    decode_ms_max, prefill_ms_max, region_max = (float(v) for v in vals)
+    value = dec_tokens / (decode_ms_max / 1e3)
+    if rank == 0:
+        info = m.info
+        H, I, V, L = info.hidden, info.intermediate, info.vocab, info.num_layers
+        QD, KD = info.num_heads * info.head_dim, info.num_kv_heads * info.head_dim
+        w_full = (L * (H * (QD + 2 * KD) + QD * H + 2 * H * I + I * H) + V * H) * 0.5625
+        kv_full = L * 2 * KD * 2 * (TP_PROMPT_LEN + TP_DECODE_TOKENS / 2)
+        per_rank = (w_full + kv_full) / world
+        tok_s = decode_ms_max / 1e3 / max(dec_tokens, 1)
+        gbs = per_rank / tok_s / 1e9
+        peak, peak_kind = peaks()
+        line = {"metric": "Qwen3-32B 4-bit batch-1 tensor-parallel greedy decode tok/s", "value": round(value, 2),
+                "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(region_max * 1e3 / args.steps, 3), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "u4xbf16->f32",
+                "data": "synthetic (seeded random-init weights and prompt ids)",
+                "config": {"workload": f"config5: Qwen3-32B 4-bit g64 (untied lm_head), batch 1, "
+                                       f"{TP_PROMPT_LEN}-token prompt, greedy decode {TP_DECODE_TOKENS}",
+                           "parallelism": f"tp{world}",
+                           "l2": "no flush: every decode step streams its weight shard (> 126 MB L2)"},
+                "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                             "frac": round(gbs / peak, 4), "peak_source": peak_kind,
+                             "bytes_per_token_per_rank": int(per_rank),
+                             "bytes_note": "per-rank share of the quantized weights (0.5625 B/param) and of the "
+                                           "bf16 K/V read at the mean KV length 2176"},
+                "decode_ms_per_token": round(decode_ms_max / max(dec_tokens, 1), 4),
+                "ttft_ms": round(prefill_ms_max / len(results), 3),
+                "ranks_agree_on_tokens": agree, "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    m.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -529,10 +628,14 @@ def main():
                     help="profiling workload for ncu: a sampled generation of N tokens; prints no bench line")
     ap.add_argument("--profile-qmm", default="", metavar="M,K,N",
                     help="profiling workload for ncu: three quantized matmuls of one shape; prints no bench line")
+    ap.add_argument("--tp-decode", action="store_true",
+                    help="Qwen3-32B tensor-parallel decode (config 5) over the torchrun ranks; one JSON line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.profile_qmm:
+    if args.tp_decode:
+        run_tp_decode(args)
+    elif args.profile_qmm:
         profile_qmm(args.profile_qmm)
     elif args.profile_sampled > 0:
         profile_sampled(args.profile_sampled, args.profile_model)
