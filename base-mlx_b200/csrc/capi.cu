@@ -471,7 +471,7 @@ int qw_quantized_matmul(const void* x, const void* w, const void* scales, const 
         a.nseg = 1;
         a.epi = qw::EPI_STORE;
         cudaStream_t st = (cudaStream_t)stream;
-        if (M <= 8) {
+        if (M <= 8 && qw::qgemv_fits(a)) {
             QW_CUDA(qw::launch_qgemv(a, st, false, sms));
         } else if (qw::qgemm_tc_supported(a) && !legacy_prefill_gemm()) {
             // fp16 copy of x for the tensor-core kernel

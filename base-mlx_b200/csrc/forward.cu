@@ -61,8 +61,12 @@ bool tc_gemm_enabled() {
 }
 
 void qmm(qw_model* m, QmmArgs a, cudaStream_t st) {
-    if (a.M <= 8)
+    if (a.M <= 8 && qgemv_fits(a))
         QW_CUDA(launch_qgemv(a, st, true, m->num_sms));
+    else if (a.M <= 8 && (a.norm_w || a.epi == EPI_LOGITS))
+        // the fused RMSNorm prologue and the logits epilogue exist in the GEMV only
+        throw Error(QW_ERR_INFERENCE, "normed / logits GEMV row of K=" + std::to_string(a.K) +
+                                          " exceeds the GEMV's shared-memory slab");
     else if (tc_gemm_enabled() && qgemm_tc_supported(a) && m->ws.xh_bytes >= qgemm_tc_scratch_bytes(a.M, a.K))
         QW_CUDA(launch_qgemm_tc(a, m->ws.xh, m->ws.xh_bytes, st));
     else

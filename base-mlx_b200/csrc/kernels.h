@@ -49,6 +49,9 @@ struct QmmArgs {
 cudaError_t launch_qgemv(QmmArgs a, cudaStream_t st, bool pdl, int num_sms);
 // Row blocks of the qgemv grid for these segments (size of amax_partial / M).
 int qgemv_row_blocks(const QmmArgs& a);
+// Whether the GEMV's whole-K weight slab (16 or 32 rows x K) fits in shared
+// memory; long rows that do not (K = 25600 at 220 KB) go to the tiled GEMM.
+bool qgemv_fits(const QmmArgs& a);
 // argmax[m] (and optionally packed keys) from the EPI_LOGITS per-CTA maxima.
 cudaError_t launch_amax_finalize(const unsigned long long* partial, int nrb, int M, int* out,
                                  unsigned long long* keys_out, cudaStream_t st);

@@ -641,6 +641,14 @@ int qgemv_row_blocks(const QmmArgs& a) {
     return nrb;
 }
 
+bool qgemv_fits(const QmmArgs& a) {
+    if (a.M < 1 || a.M > 8 || a.K <= 0 || a.K % 64 != 0) return false;
+    const int KG = a.K / 64;
+    const int RT = a.epi == EPI_SWIGLU ? 2 : 1;
+    const int NW = KG > 48 ? 8 : 4;
+    return gv_layout(KG, a.M, RT, NW).total <= 220 * 1024;
+}
+
 cudaError_t launch_qgemv(QmmArgs a, cudaStream_t st, bool pdl, int num_sms) {
     (void)num_sms;
     if (a.M < 1 || a.M > 8 || a.K <= 0 || a.K % 64 != 0 || a.nseg < 1 || a.nseg > 3)

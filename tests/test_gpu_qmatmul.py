@@ -77,3 +77,12 @@ def test_qmatmul_tc_tile_widths(bn, M, K, N, monkeypatch):
     x, w, s, b = _case(M, K, N, seed=31 + M + N)
     ref = nm.bf16_round(x @ nm.dequantize(w, s, b).T)
     _check(_run_gpu(x, w, s, b), ref)
+
+
+@pytest.mark.parametrize("M", [1, 5, 8])
+def test_qmatmul_long_rows_32b_down_proj(M):
+    """Qwen3-32B down_proj rows (K = 25600): the GEMV's whole-K weight slab does
+    not fit in shared memory, so rows of M <= 8 take the tiled GEMM instead."""
+    x, w, s, b = _case(M, 25600, 160, seed=61 + M)
+    ref = nm.bf16_round(x @ nm.dequantize(w, s, b).T)
+    _check(_run_gpu(x, w, s, b), ref)
