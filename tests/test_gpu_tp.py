@@ -141,3 +141,58 @@ def test_tp2_matches_single_gpu(case, tmp_path):
     assert len(am) == len(ref) and within(ref, am).all(), case
     forced = r0["ref_forced"]
     assert len(toks) == 24 and len(forced) == len(toks) and within(forced, toks).all(), case
+
+
+def _spec_worker(rank, world, port, out_dir):
+    """Speculative decode with a tensor-parallel target and a replicated draft
+    (the config-5 spec variant's shape at tiny size): every rank runs the same
+    spec loop, the target's verify rows go through the sharded forward and its
+    all-reduced argmax, the draft runs whole on each rank."""
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    os.environ.setdefault("NCCL_SOCKET_IFNAME", "lo")
+    import torch
+    import torch.distributed as dist
+    import qwen3_b200 as q
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        cfg = synth.tiny_config(tie_word_embeddings=False)
+        t = q.Qwen3.init_random(cfg, 77, norm_mode="random", device=rank, tp_rank=rank, tp_size=world)
+        q.tp_init(t, rank, world)
+        d = q.Qwen3.init_random(synth.tiny_config(num_hidden_layers=1), 78, norm_mode="random", device=rank)
+        print(f"[tp spec rank {rank}] models up", flush=True)
+        prompt = np.random.default_rng(4).integers(0, cfg["vocab_size"], 24).tolist()
+        plain = t.generate_greedy(prompt, 32)
+        res = {"plain": list(plain.tokens)}
+        for k, p in ((4, 0.8), (3, 0.0)):
+            r, st = q.speculative_generate(t, d, prompt, 32, k=k, force_p=p, seed=3, forced=plain.tokens)
+            res[f"k{k}"] = (list(r.tokens), (st.iters, st.proposed, st.accepted))
+        print(f"[tp spec rank {rank}] spec done", flush=True)
+        d.close()
+        t.close()
+        np.save(os.path.join(out_dir, f"s{rank}.npy"), res, allow_pickle=True)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(_ngpu() < 2, reason="needs two GPUs")
+def test_tp2_speculative_matches_tp2_greedy(tmp_path):
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_spec_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(240)
+    for p in procs:
+        if p.exitcode is None:
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    s0 = np.load(os.path.join(tmp_path, "s0.npy"), allow_pickle=True).item()
+    s1 = np.load(os.path.join(tmp_path, "s1.npy"), allow_pickle=True).item()
+    assert s0 == s1  # same tokens and accept counts on both ranks
+    for key in ("k4", "k3"):
+        toks, (iters, proposed, accepted) = s0[key]
+        assert toks == s0["plain"], key  # greedy spec output == plain greedy of the same split target
+        assert proposed >= accepted and iters > 0, key
