@@ -172,19 +172,6 @@ QW_DEV void cp_async_wait_dyn(int n) {
     }
 }
 
-// 16 x 64 tile of one group: two independent half-chains (k-steps 0-1, 2-3).
-QW_DEV void group_mma_split(float (&c)[4], uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3,
-                            const uint32_t (&bq)[8], const float (&init)[4]) {
-    float c1[4] = {0.f, 0.f, 0.f, 0.f};
-    float c0[4] = {init[0], init[1], init[2], init[3]};
-    mma_bf16(c0, nib_pair(w0, 0), nib_pair(w2, 0), nib_pair(w0, 1), nib_pair(w2, 1), bq[0], bq[1], c0);
-    mma_bf16(c1, nib_pair(w1, 0), nib_pair(w3, 0), nib_pair(w1, 1), nib_pair(w3, 1), bq[4], bq[5], c1);
-    mma_bf16(c0, nib_pair(w0, 2), nib_pair(w2, 2), nib_pair(w0, 3), nib_pair(w2, 3), bq[2], bq[3], c0);
-    mma_bf16(c1, nib_pair(w1, 2), nib_pair(w3, 2), nib_pair(w1, 3), nib_pair(w3, 3), bq[6], bq[7], c1);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) c[e] = c0[e] + c1[e];
-}
-
 template <int RT, int NW, bool SB_VEC>
 __global__ void __launch_bounds__(NW * 32) qgemv_kernel(const QmmArgs a) {
     constexpr int NT = NW * 32;
