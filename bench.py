@@ -1,4 +1,4 @@
-"""Benchmark: Qwen3-4B 4-bit batch-1 greedy decode on B200.
+"""Benchmark: Qwen3-4B 4-bit batch-1 greedy decode on B200 (benchmark config 3).
 
 One step = one request of the reference's benchmark shape: a 512-token
 seeded-random prompt, prefill, then greedy decode of 300 tokens over a KV
@@ -59,7 +59,7 @@ CFG_4B = dict(CFG_0_6B, hidden_size=2560, intermediate_size=9728, num_hidden_lay
 CFG_32B = dict(CFG_0_6B, hidden_size=5120, intermediate_size=25600, num_hidden_layers=64,
                num_attention_heads=64, num_key_value_heads=8, tie_word_embeddings=False)
 TP_PROMPT_LEN, TP_DECODE_TOKENS = 2048, 256  # config 5: 2048-token prompt, greedy decode of 256
-REF_TOK_S = 32.75  # reference on M2-class Apple Silicon, 300-token greedy decode
+REF_TOK_S = 32.75  # the reference's published rate on M2-class Apple Silicon, 300-token greedy decode
 METRIC = "Qwen3-4B 4-bit batch-1 decode tok/s (plain & spec k=4); qmatmul HBM GB/s"
 
 

@@ -1,4 +1,4 @@
-"""Full-size Qwen3-4B (BASELINE config 3 shapes) parity on the GPU.
+"""Full-size Qwen3-4B (benchmark config 3 shapes) parity on the GPU.
 
 * device-generated weights equal the oracle's generator bit for bit;
 * prefill + decode logits against the CPU oracle (C backend).  Tolerance: on

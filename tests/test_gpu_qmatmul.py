@@ -1,6 +1,6 @@
 """quantized_matmul parity: CUDA (qgemv M<=8 / qgemm M>8) vs the CPU oracle.
 
-Shapes are BASELINE config 2 (Qwen3-4B projections) plus odd-sized edge cases.
+Shapes are benchmark config 2 (Qwen3-4B projections) plus odd-sized edge cases.
 Tolerance: the CUDA path and the oracle both accumulate in fp32 and round the
 output once to bf16, so they agree to within one bf16 rounding of values of
 the output's magnitude: |gpu - ref| <= 1e-2 * max|ref| + 1e-3 elementwise, and
