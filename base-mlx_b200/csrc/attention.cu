@@ -13,6 +13,7 @@
 // be replayed at every position; positions past max_pos raise an error flag
 // instead of being written.
 #include "attn_decode.cuh"
+#include "smem_attr.h"
 
 namespace qw {
 namespace {
@@ -223,13 +224,8 @@ cudaError_t launch(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st
 template <int RMAX>
 cudaError_t launch_decode_t(const AttnArgs& a, cudaStream_t st, bool pdl) {
     const size_t smem = sizeof(DecSmem<RMAX>);
-    static bool set = false;
-    if (!set) {
-        cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<RMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
-        if (e != cudaSuccess) return e;
-        set = true;
-    }
+    const cudaError_t e = ensure_max_dyn_smem(attn_decode_kernel<RMAX>, (int)smem);
+    if (e != cudaSuccess) return e;
     return launch(attn_decode_kernel<RMAX>, dim3(a.Hkv, a.nsplit), dim3(128), smem, st, pdl, a);
 }
 
@@ -252,12 +248,8 @@ cudaError_t launch_qk_norm_rope_kvwrite(const AttnArgs& a, bf16* qout, cudaStrea
 
 cudaError_t launch_attn_prefill(const AttnArgs& a, const bf16* qroped, cudaStream_t st) {
     const size_t smem = (size_t)(PQ * QLD + PK * KLD + PK * VLD + PQ * PLD + 3 * PQ) * sizeof(float);
-    static bool set = false;
-    if (!set) {
-        cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        set = true;
-    }
+    const cudaError_t e = ensure_max_dyn_smem(attn_prefill_kernel, (int)smem);
+    if (e != cudaSuccess) return e;
     return launch(attn_prefill_kernel, dim3(a.Hq, (a.S + PQ - 1) / PQ), dim3(128), smem, st, true, a, qroped);
 }
 

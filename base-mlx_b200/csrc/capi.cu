@@ -428,6 +428,13 @@ static void* qmm_scratch(int dev, cudaStream_t st, size_t bytes) {
     std::lock_guard<std::mutex> lk(mu);
     auto& b = bufs[{dev, st}];
     if (b.second < bytes) {
+        // growing the buffer synchronises and allocates, which a stream capture cannot hold
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        QW_CUDA(cudaStreamIsCapturing(st, &cs));
+        if (cs != cudaStreamCaptureStatusNone)
+            throw qw::Error(QW_ERR_INVALID_ARG,
+                            "qw_quantized_matmul: the stream is being captured and its activation buffer must grow "
+                            "to " + std::to_string(bytes) + " bytes; make one call at the largest M before capturing");
         if (b.first) {
             QW_CUDA(cudaStreamSynchronize(st));  // the old buffer may still be read by earlier work
             cudaFree(b.first);
@@ -551,6 +558,11 @@ extern "C" int qw_quantized_matmul_argmax_static(const void* x, const void* w, c
         a.epi = qw::EPI_LOGITS;
         a.store_logits = y_or_null ? 1 : 0;
         a.amax_partial = scratch;
+        if (!qw::qgemv_fits(a))
+            throw qw::Error(QW_ERR_INVALID_ARG, "qw_quantized_matmul_argmax_static: K = " + std::to_string(K) +
+                                                    " at M = " + std::to_string(M) +
+                                                    " does not fit the GEMV's shared-memory staging (220 KB); "
+                                                    "largest K: " + std::to_string(qw::qgemv_max_k(M)));
         cudaStream_t st = (cudaStream_t)stream;
         QW_CUDA(qw::launch_qgemv(a, st, false, 0));
         QW_CUDA(qw::launch_amax_finalize(scratch, qw::qgemv_row_blocks(a), M, argmax_dev, nullptr, st));

@@ -109,6 +109,7 @@ QW_DEV void permute16(const uint32_t (&X)[8], uint32_t (&o)[8]) {
 // with the lowest index winning ties (MLX argmax semantics).
 QW_DEV unsigned long long amax_key(float v, uint32_t idx) {
     uint32_t u = __float_as_uint(v);
+    if ((u << 1) == 0u) u = 0u;  // -0.0 and +0.0 are the same value: the lower index wins between them
     u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
     return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
 }

@@ -52,6 +52,8 @@ int qgemv_row_blocks(const QmmArgs& a);
 // Whether the GEMV's whole-K weight slab (16 or 32 rows x K) fits in shared
 // memory; long rows that do not (K = 25600 at 220 KB) go to the tiled GEMM.
 bool qgemv_fits(const QmmArgs& a);
+// Largest K (a multiple of 64) whose single-segment GEMV fits, at M rows.
+int qgemv_max_k(int M);
 // argmax[m] (and optionally packed keys) from the EPI_LOGITS per-CTA maxima.
 cudaError_t launch_amax_finalize(const unsigned long long* partial, int nrb, int M, int* out,
                                  unsigned long long* keys_out, cudaStream_t st);

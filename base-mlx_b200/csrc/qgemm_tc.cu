@@ -45,6 +45,7 @@
 
 #include "kernels.h"
 #include "qmm_epi.cuh"
+#include "smem_attr.h"
 
 namespace qw {
 namespace {
@@ -455,13 +456,8 @@ bool seg_maps(const QSeg& sg, int K, SegMaps& out) {
 
 template <int RT, int BN>
 cudaError_t launch_tc_t(const QmmArgs& a, const TcMaps& maps, dim3 grid, cudaStream_t st) {
-    static bool set = false;
-    if (!set) {
-        const cudaError_t e = cudaFuncSetAttribute(qgemm_tc_kernel<RT, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   TcPlan<RT, BN>::SMEM);
-        if (e != cudaSuccess) return e;
-        set = true;
-    }
+    const cudaError_t e = ensure_max_dyn_smem(qgemm_tc_kernel<RT, BN>, (int)TcPlan<RT, BN>::SMEM);
+    if (e != cudaSuccess) return e;
     return launch_pdl(qgemm_tc_kernel<RT, BN>, grid, dim3(TC_NT), (size_t)TcPlan<RT, BN>::SMEM, st, a, maps);
 }
 

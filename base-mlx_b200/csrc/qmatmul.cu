@@ -27,6 +27,7 @@
 
 #include "kernels.h"
 #include "qmm_epi.cuh"
+#include "smem_attr.h"
 
 namespace qw {
 namespace {
@@ -606,16 +607,9 @@ cudaError_t launch_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStrea
 
 template <int RT, int NW>
 cudaError_t launch_qgemv_t(const QmmArgs& a, int nrb, size_t smem, cudaStream_t st, bool pdl) {
-    static bool set = false;
-    if (!set) {
-        cudaError_t e = cudaFuncSetAttribute(qgemv_kernel<RT, NW, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             220 * 1024);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(qgemv_kernel<RT, NW, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     220 * 1024);
-        if (e != cudaSuccess) return e;
-        set = true;
-    }
+    cudaError_t e = ensure_max_dyn_smem(qgemv_kernel<RT, NW, true>, 220 * 1024);
+    if (e == cudaSuccess) e = ensure_max_dyn_smem(qgemv_kernel<RT, NW, false>, 220 * 1024);
+    if (e != cudaSuccess) return e;
     const int KG = a.K / 64;
     if (KG % 8 == 0) return launch_ex(qgemv_kernel<RT, NW, true>, dim3(nrb), dim3(NW * 32), smem, st, pdl, a);
     return launch_ex(qgemv_kernel<RT, NW, false>, dim3(nrb), dim3(NW * 32), smem, st, pdl, a);
@@ -634,6 +628,15 @@ bool qgemv_fits(const QmmArgs& a) {
     const int RT = a.epi == EPI_SWIGLU ? 2 : 1;
     const int NW = KG > 48 ? 8 : 4;
     return gv_layout(KG, a.M, RT, NW).total <= 220 * 1024;
+}
+
+int qgemv_max_k(int M) {
+    int best = 0;
+    for (int KG = 1; KG <= 4096; ++KG) {
+        const int NW = KG > 48 ? 8 : 4;
+        if (gv_layout(KG, M, 1, NW).total <= 220 * 1024) best = KG * 64;
+    }
+    return best;
 }
 
 cudaError_t launch_qgemv(QmmArgs a, cudaStream_t st, bool pdl, int num_sms) {

@@ -216,6 +216,9 @@ QW_API int qw_quantized_matmul(const void* x, const void* w, const void* scales,
  *     QW_STATIC_AMAX_SLOTS slots; M (1..8) * ceil(N / 16) must not exceed it,
  *     otherwise QW_ERR_INVALID_ARG with the sizes in the message
  *     (Qwen3's 151936-entry vocabulary uses 75968 slots at M = 8).
+ *   - K is bounded by the GEMV's shared-memory staging of a whole 16-row
+ *     slab: up to 17984 at M = 1, 10304 at M = 5, 7808 at M = 8; a longer
+ *     row is QW_ERR_INVALID_ARG with K and M in the message.
  *   - The first call on each device (that device current) looks the array's
  *     address up once; make that first call before any stream capture.
  *   - It calls no cudaMalloc, cudaFree or other allocating routine.

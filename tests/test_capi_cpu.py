@@ -95,3 +95,10 @@ def test_unsupported_quantization_rejected():
     with pytest.raises(q.ModelLoad):
         q.Qwen3.init_random(cfg, 1)
     json.dumps(cfg)
+
+
+def test_python_static_slot_count_matches_header():
+    """qwen3_b200.STATIC_AMAX_SLOTS mirrors QW_STATIC_AMAX_SLOTS of the header."""
+    import qwen3_b200 as q
+    m = re.search(r"#define\s+QW_STATIC_AMAX_SLOTS\s+(\d+)", open(HEADER).read())
+    assert m and int(m.group(1)) == q.STATIC_AMAX_SLOTS

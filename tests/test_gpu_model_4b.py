@@ -17,6 +17,7 @@
 import numpy as np
 import pytest
 
+from oracle import numerics as nm
 from oracle import synth
 
 pytestmark = pytest.mark.gpu
@@ -124,9 +125,11 @@ def test_4b_prefill_long_prompt_matches_chunked(m4b):
         lg2, am2 = m.forward(prompt[i:i + 64], c2)
     d = np.abs(lg1 - lg2)
     assert d.max() <= 0.25 and d.mean() <= 0.04, (d.max(), d.mean())
-    for layer in (0, 17, 35):
-        k1 = c1.read(layer, "k", 0, 512).astype(np.int64)
-        k2 = c2.read(layer, "k", 0, 512).astype(np.int64)
-        assert (k1 == k2).mean() > 0.9, layer
+    # cached keys are unit-RMS per head (k_norm, then RoPE): bound every element
+    for layer, bound in ((0, 0.0625), (17, 0.25), (35, 0.5)):
+        k1 = nm.bf16_bits_to_f32(c1.read(layer, "k", 0, 512))
+        k2 = nm.bf16_bits_to_f32(c2.read(layer, "k", 0, 512))
+        dk = np.abs(k1 - k2)
+        assert dk.max() <= bound and dk.mean() <= 0.02, (layer, dk.max(), dk.mean())
     c1.close()
     c2.close()

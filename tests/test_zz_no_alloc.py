@@ -69,3 +69,31 @@ def test_static_argmax_rejects_oversize():
         q.quantized_matmul_argmax_static(p, p, p, p, 0, p, M, N, K)
     with pytest.raises(q.Error):
         q.quantized_matmul_argmax_static(p, p, p, p, 0, p, 9, 16, K)
+    # a row too long for the GEMV's shared-memory staging is an argument error naming the sizes
+    with pytest.raises(q.Error, match="does not fit"):
+        q.quantized_matmul_argmax_static(p, p, p, p, 0, p, 8, 16, 25600)
+
+
+def test_static_argmax_on_two_devices():
+    """The scratch address and the kernel's shared-memory opt-in are per device:
+    a call on device 1 after device 0 in the same process must work."""
+    import torch
+    import qwen3_b200 as q
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    M, K, N = 8, 2560, 4096
+    w, s, b = synth.quantized_weight_c(78, 3, N, K)
+    rng = np.random.default_rng(9)
+    x = nm.f32_to_bf16_bits(nm.bf16_round(rng.standard_normal((M, K)).astype(np.float32))).view(np.int16)
+    got = []
+    for dev in (0, 1):
+        d = f"cuda:{dev}"
+        with torch.cuda.device(dev):
+            wt, st_, bt = (torch.from_numpy(a).to(d) for a in (w.view(np.int32), s.view(np.int16), b.view(np.int16)))
+            xt = torch.from_numpy(x).to(d)
+            am = torch.full((M,), -1, dtype=torch.int32, device=d)
+            q.quantized_matmul_argmax_static(xt.data_ptr(), wt.data_ptr(), st_.data_ptr(), bt.data_ptr(), 0,
+                                             am.data_ptr(), M, N, K, stream=torch.cuda.current_stream(dev).cuda_stream)
+            torch.cuda.synchronize(dev)
+            got.append(am.cpu().numpy())
+    assert list(got[0]) == list(got[1])
