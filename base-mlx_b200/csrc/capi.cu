@@ -296,6 +296,52 @@ int qw_forward(qw_model* m, qw_cache* c, const uint32_t* ids, int n, int all_row
     });
 }
 
+int qw_forward_trace(qw_model* m, qw_cache* c, const uint32_t* ids, int n, uint16_t* residual_out,
+                     uint16_t* mid_out, uint16_t* attn_out, uint16_t* logits_out, uint32_t* argmax_out) {
+    return guard([&] {
+        need(m && c && ids && residual_out, "model/cache/ids/residual_out");
+        need(c->m == m, "cache belongs to another model");
+        need(n >= 1, "n must be >= 1");
+        if (c->seq_len + n > c->max_pos)
+            throw qw::Error(QW_ERR_KV_EXHAUSTED, "KV cache exhausted: requested " + std::to_string(c->seq_len + n) +
+                                                     " positions, max " + std::to_string(c->max_pos));
+        check_ids(m, ids, n);
+        QW_CUDA(cudaSetDevice(m->device));
+        qw::ensure_workspace(m, n, 1);
+        const int L = m->cfg.layers, H = m->cfg.hidden, QD = m->hq_l * m->cfg.head_dim;
+        const size_t tr_bytes = (size_t)(L + 1) * n * H * 2, mid_bytes = (size_t)L * n * H * 2,
+                     attn_bytes = (size_t)L * n * QD * 2;
+        bf16* tr = nullptr;
+        QW_CUDA(cudaMalloc(&tr, tr_bytes + mid_bytes + attn_bytes));
+        struct Release {
+            qw_model* m;
+            bf16* p;
+            ~Release() {
+                m->trace = m->trace_mid = m->trace_attn = nullptr;
+                cudaFree(p);
+            }
+        } rel{m, tr};
+        m->trace = tr;
+        m->trace_mid = tr + tr_bytes / 2;
+        m->trace_attn = m->trace_mid + mid_bytes / 2;
+        std::vector<int> h(ids, ids + n);
+        cudaStream_t st = m->stream;
+        QW_CUDA(cudaMemcpyAsync(m->ws.ids, h.data(), (size_t)n * 4, cudaMemcpyHostToDevice, st));
+        qw::forward_dev(m, c, m->ws.ids, n, 1, logits_out != nullptr, m->ws.argmax, st, nullptr, nullptr, nullptr);
+        QW_CUDA(cudaMemcpyAsync(residual_out, tr, tr_bytes, cudaMemcpyDeviceToHost, st));
+        if (mid_out) QW_CUDA(cudaMemcpyAsync(mid_out, m->trace_mid, mid_bytes, cudaMemcpyDeviceToHost, st));
+        if (attn_out) QW_CUDA(cudaMemcpyAsync(attn_out, m->trace_attn, attn_bytes, cudaMemcpyDeviceToHost, st));
+        if (logits_out)
+            QW_CUDA(cudaMemcpyAsync(logits_out, m->ws.logits, (size_t)m->vocab_l * 2, cudaMemcpyDeviceToHost, st));
+        int am = 0;
+        QW_CUDA(cudaMemcpyAsync(&am, m->ws.argmax, 4, cudaMemcpyDeviceToHost, st));
+        QW_CUDA(cudaStreamSynchronize(st));
+        c->seq_len += n;
+        qw::check_device_err(m);
+        if (argmax_out) *argmax_out = (uint32_t)am;
+    });
+}
+
 int qw_generate_greedy(qw_model* m, const uint32_t* prompt, int n_prompt, int max_new, const uint32_t* eos,
                        int n_eos, uint32_t* out, int* n_out, qw_gen_stats* stats) {
     return guard([&] {

@@ -64,14 +64,20 @@ QW_DEV uint32_t nib_pair(uint32_t w, int j) {
 // bf16x2 (128.0, 128.0): the A operand whose product with B yields 128 * sum(x).
 #define QW_BF16X2_128 0x43004300u
 
-// fp16 variant used by the decode GEMV: 0x6400 is fp16 1024.0 and its ten
-// mantissa bits take a nibble at bits 0-3 (1024 + q) or at bits 4-7
-// (1024 + 16q) without shifting, so the eight nibbles of a word become four
-// fp16 pairs with one shift and four LOP3s:
-//   nib_even(w, 0) = (e0, e4), nib_even(w, 8) = (e2, e6)      [1024 + q]
-//   nib_odd (w, 0) = (e1, e5), nib_odd (w, 8) = (e3, e7)      [1024 + 16q]
-QW_DEV uint32_t nib_even(uint32_t w) { return (w & 0x000F000Fu) | 0x64006400u; }
-QW_DEV uint32_t nib_odd(uint32_t w) { return (w & 0x00F000F0u) | 0x64006400u; }
+// fp16 variant used by the decode GEMVs: a nibble left in the low mantissa
+// bits of an fp16 with a zero exponent field is the subnormal q * 2^-24, and
+// one at bits 4-7 is 16q * 2^-24, both exact.  The eight nibbles of a word
+// become four fp16 pairs with one shift and four ANDs, and the tensor core
+// multiplies the exact small integers q (scaled by 2^-24, folded back into
+// the group scale) -- no offset, so the fp32 accumulation carries no
+// cancellation:
+//   nib_even(w, 0) = (e0, e4), nib_even(w, 8) = (e2, e6)      [q * 2^-24]
+//   nib_odd (w, 0) = (e1, e5), nib_odd (w, 8) = (e3, e7)      [16q * 2^-24]
+QW_DEV uint32_t nib_even(uint32_t w) { return w & 0x000F000Fu; }
+QW_DEV uint32_t nib_odd(uint32_t w) { return w & 0x00F000F0u; }
+// 2^24 and 2^20: the factors that turn the subnormal products back into q*x and 16q*x
+#define QW_NIB_SCALE 16777216.0f
+#define QW_NIB_SCALE_ODD 1048576.0f
 
 // D[16x8] (fp32) = A[16x16] (fp16, row) * B[16x8] (fp16, col) + C (same fragment layout as mma_bf16).
 QW_DEV void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1,

@@ -104,6 +104,9 @@ struct MkArgs {
     unsigned* tile_ctr;  // [max tiles] arrivals per split tile (reset by the finisher)
     int* err;
     int depth;       // ring slots per warp (the kernel's DEPTH)
+    bf16* trace;     // diagnostics: residual stream after the embedding and every layer, [L + 1][M][H]
+    bf16* trace_mid;   // diagnostics: residual after each attention block, [L][M][H]
+    bf16* trace_attn;  // diagnostics: attention output of each layer, [L][M][QD]
     unsigned off_union, off_misc, off_tab;
 };
 
@@ -143,8 +146,8 @@ QW_DEV void mma_zero(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint3
         : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
 }
-QW_DEV uint32_t lo4(uint32_t w) { return (w & 0x000F000Fu) | 0x64006400u; }   // 1024 + q
-QW_DEV uint32_t hi4(uint32_t w) { return (w & 0x00F000F0u) | 0x64006400u; }   // 1024 + 16q
+QW_DEV uint32_t lo4(uint32_t w) { return nib_even(w); }  // q * 2^-24 (exact fp16 subnormal)
+QW_DEV uint32_t hi4(uint32_t w) { return nib_odd(w); }   // 16q * 2^-24
 
 // Number of GEMV phases in a launch and their descriptors, in stream order:
 // layer l -> q|k|v, o, gate|up, down; then lm_head when logits are wanted.
@@ -482,6 +485,15 @@ QW_DEV void cta_arrive(const MkArgs& a) {
     if (threadIdx.x == 0) red_release_add(a.sync, 1u);
 }
 
+// Diagnostics: copy n bf16 values (a multiple of 8) from src to dst.
+QW_DEV void trace_copy_n(const bf16* src_, bf16* dst_, int n) {
+    const uint4* src = reinterpret_cast<const uint4*>(src_);
+    uint4* dst = reinterpret_cast<uint4*>(dst_);
+    for (int i = threadIdx.x; i < n / 8; i += MK_NT) dst[i] = __ldcg(src + i);
+}
+// the residual stream (final for layer l - 1) into trace[l]
+QW_DEV void trace_copy(const MkArgs& a, int l) { trace_copy_n(a.x, a.trace + (size_t)l * a.M * a.H, a.M * a.H); }
+
 // Attention items run on the whole CTA (taken by whole CTAs only).
 struct BlockSync {
     QW_DEV void operator()() const { __syncthreads(); }
@@ -520,13 +532,14 @@ QW_DEV void granule_mma(const unsigned char* gp, int lane, const GAct& x, float 
     mma_zero(ch, hi4(wv.x), hi4(a8), hi4(wv.y), hi4(b8), x.xa.z, x.xa.w);
     mma_acc(cl, lo4(wv.z), lo4(c8), lo4(wv.w), lo4(d8), x.xb.x, x.xb.y);
     mma_acc(ch, hi4(wv.z), hi4(c8), hi4(wv.w), hi4(d8), x.xb.z, x.xb.w);
-    const float s0 = bits_lo_f(sb.x), b0 = bits_hi_f(sb.x);
-    const float s1 = bits_lo_f(sb.y), b1 = bits_hi_f(sb.y);
+    // the chains hold q*x * 2^-24 (k-steps 0, 2) and 16q*x * 2^-24 (k-steps 1, 3)
+    const float s0 = bits_lo_f(sb.x) * QW_NIB_SCALE, b0 = bits_hi_f(sb.x);
+    const float s1 = bits_lo_f(sb.y) * QW_NIB_SCALE, b1 = bits_hi_f(sb.y);
     const float s016 = s0 * 0.0625f, s116 = s1 * 0.0625f;
-    acc[0] = fmaf(s0, cl[0] + x.z0, fmaf(s016, ch[0], fmaf(b0, x.sx0, acc[0])));
-    acc[1] = fmaf(s0, cl[1] + x.z1, fmaf(s016, ch[1], fmaf(b0, x.sx1, acc[1])));
-    acc[2] = fmaf(s1, cl[2] + x.z0, fmaf(s116, ch[2], fmaf(b1, x.sx0, acc[2])));
-    acc[3] = fmaf(s1, cl[3] + x.z1, fmaf(s116, ch[3], fmaf(b1, x.sx1, acc[3])));
+    acc[0] = fmaf(s0, cl[0], fmaf(s016, ch[0], fmaf(b0, x.sx0, acc[0])));
+    acc[1] = fmaf(s0, cl[1], fmaf(s016, ch[1], fmaf(b0, x.sx1, acc[1])));
+    acc[2] = fmaf(s1, cl[2], fmaf(s116, ch[2], fmaf(b1, x.sx0, acc[2])));
+    acc[3] = fmaf(s1, cl[3], fmaf(s116, ch[3], fmaf(b1, x.sx1, acc[3])));
 }
 
 // ---- one GEMV phase --------------------------------------------------------
@@ -822,8 +835,14 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
                     uint4* d = reinterpret_cast<uint4*>(a.x + (size_t)m * a.H + k);
                     d[0] = make_uint4(w8[0], w8[1], w8[2], w8[3]);
                     d[1] = make_uint4(w8[4], w8[5], w8[6], w8[7]);
+                    if (a.trace) {
+                        uint4* t = reinterpret_cast<uint4*>(a.trace + (size_t)m * a.H + k);
+                        t[0] = d[0];
+                        t[1] = d[1];
+                    }
                 }
             }
+            if (l > 0 && a.trace && blockIdx.x == 0) trace_copy(a, l);
             __syncthreads();
             gemv_phase<K_QKV, DEPTH>(a, tab[4 * l + K_QKV], M, xs, seeds, red, pc, gpos, ring, false, mm);
             // the attention tiles' cached K/V rows do not depend on this step:
@@ -865,6 +884,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
             float* red = seeds + (size_t)lin.KG * 4 * SEEDF;
             ok = cta_wait(a, arrivals * C, mm);
             if (!ok) break;
+            if (a.trace && blockIdx.x == 0) trace_copy_n(a.attn, a.trace_attn + (size_t)l * a.M * a.QD, a.M * a.QD);
             StageSrc s{a.attn, a.QD, 0, nullptr};
             stage_acts(a, s, a.QD, M, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
             __syncthreads();
@@ -880,6 +900,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
             float* red = seeds + (size_t)lin.KG * 4 * SEEDF;
             ok = cta_wait(a, arrivals * C, mm);
             if (!ok) break;
+            if (a.trace && blockIdx.x == 0) trace_copy_n(a.x, a.trace_mid + (size_t)l * a.M * a.H, a.M * a.H);
             StageSrc s{a.x, a.H, 0, Ly.post_norm};
             stage_acts(a, s, a.H, M, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
             __syncthreads();
@@ -911,6 +932,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
         float* seeds = reinterpret_cast<float*>(uni + MK_UNI_RESERVED + (size_t)lin.KG * rows * XW * 4);
         float* red = seeds + (size_t)lin.KG * 4 * SEEDF;
         ok = cta_wait(a, arrivals * C, mm);
+        if (ok && a.trace && blockIdx.x == 0) trace_copy(a, a.L);
         if (ok) {
             StageSrc s{a.x, a.H, M - rows, a.final_norm};
             stage_acts(a, s, a.H, rows, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
@@ -1304,6 +1326,9 @@ bool mk_forward(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_mo
     a.part_g = s->part_g;
     a.tile_ctr = s->tile_ctr;
     a.err = m->d_err;
+    a.trace = m->trace;
+    a.trace_mid = m->trace_mid;
+    a.trace_attn = m->trace_attn;
     if (R <= 8) return mk_launch_t<8>(m, a, st, 0);
     if (R <= 16) return mk_launch_t<16>(m, a, st, 1);
     return mk_launch_t<32>(m, a, st, 2);

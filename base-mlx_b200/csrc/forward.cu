@@ -87,6 +87,7 @@ void forward_dev(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_m
         return;
 
     QW_CUDA(launch_embed(d_ids, S, m->embed.w, m->embed.s, m->embed.b, H, cf.vocab, w.x, m->d_err, st, true));
+    if (m->trace) QW_CUDA(cudaMemcpyAsync(m->trace, w.x, (size_t)S * H * 2, cudaMemcpyDeviceToDevice, st));
 
     AttnArgs aa;
     std::memset(&aa, 0, sizeof(aa));
@@ -139,6 +140,9 @@ void forward_dev(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_m
             QW_CUDA(launch_qk_norm_rope_kvwrite(aa, w.qr, st));
             QW_CUDA(launch_attn_prefill(aa, w.qr, st));
         }
+        if (m->trace)
+            QW_CUDA(cudaMemcpyAsync(m->trace_attn + (size_t)l * S * QD, w.attn, (size_t)S * QD * 2,
+                                    cudaMemcpyDeviceToDevice, st));
         {
             QmmArgs a = qmm_base(m, w.attn, QD, S, QD);
             a.seg[0] = seg_of(L.o, tp ? (void*)w.f32 : (void*)w.x, H);
@@ -150,6 +154,9 @@ void forward_dev(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_m
                 QW_CUDA(launch_resid_add_f32(w.x, w.f32, S * H, st));
             }
         }
+        if (m->trace)
+            QW_CUDA(cudaMemcpyAsync(m->trace_mid + (size_t)l * S * H, w.x, (size_t)S * H * 2,
+                                    cudaMemcpyDeviceToDevice, st));
         xin = w.x;
         if (!decode) {
             QW_CUDA(launch_rmsnorm(w.x, L.post_norm, w.h, S, H, cf.eps, st));
@@ -175,6 +182,9 @@ void forward_dev(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_m
                 QW_CUDA(launch_resid_add_f32(w.x, w.f32, S * H, st));
             }
         }
+        if (m->trace)
+            QW_CUDA(cudaMemcpyAsync(m->trace + (size_t)(l + 1) * S * H, w.x, (size_t)S * H * 2,
+                                    cudaMemcpyDeviceToDevice, st));
     }
 
     if (logits_mode) {

@@ -113,6 +113,14 @@ struct qw_model {
     qw_cache* gen_cache = nullptr;  // cache used by the generate entry points
     void* spec_state = nullptr;     // speculative-decoding graphs (spec.cu)
     qw::MkState* mk = nullptr;      // persistent decode kernel state (decode_mk.cu)
+    // diagnostics (qw_forward_trace): when set, a forward copies the residual
+    // stream [S, hidden] after the embedding and after every layer into
+    // trace[0..layers] (bf16, [layers + 1][S][hidden]), the residual after
+    // each layer's attention block into trace_mid ([layers][S][hidden]) and
+    // the attention output (o_proj input) into trace_attn ([layers][S][heads * 128])
+    bf16* trace = nullptr;
+    bf16* trace_mid = nullptr;
+    bf16* trace_attn = nullptr;
     ~qw_model();
 };
 

@@ -355,8 +355,7 @@ __global__ void __launch_bounds__(NW * 32) qgemv_kernel(const QmmArgs a) {
         const float2 xe = *reinterpret_cast<const float2*>(xsum + gl * 16 + 2 * t);
         const float2 xo = *reinterpret_cast<const float2*>(xsum + gl * 16 + 8 + 2 * t);
         const float xt0 = xe.x + xo.x, xt1 = xe.y + xo.y;
-        const float ie[4] = {-1024.f * xe.x, -1024.f * xe.y, -1024.f * xe.x, -1024.f * xe.y};
-        const float io[4] = {-1024.f * xo.x, -1024.f * xo.y, -1024.f * xo.x, -1024.f * xo.y};
+        const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int rt = 0; rt < RT; ++rt) {
             const int r0 = rt * 16 + g;
@@ -364,11 +363,13 @@ __global__ void __launch_bounds__(NW * 32) qgemv_kernel(const QmmArgs a) {
             const uint2 wb = *reinterpret_cast<const uint2*>(W + (r0 + 8) * L.rs + gl * 8 + 2 * t);
             const uint32_t wa8x = wa.x >> 8, wb8x = wb.x >> 8, wa8y = wa.y >> 8, wb8y = wb.y >> 8;
             float ce[4], co[4];
-            mma_f16(ce, nib_even(wa.x), nib_even(wb.x), nib_even(wa8x), nib_even(wb8x), be.x, be.y, ie);
-            mma_f16(co, nib_odd(wa.x), nib_odd(wb.x), nib_odd(wa8x), nib_odd(wb8x), bo.x, bo.y, io);
+            mma_f16(ce, nib_even(wa.x), nib_even(wb.x), nib_even(wa8x), nib_even(wb8x), be.x, be.y, zero4);
+            mma_f16(co, nib_odd(wa.x), nib_odd(wb.x), nib_odd(wa8x), nib_odd(wb8x), bo.x, bo.y, zero4);
             mma_f16(ce, nib_even(wa.y), nib_even(wb.y), nib_even(wa8y), nib_even(wb8y), be.z, be.w, ce);
             mma_f16(co, nib_odd(wa.y), nib_odd(wb.y), nib_odd(wa8y), nib_odd(wb8y), bo.z, bo.w, co);
-            const float s0 = u16_to_f(Ssm[r0 * L.ngp + gl]), s1 = u16_to_f(Ssm[(r0 + 8) * L.ngp + gl]);
+            // 2^24 undoes the subnormal encoding of the nibbles (exact: a power of two)
+            const float s0 = u16_to_f(Ssm[r0 * L.ngp + gl]) * QW_NIB_SCALE;
+            const float s1 = u16_to_f(Ssm[(r0 + 8) * L.ngp + gl]) * QW_NIB_SCALE;
             const float b0 = u16_to_f(Bsm[r0 * L.ngp + gl]), b1 = u16_to_f(Bsm[(r0 + 8) * L.ngp + gl]);
             // sum q*x = ce + co/16 (odd nibbles entered as 16q)
             acc[rt][0] = fmaf(s0, fmaf(co[0], 0.0625f, ce[0]), acc[rt][0]);

@@ -124,6 +124,7 @@ SIGNATURES = {
     "qw_kv_slice_update": [P, I, I, U16P, I, I],
     "qw_kv_read": [P, I, I, U16P, I, I],
     "qw_forward": [P, P, U32P, I, I, U16P, U32P],
+    "qw_forward_trace": [P, P, U32P, I, U16P, U16P, U16P, U16P, U32P],
     "qw_generate_greedy": [P, U32P, I, I, U32P, I, U32P, ctypes.POINTER(I), ctypes.POINTER(GenStats)],
     "qw_generate_sampled": [P, U32P, I, I, ctypes.c_float, ctypes.c_float, ctypes.c_uint64, I, U32P, I, U32P,
                             ctypes.POINTER(I), ctypes.POINTER(GenStats)],
@@ -292,6 +293,24 @@ class Qwen3:
     def forward_multi(self, tokens, cache: KvCache, want_logits: bool = True):
         """Architecture::forward_multi: logits of every row [S, vocab], argmax per row."""
         return self._forward(tokens, cache, True, want_logits)
+
+    def forward_trace(self, tokens, cache: KvCache):
+        """forward() that also returns intermediate values as float32: the residual
+        stream after the embedding and after every layer [layers + 1, n, hidden],
+        the residual after each attention block [layers, n, hidden], each layer's
+        attention output [layers, n, heads * head_dim]; then logits [vocab], argmax."""
+        ids, ids_p = _u32(tokens)
+        inf = self.info
+        n = len(ids)
+        qd = inf.num_heads // inf.tp_size * inf.head_dim
+        res = np.empty((inf.num_layers + 1, n, inf.hidden), np.uint16)
+        mid = np.empty((inf.num_layers, n, inf.hidden), np.uint16)
+        att = np.empty((inf.num_layers, n, qd), np.uint16)
+        logits = np.empty(self.vocab_local, np.uint16)
+        am = np.empty(1, np.uint32)
+        check(lib().qw_forward_trace(self.h, cache.h, ids_p, n, res.ctypes.data_as(U16P), mid.ctypes.data_as(U16P),
+                                     att.ctypes.data_as(U16P), logits.ctypes.data_as(U16P), am.ctypes.data_as(U32P)))
+        return bf16_to_f32(res), bf16_to_f32(mid), bf16_to_f32(att), bf16_to_f32(logits), int(am[0])
 
     def generate_greedy(self, prompt, max_new: int, eos=None) -> GenerationResult:
         p, pp = _u32(prompt)

@@ -148,6 +148,19 @@ QW_API int qw_kv_read(const qw_cache* c, int layer, int which_v, uint16_t* dst_h
 QW_API int qw_forward(qw_model* m, qw_cache* c, const uint32_t* ids_host, int n, int all_rows,
                       uint16_t* logits_out_host, uint32_t* argmax_out_host);
 
+/* Diagnostics (no reference counterpart; an MLX caller can inspect any
+ * intermediate array): Architecture::forward of `n` tokens that also copies
+ * the residual stream after the embedding and after every layer to
+ * residual_out_host (bf16 [num_layers + 1][n][hidden]), the residual after
+ * every layer's attention block to mid_out_host (optional, bf16
+ * [num_layers][n][hidden]) and every layer's attention output (the o_proj
+ * input) to attn_out_host (optional, bf16 [num_layers][n][heads * head_dim]).
+ * Same decode / prefill path as qw_forward; allocates and frees a device
+ * buffer for the copies. */
+QW_API int qw_forward_trace(qw_model* m, qw_cache* c, const uint32_t* ids_host, int n, uint16_t* residual_out_host,
+                            uint16_t* mid_out_host, uint16_t* attn_out_host, uint16_t* logits_out_host,
+                            uint32_t* argmax_out_host);
+
 /* ---- generation --------------------------------------------------------- */
 
 /* Greedy generation (temperature 0).  out_host receives up to max_new ids (a

@@ -115,6 +115,8 @@ class QLinearRef:
         x = np.ascontiguousarray(x, dtype=np.float32)
         if self.backend == "c":
             return nm.bf16_round(qmm_c(x, self.w, self.s, self.b))
+        if self.backend == "torch":
+            return nm.bf16_round(qmm_torch(x, self.w, self.s, self.b))
         return nm.bf16_round(x @ self.dequant().T)
 
 
@@ -205,33 +207,58 @@ class Qwen3Ref:
         pos = np.arange(off, off + S)
         scale = np.float32(1.0) / np.sqrt(np.float32(self.D))
         x = self.embed_rows(tokens)
-        for li, ly in enumerate(self.layers):
-            h = rms_norm(x, ly["in_norm"], self.eps)
-            q = ly["q"].forward(h).reshape(S, self.Hq, self.D)
-            k = ly["k"].forward(h).reshape(S, self.Hkv, self.D)
-            v = ly["v"].forward(h).reshape(S, self.Hkv, self.D)
-            q = rms_norm(q, ly["q_norm"], self.eps)
-            k = rms_norm(k, ly["k_norm"], self.eps)
-            q = rope(q, pos, self.cos, self.sin)
-            k = rope(k, pos, self.cos, self.sin)
-            cache.k[li][:, off:off + S, :] = k.transpose(1, 0, 2)
-            cache.v[li][:, off:off + S, :] = v.transpose(1, 0, 2)
-            attn = sdpa(q, cache.k[li][:, :off + S], cache.v[li][:, :off + S], off, scale)
-            o = ly["o"].forward(attn)
-            x = nm.bf16_round(x + o)
-            h2 = rms_norm(x, ly["post_norm"], self.eps)
-            g = ly["gate"].forward(h2)
-            u = ly["up"].forward(h2)
-            mlp = ly["down"].forward(silu_mul(g, u))
-            x = nm.bf16_round(x + mlp)
+        if trace is not None:
+            trace.append(x.copy())
+        for li in range(self.L):
+            x = self.layer(li, x, cache, off)
             if trace is not None:
                 trace.append(x.copy())
-        x = rms_norm(x, self.norm, self.eps)
-        if not return_all:
-            x = x[S - 1:S]
-        logits = self.lm_head_fwd(x)
+        logits = self.head(x if return_all else x[S - 1:S])
         cache.seq_len += S
         return logits if return_all else logits[0]
+
+    def layer(self, li: int, x: np.ndarray, cache: KvCacheRef, off: int) -> np.ndarray:
+        """One decoder layer (qwen3.rs:381-541) on rows x [S, H] at positions
+        off..off+S: writes this layer's K/V rows into the cache and returns the
+        residual stream after the layer.  The cache's seq_len is not changed."""
+        attn = self.attention(li, x, cache, off)
+        return self.mlp(li, self.attn_residual(li, x, attn))
+
+    def attention(self, li: int, x: np.ndarray, cache: KvCacheRef, off: int) -> np.ndarray:
+        """qkv_block, q/k norm, RoPE, KV write and SDPA (qwen3.rs:381-518): the
+        attention output [S, Hq*D] (bf16 values), the o_proj input."""
+        ly = self.layers[li]
+        S = x.shape[0]
+        pos = np.arange(off, off + S)
+        scale = np.float32(1.0) / np.sqrt(np.float32(self.D))
+        h = rms_norm(x, ly["in_norm"], self.eps)
+        q = ly["q"].forward(h).reshape(S, self.Hq, self.D)
+        k = ly["k"].forward(h).reshape(S, self.Hkv, self.D)
+        v = ly["v"].forward(h).reshape(S, self.Hkv, self.D)
+        q = rms_norm(q, ly["q_norm"], self.eps)
+        k = rms_norm(k, ly["k_norm"], self.eps)
+        q = rope(q, pos, self.cos, self.sin)
+        k = rope(k, pos, self.cos, self.sin)
+        cache.k[li][:, off:off + S, :] = k.transpose(1, 0, 2)
+        cache.v[li][:, off:off + S, :] = v.transpose(1, 0, 2)
+        return sdpa(q, cache.k[li][:, :off + S], cache.v[li][:, :off + S], off, scale)
+
+    def attn_residual(self, li: int, x: np.ndarray, attn: np.ndarray) -> np.ndarray:
+        """o_proj + residual (qwen3.rs:519-520)."""
+        return nm.bf16_round(x + self.layers[li]["o"].forward(attn))
+
+    def mlp(self, li: int, x: np.ndarray) -> np.ndarray:
+        """post-attention RMSNorm, mlp_block and residual (kernels.rs:55-78, qwen3.rs:521-541)."""
+        ly = self.layers[li]
+        h2 = rms_norm(x, ly["post_norm"], self.eps)
+        g = ly["gate"].forward(h2)
+        u = ly["up"].forward(h2)
+        mlp = ly["down"].forward(silu_mul(g, u))
+        return nm.bf16_round(x + mlp)
+
+    def head(self, x: np.ndarray) -> np.ndarray:
+        """Final RMSNorm and lm_head (qwen3.rs:545-561) of rows x [S, H] -> logits [S, V]."""
+        return self.lm_head_fwd(rms_norm(x, self.norm, self.eps))
 
 
 # ------------------------------------------------------------ C helper ---
@@ -252,6 +279,29 @@ def _lib():
         lib.qmm_ref_f32.restype = ctypes.c_int
         _LIB = lib
     return _LIB
+
+
+def qmm_torch(x, w, s, b) -> np.ndarray:
+    """y[M,N] = x[M,K] . dequant(W)^T in fp32 with torch on the CPU: the weight
+    is dequantised exactly (s*q + b, one rounding) one 4096-row block at a time
+    and multiplied with torch's fp32 matmul (no cache of dequantised weights,
+    so a 4B-parameter model fits in host memory).  For long teacher-forced
+    sequences where the C loop would take minutes."""
+    import torch
+    xt = torch.from_numpy(np.ascontiguousarray(x, np.float32))
+    N, KW = w.shape
+    K = KW * 8
+    y = torch.empty((xt.shape[0], N), dtype=torch.float32)
+    shifts = torch.arange(0, 32, 4, dtype=torch.int64)
+    for n0 in range(0, N, 4096):
+        n1 = min(N, n0 + 4096)
+        wb = torch.from_numpy(np.ascontiguousarray(w[n0:n1]).view(np.int32)).to(torch.int64) & 0xFFFFFFFF
+        q = ((wb.unsqueeze(-1) >> shifts) & 0xF).to(torch.float32).reshape(n1 - n0, K // 64, 64)
+        sc = torch.from_numpy(nm.bf16_bits_to_f32(s[n0:n1])).unsqueeze(-1)
+        bi = torch.from_numpy(nm.bf16_bits_to_f32(b[n0:n1])).unsqueeze(-1)
+        deq = (q * sc + bi).reshape(n1 - n0, K)
+        y[:, n0:n1] = xt @ deq.T
+    return y.numpy()
 
 
 def qmm_c(x, w, s, b, threads: int = 0) -> np.ndarray:
