@@ -9,10 +9,12 @@
 // (kernels.rs:55-78), the final norm -> lm_head -> argmax (qwen3.rs:78-91,
 // engine.rs:197-201) and the greedy step bookkeeping.
 //
-// Grid = one CTA per SM (cooperative launch: all CTAs are resident), 16 warps.
-// Phases are separated by a grid-wide arrival counter; every wait is bounded
-// (2 s of globaltimer), after which the launch sets QW_DERR_TIMEOUT, raises an
-// abort flag that makes every other wait return, drains its copies and exits.
+// Grid = one CTA per SM (cooperative launch: all CTAs are resident) of 16
+// compute warps and one producer warp.  Phases are separated by a grid-wide
+// arrival counter; every wait is bounded (2 s of globaltimer), after which the
+// launch sets QW_DERR_TIMEOUT, raises an abort flag that makes every other wait
+// return, drains its copies and exits.  The compute warps synchronise among
+// themselves with a named barrier (the producer warp never joins it).
 //
 // Weight stream.  At model load every quantized linear is repacked into
 // 576-byte granules (16 rows x 64 inputs).  Bytes 0..511 hold the nibbles so
@@ -21,19 +23,21 @@
 // group's four mma.m16n8k16 k-steps: steps 0 and 2 take (w & 0x000F000F) |
 // 0x64006400 (fp16 1024 + q), steps 1 and 3 take (w & 0x00F000F0) | 0x64006400
 // (1024 + 16q), each on two accumulator chains seeded with -1024 * sum(x).
-// Bytes 512..575 hold the 16 rows' bf16 scales and biases, 8 bytes per row
-// pair (g, g+8).  Work is split stream-K style: every CTA owns an equal
-// contiguous range of a phase's (tile, group) pairs and every warp an equal
-// contiguous sixteenth of it; tiles split between CTAs are finished by the
-// last CTA to arrive, summing partials in CTA order (results do not depend on
-// arrival order or on the number of rows).
-// Each warp streams its own granule sequence -- across tile, phase and layer
-// boundaries, since weights never depend on activations -- through a private
-// ring of shared-memory slots with 16-byte cp.async copies, `depth` granules
-// ahead of the one it computes, so HBM keeps streaming while the CTA waits at
-// a phase barrier.  Copies are committed two granules per group: the fixed
-// cost of a commit/wait pair per granule held a copy-only stream near half
-// the HBM rate.
+// The nibbles reach the tensor core as exact fp16 subnormals (q * 2^-24 and,
+// for the high nibble of a byte, 16q * 2^-24, whose k-steps take x/16), so the
+// fp32 accumulation carries no offset to cancel.  Bytes 512..575 hold the 16
+// rows' bf16 scales (pre-multiplied by 2^24 at packing, exact) and biases,
+// 8 bytes per row pair (g, g+8).  Every CTA owns whole 16-row tiles of a phase
+// and every warp an equal contiguous sixteenth of the CTA's (tile, group)
+// pairs; tile partial sums are combined across warps in warp order (results
+// do not depend on the number of rows).
+// Weight stream: weights never depend on activations, so the producer warp
+// (lane w serving compute warp w) walks warp w's granule sequence across tile,
+// phase and layer boundaries and copies it, R granules (4.6 KB) per bulk copy
+// (cp.async.bulk, completion counted on an mbarrier), into a private ring of
+// two stages per compute warp; the compute warp releases a stage through a
+// second mbarrier.  HBM keeps streaming while the compute warps wait at a
+// phase barrier, and no compute warp spends issue slots on copies.
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -42,13 +46,19 @@
 
 #include "attn_decode.cuh"
 #include "model.h"
+#include "smem_attr.h"
 
 namespace qw {
 
 namespace {
 
-constexpr int MK_NW = 16;
-constexpr int MK_NT = MK_NW * 32;
+#ifndef QW_MK_NW
+#define QW_MK_NW 16
+#endif
+constexpr int MK_NW = QW_MK_NW;           // compute warps
+constexpr int MK_NT = MK_NW * 32;         // compute threads (the named barrier's count)
+constexpr int MK_THREADS = MK_NT + 32;    // + the producer warp
+constexpr int MK_NSLOT = 2;               // ring stages per compute warp
 constexpr int GR_BYTES = 576;  // one granule: 512 B nibbles + 64 B scales/biases
 // The GEMV phases stage their activations past the head of the shared union,
 // which holds the attention tile mbarriers (attn::DecSmem::tbar, written by
@@ -56,7 +66,7 @@ constexpr int GR_BYTES = 576;  // one granule: 512 B nibbles + 64 B scales/biase
 // barrier that an arrival could still update.
 constexpr size_t MK_UNI_RESERVED = 128;
 constexpr int XW = 36;         // words per (group, column) block of staged activations (32 + 4 pad)
-constexpr int SEEDF = 8;       // floats per (group, quad t) seed entry
+constexpr int SEEDF = 2;       // floats per (group, quad t) entry: sum(x) of columns 2t, 2t+1
 constexpr unsigned long long MK_TIMEOUT_NS = 2000000000ull;
 
 enum { K_QKV = 0, K_O = 1, K_GU = 2, K_DOWN = 3 };
@@ -100,10 +110,7 @@ struct MkArgs {
     int* out;
     const int* gate;
     unsigned* sync;  // [0] phase arrivals, [1] final arrivals, [2] abort flag
-    float* part_g;   // [gridDim.x][2][256] partial sums of split tiles
-    unsigned* tile_ctr;  // [max tiles] arrivals per split tile (reset by the finisher)
     int* err;
-    int depth;       // ring slots per warp (the kernel's DEPTH)
     bf16* trace;     // diagnostics: residual stream after the embedding and every layer, [L + 1][M][H]
     bf16* trace_mid;   // diagnostics: residual after each attention block, [L][M][H]
     bf16* trace_attn;  // diagnostics: attention output of each layer, [L][M][QD]
@@ -112,6 +119,7 @@ struct MkArgs {
 
 struct MkMisc {
     int wft[MK_NW];  // first tile (CTA-local) of each warp's range in the current phase
+    int2 wr[MK_NW];  // each warp's range of tile-groups in the current phase, CTA-relative
     float rnorm[8];
     float ssq[MK_NW][8];
     unsigned long long amax[8];
@@ -164,8 +172,6 @@ QW_DEV MkLin phase_lin(const MkArgs& a, int pi) {
 // A tile whose tile-groups are split between CTAs is finished by the last of
 // them to arrive, which sums the CTAs' partial sums in CTA order.
 QW_DEV int range_lo(int c, int N, int C) { return (int)(((long long)c * N) / C); }
-// CTA owning tile-group x
-QW_DEV int cta_of(int x, int N, int C) { return (int)(((long long)(x + 1) * C - 1) / N); }
 
 // Per-CTA description of one GEMV phase, built once per launch in shared
 // memory so that walking the granule stream needs no global loads.
@@ -180,65 +186,120 @@ static_assert(sizeof(PhaseInfo) == 32, "PhaseInfo layout");
 
 QW_DEV void warp_range(const PhaseInfo& P, int warp, int& wa, int& wb) {
     const int n = P.tg1 - P.tg0;
-    wa = P.tg0 + ((warp * n) >> 4);
-    wb = P.tg0 + (((warp + 1) * n) >> 4);
+    wa = P.tg0 + (warp * n) / MK_NW;
+    wb = P.tg0 + ((warp + 1) * n) / MK_NW;
 }
 
-// Walks a warp's granule sequence: for each phase in order, the warp's
-// contiguous range of granules [wa*R16, wb*R16).
-struct Cursor {
-    const PhaseInfo* tab;
-    int np, pi;
-    const unsigned char* p;    // next granule
-    const unsigned char* end;  // end of the warp's range in phase pi
+QW_DEV void mbar_arrive_cta(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Bounded mbarrier wait (4 s of globaltimer, or the launch's abort flag).
+QW_DEV bool mbar_wait_mk(uint64_t* bar, uint32_t parity, const unsigned* abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer();
+    for (unsigned it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63u) == 0) {
+            if (*reinterpret_cast<const volatile unsigned*>(abort_flag)) return false;
+            if (globaltimer() - t0 > 2 * MK_TIMEOUT_NS) return false;
+        }
+    }
+}
 
-    QW_DEV void enter(int warp) {
-        while (pi < np) {
-            const PhaseInfo& P = tab[pi];
+QW_DEV bool mbar_test(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Producer lane w (of 16): copies compute warp w's granules, phase after phase,
+// into its ring (R granules per stage, a stage never spans two phases).  Stage
+// s goes to slot s % MK_NSLOT once the compute warp has released the slot's
+// previous stage.  The lanes poll their release barriers without blocking and
+// the warp never waits on one lane's barrier while another lane could copy;
+// after a round without progress it sleeps briefly, leaving issue slots to the
+// compute warps.  Before returning it waits until every copy it issued has
+// landed, so the CTA never exits with a copy in flight.
+template <int R>
+QW_DEV void producer_loop(const MkArgs& a, const PhaseInfo* tab, int np, int lane, unsigned char* ring,
+                          uint64_t* fullb, uint64_t* emptyb) {
+    const int w = lane < MK_NW ? lane : 0;
+    unsigned char* wring = ring + (size_t)w * MK_NSLOT * R * GR_BYTES;
+    uint64_t* fb = fullb + w * MK_NSLOT;
+    uint64_t* eb = emptyb + w * MK_NSLOT;
+    unsigned stage = 0;
+    int pi = 0, gi = 0, ge = 0;
+    // next non-empty range of this lane's warp, from phase pi on
+    auto enter = [&]() {
+        for (; pi < np; ++pi) {
             int wa, wb;
-            warp_range(P, warp, wa, wb);
-            p = P.w + (size_t)wa * P.R16 * GR_BYTES;
-            end = P.w + (size_t)wb * P.R16 * GR_BYTES;
-            if (p < end) return;
-            ++pi;
+            warp_range(tab[pi], w, wa, wb);
+            gi = wa * tab[pi].R16;
+            ge = wb * tab[pi].R16;
+            if (gi < ge) return;
+        }
+    };
+    if (lane < MK_NW) enter();
+    bool active = lane < MK_NW && pi < np;
+    bool failed = false;
+    unsigned long long t_last = globaltimer();
+    unsigned idle = 0;
+    while (__any_sync(0xffffffffu, active)) {
+        bool progress = false;
+        if (active) {
+            const unsigned slot = stage % MK_NSLOT;
+            if (stage < MK_NSLOT || mbar_test(&eb[slot], ((stage / MK_NSLOT) - 1) & 1)) {
+                const int n = min(R, ge - gi);
+                mbar_arrive_expect_tx(&fb[slot], (uint32_t)(n * GR_BYTES));
+                bulk_g2s(wring + (size_t)slot * R * GR_BYTES, tab[pi].w + (size_t)gi * GR_BYTES,
+                         (uint32_t)(n * GR_BYTES), &fb[slot]);
+                gi += n;
+                ++stage;
+                if (gi >= ge) {
+                    ++pi;
+                    enter();
+                    active = pi < np;
+                }
+                progress = true;
+            }
+        }
+        if (__any_sync(0xffffffffu, progress)) {
+            idle = 0;
+        } else if ((++idle & 1023u) == 0) {
+            // rarely: the abort flag (a global read) and the time bound
+            const unsigned long long now = globaltimer();
+            if (idle == 1024u) t_last = now;
+            if (*reinterpret_cast<const volatile unsigned*>(a.sync + 2) || now - t_last > 2 * MK_TIMEOUT_NS) {
+                failed = !*reinterpret_cast<const volatile unsigned*>(a.sync + 2);
+                break;
+            }
+        } else {
+            __nanosleep(20);
         }
     }
-    QW_DEV void init(const PhaseInfo* t, int n, int warp) {
-        tab = t;
-        np = n;
-        pi = 0;
-        enter(warp);
+    if (failed && lane == 0) {
+        atomicOr(a.err, QW_DERR_TIMEOUT);
+        atomicExch(a.sync + 2, 1u);
     }
-    QW_DEV bool done() const { return pi >= np; }
-    QW_DEV void advance(int warp) {
-        p += GR_BYTES;
-        if (p >= end) {
-            ++pi;
-            enter(warp);
+    if (lane < MK_NW) {
+        for (unsigned s2 = stage > MK_NSLOT ? stage - MK_NSLOT : 0; s2 < stage; ++s2) {
+            // landed, or consumed (the slot's phase has moved on): returns at once
+            const unsigned long long t0 = globaltimer();
+            while (!mbar_test(&fb[s2 % MK_NSLOT], (s2 / MK_NSLOT) & 1))
+                if (globaltimer() - t0 > 2 * MK_TIMEOUT_NS) break;
         }
     }
-};
-
-// Issue the copies of the producer cursor's next two granules into the slot
-// pair at `dst` (one commit group per pair; fewer granules, or an empty group,
-// once the stream has ended).  Every lane walks the cursor in lockstep.
-QW_DEV void issue_pair(Cursor& pc, int warp, int lane, unsigned char* dst) {
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-        if (!pc.done()) {
-            cp_async16(dst + u * GR_BYTES + 16 * lane, pc.p + 16 * lane);
-            if (lane < 4) cp_async16(dst + u * GR_BYTES + 512 + 16 * lane, pc.p + 512 + 16 * lane);
-            pc.advance(warp);
-        }
-    }
-    cp_async_commit();
 }
 
 // ---- activation staging ----------------------------------------------------
 // x' for one GEMV phase: per (group gl, column m) a block of XW words, words
-// t*8 + 2j + h = fp16 pair (x[64gl+16j+2t+8h], x[..+1]); per (gl, quad t)
-// SEEDF floats {-1024*lo(2t), -1024*lo(2t+1), -1024*hi(2t), -1024*hi(2t+1),
-// sum(2t), sum(2t+1)}, lo/hi = sums over k-steps {0,2} / {1,3}.
+// t*8 + 2j + h = fp16 pair (x[64gl+16j+2t+8h], x[..+1]), divided by 16 for the
+// odd k-steps j (their nibbles enter the tensor core as 16q); per (gl, quad t)
+// SEEDF floats {sum(x) of column 2t, of column 2t+1} for the bias term.
 // Source: rows [row0, row0+Mx) of a bf16 matrix (ld) or of the embedding.
 struct StageSrc {
     const bf16* x;     // null -> embedding rows of ids[row0 + m]
@@ -279,11 +340,11 @@ QW_DEV void load16(const MkArgs& a, const StageSrc& s, int m, int k, float (&v)[
 QW_DEV float stage_unit(const float (&v)[16], int gl, int m, int j, int Mx, uint32_t* xs) {
     float sum = 0.f;
     uint32_t h[8];
+    const float f = (j & 1) ? 0.0625f : 1.0f;  // exact power-of-two scaling
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const __half2 hh = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-        const float2 back = __half22float2(hh);
-        sum += back.x + back.y;
+        sum += v[2 * i] + v[2 * i + 1];
+        const __half2 hh = __floats2half2_rn(v[2 * i] * f, v[2 * i + 1] * f);
         h[i] = *reinterpret_cast<const uint32_t*>(&hh);
     }
     uint32_t* blk = xs + (size_t)(gl * Mx + m) * XW;
@@ -295,16 +356,12 @@ QW_DEV float stage_unit(const float (&v)[16], int gl, int m, int j, int Mx, uint
     return sum;
 }
 
-// j-quads share (gl, m): lo = steps 0+2, hi = steps 1+3 (every lane of the warp
-// takes part in the shuffles).
+// The four k-step units of (gl, m) sit in one lane quad: their sum is sum(x)
+// of the group and column (every lane of the warp takes part in the shuffles).
 QW_DEV void stage_seeds(float sum, bool valid, int gl, int m, int j, float* seeds) {
     const float pair = sum + __shfl_xor_sync(0xffffffffu, sum, 2);
     const float tot = pair + __shfl_xor_sync(0xffffffffu, pair, 1);
-    if (valid && j < 2) {
-        float* e = seeds + (size_t)(gl * 4 + (m >> 1)) * SEEDF;
-        e[2 * j + (m & 1)] = -1024.f * pair;  // j = 0: lo, j = 1: hi
-        if (j == 0) e[4 + (m & 1)] = tot;
-    }
+    if (valid && j == 0) seeds[(size_t)(gl * 4 + (m >> 1)) * SEEDF + (m & 1)] = tot;
 }
 
 QW_DEV void apply_norm(const StageSrc& s, float r, int k, float (&v)[16]) {
@@ -359,6 +416,9 @@ QW_DEV void unpack16(const uint32_t (&X)[8], float (&v)[16]) {
     }
 }
 
+// Barrier of the compute warps only (named barrier 1; the producer warp never joins).
+QW_DEV void csync() { asm volatile("bar.sync 1, %0;" ::"n"(MK_NT) : "memory"); }
+
 QW_DEV void stage_acts(const MkArgs& a, const StageSrc& s, int K, int Mx, uint32_t* xs, float* seeds, float* sq,
                        MkMisc& mm) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -380,7 +440,7 @@ QW_DEV void stage_acts(const MkArgs& a, const StageSrc& s, int K, int Mx, uint32
             load16_packed(a, s, m1, gl1 * 64 + 16 * j1, X1);
             sq[u1] = sumsq_packed(X1);
         }
-        __syncthreads();
+        csync();
         if (warp < Mx) {
             // row `warp`: its KG*4 units, lane-strided, then a fixed shuffle tree
             float q = 0.f;
@@ -388,7 +448,7 @@ QW_DEV void stage_acts(const MkArgs& a, const StageSrc& s, int K, int Mx, uint32
             q = warp_sum(q);
             if (lane == 0) mm.rnorm[warp] = 1.0f / sqrtf(q / (float)K + a.eps);
         }
-        __syncthreads();
+        csync();
         float sum0 = 0.f, sum1 = 0.f;
         if (u0 < units) {
             float v[16];
@@ -431,13 +491,13 @@ QW_DEV void stage_acts(const MkArgs& a, const StageSrc& s, int K, int Mx, uint32
                 if (lane == 0) mm.ssq[warp][m] = w;
             }
         }
-        __syncthreads();
+        csync();
         if (tid < Mx) {
             float tot = 0.f;
             for (int w = 0; w < MK_NW; ++w) tot += mm.ssq[w][tid];
             mm.rnorm[tid] = 1.0f / sqrtf(tot / (float)K + a.eps);
         }
-        __syncthreads();
+        csync();
     }
     for (int ub = 0; ub < units; ub += MK_NT) {
         const int u = ub + tid;
@@ -475,13 +535,13 @@ QW_DEV bool cta_wait(const MkArgs& a, unsigned target, MkMisc& mm) {
             }
         }
     }
-    __syncthreads();  // the acquire above, then this barrier, orders every thread's reads
+    csync();  // the acquire above, then this barrier, orders every thread's reads
     return !*reinterpret_cast<volatile int*>(&mm.bad);
 }
 // Block barrier, then one release-add: publishes every thread's earlier writes
 // (the barrier orders them before the release, which is cumulative).
 QW_DEV void cta_arrive(const MkArgs& a) {
-    __syncthreads();
+    csync();
     if (threadIdx.x == 0) red_release_add(a.sync, 1u);
 }
 
@@ -495,51 +555,41 @@ QW_DEV void trace_copy_n(const bf16* src_, bf16* dst_, int n) {
 QW_DEV void trace_copy(const MkArgs& a, int l) { trace_copy_n(a.x, a.trace + (size_t)l * a.M * a.H, a.M * a.H); }
 
 // Attention items run on the whole CTA (taken by whole CTAs only).
-struct BlockSync {
-    QW_DEV void operator()() const { __syncthreads(); }
+struct CSync {
+    QW_DEV void operator()() const { csync(); }
 };
 
 // Staged activations of one group for this lane: B fragments of the four
-// k-steps and the per-column seed terms.
+// k-steps (odd steps as x/16) and sum(x) of columns 2t, 2t+1.
 struct GAct {
-    uint4 xa, xb;   // (step 0, step 1) and (step 2, step 3) B fragment pairs
-    float z0, z1;   // -(1024 lo + 64 hi) for columns 2t, 2t+1
-    float sx0, sx1; // sum(x) for columns 2t, 2t+1
+    uint4 xa, xb;  // (step 0, step 1) and (step 2, step 3) B fragment pairs
+    float2 sx;
 };
 QW_DEV GAct load_act(const uint32_t* xs_lane, const float* seeds_lane, int gl, int col_stride) {
     GAct r;
     const uint32_t* xp = xs_lane + (size_t)gl * col_stride;
     r.xa = *reinterpret_cast<const uint4*>(xp);
     r.xb = *reinterpret_cast<const uint4*>(xp + 4);
-    const float* sp = seeds_lane + (size_t)gl * 4 * SEEDF;
-    const float4 sd = *reinterpret_cast<const float4*>(sp);
-    const float2 sx = *reinterpret_cast<const float2*>(sp + 4);
-    r.z0 = fmaf(sd.z, 0.0625f, sd.x);
-    r.z1 = fmaf(sd.w, 0.0625f, sd.y);
-    r.sx0 = sx.x;
-    r.sx1 = sx.y;
+    r.sx = *reinterpret_cast<const float2*>(seeds_lane + (size_t)gl * 4 * SEEDF);
     return r;
 }
-// One granule: four mma over the group's k-steps (two chains: 1024+q and
-// 1024+16q), then acc += s * sum(q x) + b * sum(x) per row and column.
-QW_DEV void granule_mma(const unsigned char* gp, int lane, const GAct& x, float (&acc)[4]) {
-    const int g = lane >> 2;
-    const uint4 wv = *reinterpret_cast<const uint4*>(gp + 16 * lane);
-    const uint2 sb = *reinterpret_cast<const uint2*>(gp + 512 + 8 * g);
+// One granule's four mma over the group's k-steps, one chain: c = 2^-24 * sum(q x)
+// per row (g, g+8) and column (2t, 2t+1).
+QW_DEV void granule_mma(const uint4 wv, const GAct& x, float (&c)[4]) {
     const uint32_t a8 = wv.x >> 8, b8 = wv.y >> 8, c8 = wv.z >> 8, d8 = wv.w >> 8;
-    float cl[4], ch[4];
-    mma_zero(cl, lo4(wv.x), lo4(a8), lo4(wv.y), lo4(b8), x.xa.x, x.xa.y);
-    mma_zero(ch, hi4(wv.x), hi4(a8), hi4(wv.y), hi4(b8), x.xa.z, x.xa.w);
-    mma_acc(cl, lo4(wv.z), lo4(c8), lo4(wv.w), lo4(d8), x.xb.x, x.xb.y);
-    mma_acc(ch, hi4(wv.z), hi4(c8), hi4(wv.w), hi4(d8), x.xb.z, x.xb.w);
-    // the chains hold q*x * 2^-24 (k-steps 0, 2) and 16q*x * 2^-24 (k-steps 1, 3)
-    const float s0 = bits_lo_f(sb.x) * QW_NIB_SCALE, b0 = bits_hi_f(sb.x);
-    const float s1 = bits_lo_f(sb.y) * QW_NIB_SCALE, b1 = bits_hi_f(sb.y);
-    const float s016 = s0 * 0.0625f, s116 = s1 * 0.0625f;
-    acc[0] = fmaf(s0, cl[0], fmaf(s016, ch[0], fmaf(b0, x.sx0, acc[0])));
-    acc[1] = fmaf(s0, cl[1], fmaf(s016, ch[1], fmaf(b0, x.sx1, acc[1])));
-    acc[2] = fmaf(s1, cl[2], fmaf(s116, ch[2], fmaf(b1, x.sx0, acc[2])));
-    acc[3] = fmaf(s1, cl[3], fmaf(s116, ch[3], fmaf(b1, x.sx1, acc[3])));
+    mma_zero(c, lo4(wv.x), lo4(a8), lo4(wv.y), lo4(b8), x.xa.x, x.xa.y);
+    mma_acc(c, hi4(wv.x), hi4(a8), hi4(wv.y), hi4(b8), x.xa.z, x.xa.w);
+    mma_acc(c, lo4(wv.z), lo4(c8), lo4(wv.w), lo4(d8), x.xb.x, x.xb.y);
+    mma_acc(c, hi4(wv.z), hi4(c8), hi4(wv.w), hi4(d8), x.xb.z, x.xb.w);
+}
+// acc += (2^24 s) * c + b * sum(x) for rows g (s0, b0) and g + 8 (s1, b1).
+QW_DEV void granule_epi(const uint2 sb, const float (&c)[4], const float2 sx, float (&acc)[4]) {
+    const float s0 = bits_lo_f(sb.x), b0 = bits_hi_f(sb.x);
+    const float s1 = bits_lo_f(sb.y), b1 = bits_hi_f(sb.y);
+    acc[0] = fmaf(s0, c[0], fmaf(b0, sx.x, acc[0]));
+    acc[1] = fmaf(s0, c[1], fmaf(b0, sx.y, acc[1]));
+    acc[2] = fmaf(s1, c[2], fmaf(b1, sx.x, acc[2]));
+    acc[3] = fmaf(s1, c[3], fmaf(b1, sx.y, acc[3]));
 }
 
 // ---- one GEMV phase --------------------------------------------------------
@@ -547,7 +597,8 @@ QW_DEV void granule_mma(const unsigned char* gp, int lane, const GAct& x, float 
 // Epilogue of one output element (tile row `row`, column m) with the final
 // fp32 sums v[sub].
 template <int KIND>
-QW_DEV void store_elem(const MkArgs& a, bool lm, int row, int m, const float (&v)[2], unsigned long long (&best)[8]) {
+QW_DEV void store_elem(const MkArgs& a, bool lm, int row, int m, const float (&v)[2], unsigned long long (&best)[8],
+                       float resid) {
     if (KIND == K_GU && !lm) {
         const float gv = bfr(v[0]), uv = bfr(v[1]);
         const float sg = bfr(1.0f / (1.0f + expf(-gv)));
@@ -568,21 +619,44 @@ QW_DEV void store_elem(const MkArgs& a, bool lm, int row, int m, const float (&v
         else
             a.v[(size_t)m * a.KD + row - a.QD - a.KD] = f2bf(v[0]);
     } else {
-        bf16* y = a.x + (size_t)m * a.H + row;
-        *y = f2bf(__fadd_rn(bf2f(__ldcg(y)), bfr(v[0])));
+        a.x[(size_t)m * a.H + row] = f2bf(__fadd_rn(resid, bfr(v[0])));
     }
 }
 
+// ---- optional timing stamps (builds with -DQW_MK_PROFILE only) --------------
+// Thread 0 of each CTA records globaltimer at points of every phase:
+// g_mk_prof[cta][phase][k], k = 0 after the phase barrier, 1 after activation
+// staging, 2 first weight stage ready, 3 own weight loop done, 4 all warps'
+// loops done, 5 epilogue done, 6 before arriving.  Read with qw_debug_mk_prof.
+#ifdef QW_MK_PROFILE
+constexpr int MK_PROF_PHASES = 4 * 64 * 2 + 2;
+__device__ unsigned long long g_mk_prof[160][MK_PROF_PHASES][8];
+#define MK_STAMP(ph, k) \
+    do { \
+        if (threadIdx.x == 0 && (ph) < MK_PROF_PHASES) g_mk_prof[blockIdx.x][(ph)][(k)] = globaltimer(); \
+    } while (0)
+#else
+#define MK_STAMP(ph, k) \
+    do { \
+    } while (0)
+#endif
+
+template <int KIND>
+__device__ __noinline__ void gemv_epilogue(const MkArgs& a, const PhaseInfo& P, int Mx, const float* red, bool lm,
+                                           MkMisc& mm);
+
 // One GEMV phase: each warp computes its granule range from its ring, writing
 // one partial per tile segment to shared memory (red: [warp][segment][sub][128]);
-// then the CTA reduces the segments of each tile in warp order and either
-// stores the outputs (tiles it owns completely) or hands its partial to the
-// CTA that finishes a split tile.
-template <int KIND, int DEPTH>
-QW_DEV void gemv_phase(const MkArgs& a, const PhaseInfo& P, int Mx, uint32_t* xs, float* seeds, float* red,
-                       Cursor& pc, unsigned& gpos, unsigned char* ring, bool lm, MkMisc& mm) {
+// then the CTA reduces the segments of each tile in warp order and stores the
+// outputs.  Granules enter their sub-tile's accumulator in phase order (the
+// granules' own mma chains are independent, so this costs no latency): the
+// summation order depends only on the warp's range, never on the stage size R.
+template <int KIND, int R>
+__device__ __noinline__ void gemv_phase(const MkArgs& a, const PhaseInfo& P, int Mx, uint32_t* xs, float* seeds, float* red,
+                       unsigned& stage, unsigned char* ring, uint64_t* fullb, uint64_t* emptyb, bool lm, MkMisc& mm,
+                       int prof_id) {
+    (void)prof_id;
     constexpr int R16 = KIND == K_GU ? 2 : 1;
-    constexpr int NS = DEPTH / 2;  // slot pairs per warp, one commit group each
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int KG = P.KG;
@@ -591,106 +665,108 @@ QW_DEV void gemv_phase(const MkArgs& a, const PhaseInfo& P, int Mx, uint32_t* xs
     const int col_stride = Mx * XW;
     const uint32_t* xs_lane = xs + (size_t)mcol * XW + t * 8;
     const float* seeds_lane = seeds + (size_t)t * SEEDF;
-    unsigned char* wring = ring + (size_t)warp * DEPTH * GR_BYTES;
-    auto gptr = [&](int u) { return wring + (size_t)((gpos + u) & (DEPTH - 1)) * GR_BYTES; };
-    // refill the slot pair of chunk c (granules 2c, 2c+1) with the chunk NS ahead
-    auto refill = [&](unsigned c) { issue_pair(pc, warp, lane, wring + (size_t)(c % NS) * 2 * GR_BYTES); };
+    const unsigned char* wring = ring + (size_t)warp * MK_NSLOT * R * GR_BYTES;
+    uint64_t* fb = fullb + warp * MK_NSLOT;
+    uint64_t* eb = emptyb + warp * MK_NSLOT;
 
     int wa, wb;
     warp_range(P, warp, wa, wb);
-    if (lane == 0) mm.wft[warp] = (wa - P.tg0) / KG;
-    int seg = 0;
-    for (int tg = wa; tg < wb; ++seg) {
-        // one tile segment: tile-groups [tg, se) of tile `tile`
-        const int tile = tg / KG;
-        const int se = min(wb, (tile + 1) * KG);
-        const int gl0 = tg - tile * KG;
-        const int ng = (se - tg) * R16;
-        float acc[4][4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) acc[u][0] = acc[u][1] = acc[u][2] = acc[u][3] = 0.f;
-        int gi = 0;
-        // four granules per step: independent mma chains in flight
-        for (; gi + 4 <= ng; gi += 4) {
-            // groups newer than the last pair these four granules touch may stay pending
-            if ((gpos & 1) == 0)
-                cp_async_wait<NS - 2>();
-            else
-                cp_async_wait<NS - 3>();
-            __syncwarp();
-            if (R16 == 1) {
-                const int gl = gl0 + gi;
-                const GAct x0 = load_act(xs_lane, seeds_lane, gl, col_stride);
-                const GAct x1 = load_act(xs_lane, seeds_lane, gl + 1, col_stride);
-                const GAct x2 = load_act(xs_lane, seeds_lane, gl + 2, col_stride);
-                const GAct x3 = load_act(xs_lane, seeds_lane, gl + 3, col_stride);
-                granule_mma(gptr(0), lane, x0, acc[0]);
-                granule_mma(gptr(1), lane, x1, acc[1]);
-                granule_mma(gptr(2), lane, x2, acc[2]);
-                granule_mma(gptr(3), lane, x3, acc[3]);
-            } else {
-                const int gl = gl0 + gi / 2;
-                const GAct x0 = load_act(xs_lane, seeds_lane, gl, col_stride);
-                const GAct x1 = load_act(xs_lane, seeds_lane, gl + 1, col_stride);
-                granule_mma(gptr(0), lane, x0, acc[0]);
-                granule_mma(gptr(1), lane, x0, acc[1]);
-                granule_mma(gptr(2), lane, x1, acc[2]);
-                granule_mma(gptr(3), lane, x1, acc[3]);
-            }
-            __syncwarp();
-            // refill the two pairs whose second granule was just consumed
-            if ((gpos & 1) == 0) {
-                refill(gpos / 2);
-                refill(gpos / 2 + 1);
-            } else {
-                refill((gpos - 1) / 2);
-                refill((gpos + 1) / 2);
-            }
-            gpos += 4;
-        }
-        for (; gi < ng; ++gi) {
-            if ((gpos & 1) == 0) cp_async_wait<NS - 1>();
-            __syncwarp();
-            const GAct x0 = load_act(xs_lane, seeds_lane, gl0 + gi / R16, col_stride);
-            if ((gi & 3) == 0) granule_mma(gptr(0), lane, x0, acc[0]);
-            else if ((gi & 3) == 1) granule_mma(gptr(0), lane, x0, acc[1]);
-            else if ((gi & 3) == 2) granule_mma(gptr(0), lane, x0, acc[2]);
-            else granule_mma(gptr(0), lane, x0, acc[3]);
-            __syncwarp();
-            if (gpos & 1) refill((gpos - 1) / 2);
-            gpos += 1;
-        }
-        // partial accumulators combined in a fixed order (sub-tile = granule parity)
-        float* r0 = red + ((size_t)(warp * seg_stride + seg) * R16 * 32 + lane) * 4;
-        if (R16 == 1) {
-            *reinterpret_cast<float4*>(r0) = make_float4((acc[0][0] + acc[1][0]) + (acc[2][0] + acc[3][0]),
-                                                         (acc[0][1] + acc[1][1]) + (acc[2][1] + acc[3][1]),
-                                                         (acc[0][2] + acc[1][2]) + (acc[2][2] + acc[3][2]),
-                                                         (acc[0][3] + acc[1][3]) + (acc[2][3] + acc[3][3]));
-        } else {
-            *reinterpret_cast<float4*>(r0) =
-                make_float4(acc[0][0] + acc[2][0], acc[0][1] + acc[2][1], acc[0][2] + acc[2][2], acc[0][3] + acc[2][3]);
-            *reinterpret_cast<float4*>(r0 + 128) =
-                make_float4(acc[1][0] + acc[3][0], acc[1][1] + acc[3][1], acc[1][2] + acc[3][2], acc[1][3] + acc[3][3]);
-        }
-        tg = se;
+    if (lane == 0) {
+        mm.wft[warp] = (wa - P.tg0) / KG;
+        mm.wr[warp] = make_int2(wa - P.tg0, wb - P.tg0);
     }
-    __syncthreads();
+    const int per_tile = KG * R16;  // granules of one tile
+    int gi = wa * R16;              // phase-local index of the warp's next granule
+    const int gend = wb * R16;
+    int seg = 0;
+    int seg_end = (gi / per_tile + 1) * per_tile;
+    float acc[R16][4];
+#pragma unroll
+    for (int u = 0; u < R16; ++u) acc[u][0] = acc[u][1] = acc[u][2] = acc[u][3] = 0.f;
+    auto flush = [&]() {
+        float* r0 = red + ((size_t)(warp * seg_stride + seg) * R16 * 32 + lane) * 4;
+#pragma unroll
+        for (int u = 0; u < R16; ++u) {
+            *reinterpret_cast<float4*>(r0 + u * 128) = make_float4(acc[u][0], acc[u][1], acc[u][2], acc[u][3]);
+            acc[u][0] = acc[u][1] = acc[u][2] = acc[u][3] = 0.f;
+        }
+        ++seg;
+    };
+    while (gi < gend) {
+        const int n = min(R, gend - gi);
+        const unsigned slot = stage % MK_NSLOT;
+        if (!mbar_wait_mk(&fb[slot], (stage / MK_NSLOT) & 1, a.sync + 2)) {
+            if (lane == 0) {
+                atomicOr(a.err, QW_DERR_TIMEOUT);
+                atomicExch(a.sync + 2, 1u);
+            }
+            break;
+        }
+        if (gi == wa * R16) MK_STAMP(prof_id, 2);
+        const unsigned char* sp = wring + (size_t)slot * R * GR_BYTES;
+        // a stage starts at an even granule when R16 == 2 (ranges and stages are whole pairs)
+        int gl = (gi / R16) % KG;
+        GAct x = load_act(xs_lane, seeds_lane, gl, col_stride);
+        // four granules at a time (their weights in registers), the batches not unrolled
+#pragma unroll 1
+        for (int j0 = 0; j0 < n; j0 += 4) {
+            uint4 wv[4];
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj)
+                if (j0 + jj < n) wv[jj] = *reinterpret_cast<const uint4*>(sp + (j0 + jj) * GR_BYTES + 16 * lane);
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const int j = j0 + jj;
+                if (j < n) {
+                    if (gi + j == seg_end) {
+                        flush();
+                        seg_end += per_tile;
+                    }
+                    if (j > 0 && (R16 == 1 || (jj & 1) == 0)) {
+                        if (++gl == KG) gl = 0;
+                        x = load_act(xs_lane, seeds_lane, gl, col_stride);
+                    }
+                    float c[4];
+                    granule_mma(wv[jj], x, c);
+                    const uint2 sb = *reinterpret_cast<const uint2*>(sp + j * GR_BYTES + 512 + 8 * g);
+                    granule_epi(sb, c, x.sx, acc[R16 == 2 ? (jj & 1) : 0]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cta(&eb[slot]);
+        gi += n;
+        ++stage;
+    }
+    MK_STAMP(prof_id, 3);
+    flush();
+    csync();
+    MK_STAMP(prof_id, 4);
+    gemv_epilogue<KIND>(a, P, Mx, red, lm, mm);
+    MK_STAMP(prof_id, 5);
+}
 
+// The CTA's outputs of one GEMV phase from the warps' tile-segment partials.
+template <int KIND>
+__device__ __noinline__ void gemv_epilogue(const MkArgs& a, const PhaseInfo& P, int Mx, const float* red, bool lm,
+                                           MkMisc& mm) {
+    constexpr int R16 = KIND == K_GU ? 2 : 1;
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int KG = P.KG;
+    const int seg_stride = P.seg_stride;
     // ---- epilogue -------------------------------------------------------------
-    const int C = gridDim.x, c = blockIdx.x;
     const int tfirst = P.tg0 / KG, tlast = (P.tg1 - 1) / KG;
     const int ntl = P.tg1 > P.tg0 ? tlast - tfirst + 1 : 0;
     // CTA partial of tile (tfirst + tl), element (sub, lane slot ln, e): warps in order
-    const int tg0 = P.tg0, nrange = P.tg1 - P.tg0;
+    const int tg0 = P.tg0;
     auto cta_part = [&](int tl, int sub, int ln, int e) {
         const int lo = (tfirst + tl) * KG - tg0, hi = lo + KG;  // tile's tile-groups, CTA-relative
         float v = 0.f;
 #pragma unroll
         for (int w = 0; w < MK_NW; ++w) {
-            const int xa = (w * nrange) >> 4, xb = ((w + 1) * nrange) >> 4;
-            if (xa < xb && xa < hi && xb > lo) {
-                const int sg = (tfirst + tl) - (tfirst + mm.wft[w]);
+            const int2 xr = mm.wr[w];
+            if (xr.x < xr.y && xr.x < hi && xr.y > lo) {
+                const int sg = tl - mm.wft[w];
                 v += red[((size_t)(w * seg_stride + sg) * R16 + sub) * 32 * 4 + ln * 4 + e];
             }
         }
@@ -701,54 +777,19 @@ QW_DEV void gemv_phase(const MkArgs& a, const PhaseInfo& P, int Mx, uint32_t* xs
     for (int j = 0; j < 8; ++j) best[j] = 0ull;
     if (lm) {
         if (tid < 8) mm.amax[tid] = 0ull;
-        __syncthreads();
+        csync();
     }
-    // 1. tiles owned completely: outputs now
+    // every tile of the phase is owned by one CTA: outputs (thread per element;
+    // the residual read is issued before the reduction so its latency overlaps it)
     const int nout = ntl * 16 * Mx;
     for (int o = tid; o < nout; o += MK_NT) {
         const int m = o % Mx, rr = o / Mx, r = rr & 15, tl = rr >> 4;
-        const int tile = tfirst + tl;
-        if (tile * KG < P.tg0 || (tile + 1) * KG > P.tg1) continue;  // split tile
+        const int row = (tfirst + tl) * 16 + r;
         const int ln = 4 * (r & 7) + (m >> 1), e = 2 * (r >> 3) + (m & 1);
+        float resid = 0.f;
+        if ((KIND == K_O || KIND == K_DOWN) && !lm) resid = bf2f(__ldcg(a.x + (size_t)m * a.H + row));
         float v[2] = {cta_part(tl, 0, ln, e), R16 == 2 ? cta_part(tl, 1, ln, e) : 0.f};
-        store_elem<KIND>(a, lm, tile * 16 + r, m, v, best);
-    }
-    // 2. split tiles (at most the first and the last): publish this CTA's
-    //    partial; the last CTA to arrive sums them in CTA order
-    for (int side = 0; side < 2; ++side) {
-        const int tl = side == 0 ? 0 : ntl - 1;
-        if (ntl == 0 || (side == 1 && ntl == 1)) break;
-        const int tile = tfirst + tl;
-        if (tile * KG >= P.tg0 && (tile + 1) * KG <= P.tg1) continue;  // owned completely
-        float* slotp = a.part_g + ((size_t)c * 2 + side) * 256;
-        for (int i = tid; i < R16 * 128; i += MK_NT) {
-            const int sub = i >> 7, ln = (i >> 2) & 31, e = i & 3;
-            slotp[i] = cta_part(tl, sub, ln, e);
-        }
-        __syncthreads();
-        // CTAs with a non-empty share of this tile (empty ranges exist when N < C)
-        const int cf = cta_of(tile * KG, P.N, C), cl = cta_of((tile + 1) * KG - 1, P.N, C);
-        int ncov = 0;
-        for (int cc = cf; cc <= cl; ++cc) ncov += range_lo(cc, P.N, C) < range_lo(cc + 1, P.N, C);
-        if (tid == 0) mm.last = atom_add_acq_rel(&a.tile_ctr[tile], 1u) == (unsigned)(ncov - 1);
-        __syncthreads();
-        if (mm.last) {
-            for (int o = tid; o < 16 * Mx; o += MK_NT) {
-                const int m = o % Mx, r = o / Mx;
-                const int ln = 4 * (r & 7) + (m >> 1), e = 2 * (r >> 3) + (m & 1);
-                float v[2] = {0.f, 0.f};
-                for (int cc = cf; cc <= cl; ++cc) {
-                    if (range_lo(cc, P.N, C) >= range_lo(cc + 1, P.N, C)) continue;
-                    const int sd = (tile == range_lo(cc, P.N, C) / KG) ? 0 : 1;
-                    const float* sp = a.part_g + ((size_t)cc * 2 + sd) * 256;
-                    v[0] += __ldcg(sp + ln * 4 + e);
-                    if (R16 == 2) v[1] += __ldcg(sp + 128 + ln * 4 + e);
-                }
-                store_elem<KIND>(a, lm, tile * 16 + r, m, v, best);
-            }
-            if (tid == 0) a.tile_ctr[tile] = 0u;
-        }
-        __syncthreads();
+        store_elem<KIND>(a, lm, row, m, v, best, resid);
     }
     if (lm) {
 #pragma unroll
@@ -760,18 +801,20 @@ QW_DEV void gemv_phase(const MkArgs& a, const PhaseInfo& P, int Mx, uint32_t* xs
                 if (lane == 0 && b) atomicMax(&mm.amax[m], b);
             }
         }
-        __syncthreads();
+        csync();
         if (tid < Mx) a.amax_cta[(size_t)blockIdx.x * 8 + tid] = mm.amax[tid];
     }
 }
 
 // ---- the kernel ------------------------------------------------------------
-template <int RMAX, int DEPTH>
-__global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
+template <int RMAX, int R>
+__global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const __grid_constant__ MkArgs a) {
     extern __shared__ __align__(128) unsigned char sm[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     MkMisc& mm = *reinterpret_cast<MkMisc*>(sm + a.off_misc);
     unsigned char* ring = sm;
+    uint64_t* fullb = reinterpret_cast<uint64_t*>(sm + (size_t)MK_NW * MK_NSLOT * R * GR_BYTES);
+    uint64_t* emptyb = fullb + MK_NW * MK_NSLOT;
     unsigned char* uni = sm + a.off_union;
     const int C = gridDim.x;
 
@@ -780,12 +823,17 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
     if (tid == 0) {
         mm.bad = 0;
         mm.last = 0;
+        for (int i = 0; i < MK_NW * MK_NSLOT; ++i) {
+            mbar_init(&fullb[i], 1);
+            mbar_init(&emptyb[i], 1);
+        }
+        fence_mbar_init();
     }
 
     // this CTA's share of every GEMV phase
     PhaseInfo* tab = reinterpret_cast<PhaseInfo*>(sm + a.off_tab);
     const int np = n_gemv_phases(a);
-    for (int pi = tid; pi < np; pi += MK_NT) {
+    for (int pi = tid; pi < np; pi += MK_THREADS) {
         const MkLin lin = phase_lin(a, pi);
         PhaseInfo P;
         P.w = lin.w;
@@ -798,14 +846,16 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
         P.seg_stride = lin.seg_stride;
         tab[pi] = P;
     }
+    // the last barrier of all MK_THREADS threads: the phase table and the stage
+    // barriers are ready before the producer warp reads them
     __syncthreads();
 
-    // prime the ring: `depth` granules per warp in flight
-    Cursor pc;
-    pc.init(tab, np, warp);
-    for (int i = 0; i < DEPTH / 2; ++i) issue_pair(pc, warp, lane, ring + ((size_t)warp * DEPTH + 2 * i) * GR_BYTES);
-    unsigned gpos = 0;
-    __syncthreads();
+    if (warp == MK_NW) {
+        // the producer warp: lane w streams compute warp w's weights
+        producer_loop<R>(a, tab, np, lane, ring, fullb, emptyb);
+        return;
+    }
+    unsigned stage = 0;
 
     const int M = a.M;
     unsigned arrivals = 0;  // completed phases (grid barrier target = arrivals * C)
@@ -820,6 +870,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
             float* red = seeds + (size_t)lin.KG * 4 * SEEDF;
             if (l > 0) ok = cta_wait(a, arrivals * C, mm);
             if (!ok) break;
+            MK_STAMP(5 * l, 0);
             StageSrc s{l == 0 ? nullptr : a.x, a.H, 0, Ly.in_norm};
             stage_acts(a, s, a.H, M, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
             if (l == 0 && blockIdx.x == 0) {
@@ -843,19 +894,22 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
                 }
             }
             if (l > 0 && a.trace && blockIdx.x == 0) trace_copy(a, l);
-            __syncthreads();
-            gemv_phase<K_QKV, DEPTH>(a, tab[4 * l + K_QKV], M, xs, seeds, red, pc, gpos, ring, false, mm);
+            csync();
+            MK_STAMP(5 * l, 1);
+            gemv_phase<K_QKV, R>(a, tab[4 * l + K_QKV], M, xs, seeds, red, stage, ring, fullb, emptyb, false, mm,
+                                 5 * l + 0);
             // the attention tiles' cached K/V rows do not depend on this step:
             // start loading them before waiting for the other CTAs' q|k|v
-            __syncthreads();
+            csync();
             if ((int)blockIdx.x < a.aa.Hkv * a.aa.nsplit) {
                 AttnArgs aa = a.aa;
                 aa.kcache = a.kc0 + (size_t)l * a.kv_layer_elems;
                 aa.vcache = a.vc0 + (size_t)l * a.kv_layer_elems;
                 attn::attn_decode_preload<RMAX, MK_NT>(aa, *reinterpret_cast<attn::DecSmem<RMAX>*>(uni),
                                                        blockIdx.x / a.aa.nsplit, blockIdx.x % a.aa.nsplit,
-                                                       a.aa.nsplit, tid, BlockSync{});
+                                                       a.aa.nsplit, tid, CSync{});
             }
+            MK_STAMP(5 * l, 6);
             cta_arrive(a);
             ++arrivals;
         }
@@ -863,6 +917,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
         {
             ok = cta_wait(a, arrivals * C, mm);
             if (!ok) break;
+            MK_STAMP(5 * l + 1, 0);
             if ((int)blockIdx.x < a.aa.Hkv * a.aa.nsplit) {
                 AttnArgs aa = a.aa;
                 aa.q_norm_w = Ly.q_norm;
@@ -871,8 +926,10 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
                 aa.vcache = a.vc0 + (size_t)l * a.kv_layer_elems;
                 attn::DecSmem<RMAX>& asm_ = *reinterpret_cast<attn::DecSmem<RMAX>*>(uni);
                 attn::attn_decode_body<RMAX, MK_NT>(aa, asm_, blockIdx.x / a.aa.nsplit, blockIdx.x % a.aa.nsplit,
-                                                    a.aa.nsplit, tid, BlockSync{}, true);
+                                                    a.aa.nsplit, tid, CSync{}, true);
             }
+            MK_STAMP(5 * l + 1, 5);
+            MK_STAMP(5 * l + 1, 6);
             cta_arrive(a);
             ++arrivals;
         }
@@ -884,11 +941,15 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
             float* red = seeds + (size_t)lin.KG * 4 * SEEDF;
             ok = cta_wait(a, arrivals * C, mm);
             if (!ok) break;
+            MK_STAMP(5 * l + 2, 0);
             if (a.trace && blockIdx.x == 0) trace_copy_n(a.attn, a.trace_attn + (size_t)l * a.M * a.QD, a.M * a.QD);
             StageSrc s{a.attn, a.QD, 0, nullptr};
             stage_acts(a, s, a.QD, M, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
-            __syncthreads();
-            gemv_phase<K_O, DEPTH>(a, tab[4 * l + K_O], M, xs, seeds, red, pc, gpos, ring, false, mm);
+            csync();
+            MK_STAMP(5 * l + 2, 1);
+            gemv_phase<K_O, R>(a, tab[4 * l + K_O], M, xs, seeds, red, stage, ring, fullb, emptyb, false, mm,
+                                 5 * l + 2);
+            MK_STAMP(5 * l + 2, 6);
             cta_arrive(a);
             ++arrivals;
         }
@@ -900,11 +961,15 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
             float* red = seeds + (size_t)lin.KG * 4 * SEEDF;
             ok = cta_wait(a, arrivals * C, mm);
             if (!ok) break;
+            MK_STAMP(5 * l + 3, 0);
             if (a.trace && blockIdx.x == 0) trace_copy_n(a.x, a.trace_mid + (size_t)l * a.M * a.H, a.M * a.H);
             StageSrc s{a.x, a.H, 0, Ly.post_norm};
             stage_acts(a, s, a.H, M, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
-            __syncthreads();
-            gemv_phase<K_GU, DEPTH>(a, tab[4 * l + K_GU], M, xs, seeds, red, pc, gpos, ring, false, mm);
+            csync();
+            MK_STAMP(5 * l + 3, 1);
+            gemv_phase<K_GU, R>(a, tab[4 * l + K_GU], M, xs, seeds, red, stage, ring, fullb, emptyb, false, mm,
+                                 5 * l + 3);
+            MK_STAMP(5 * l + 3, 6);
             cta_arrive(a);
             ++arrivals;
         }
@@ -916,10 +981,14 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
             float* red = seeds + (size_t)lin.KG * 4 * SEEDF;
             ok = cta_wait(a, arrivals * C, mm);
             if (!ok) break;
+            MK_STAMP(5 * l + 4, 0);
             StageSrc s{a.mlp, a.I, 0, nullptr};
             stage_acts(a, s, a.I, M, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
-            __syncthreads();
-            gemv_phase<K_DOWN, DEPTH>(a, tab[4 * l + K_DOWN], M, xs, seeds, red, pc, gpos, ring, false, mm);
+            csync();
+            MK_STAMP(5 * l + 4, 1);
+            gemv_phase<K_DOWN, R>(a, tab[4 * l + K_DOWN], M, xs, seeds, red, stage, ring, fullb, emptyb, false, mm,
+                                 5 * l + 4);
+            MK_STAMP(5 * l + 4, 6);
             cta_arrive(a);
             ++arrivals;
         }
@@ -932,21 +1001,25 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
         float* seeds = reinterpret_cast<float*>(uni + MK_UNI_RESERVED + (size_t)lin.KG * rows * XW * 4);
         float* red = seeds + (size_t)lin.KG * 4 * SEEDF;
         ok = cta_wait(a, arrivals * C, mm);
+        MK_STAMP(5 * a.L, 0);
         if (ok && a.trace && blockIdx.x == 0) trace_copy(a, a.L);
         if (ok) {
             StageSrc s{a.x, a.H, M - rows, a.final_norm};
             stage_acts(a, s, a.H, rows, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
-            __syncthreads();
-            gemv_phase<K_O, DEPTH>(a, tab[4 * a.L], rows, xs, seeds, red, pc, gpos, ring, true, mm);
+            csync();
+            MK_STAMP(5 * a.L, 1);
+            gemv_phase<K_O, R>(a, tab[4 * a.L], rows, xs, seeds, red, stage, ring, fullb, emptyb, true, mm, 5 * a.L);
+            MK_STAMP(5 * a.L, 6);
         }
     }
-    // no copy may still be landing in shared memory when the CTA exits
+    // no copy may still be landing in shared memory when the CTA exits (the
+    // producer warp waits for its own bulk copies)
     cp_async_wait<0>();
-    __syncthreads();
+    csync();
 
     // ---- last CTA: argmax over CTAs, step bookkeeping, counter reset
     if (tid == 0) mm.last = atom_add_acq_rel(a.sync + 1, 1u) == (unsigned)(C - 1);
-    __syncthreads();
+    csync();
     if (!mm.last) return;
     const bool aborted = *reinterpret_cast<volatile unsigned*>(a.sync + 2) != 0;
     if (!aborted && a.logits_rows > 0 && warp == 0) {
@@ -958,7 +1031,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const MkArgs a) {
             if (lane == 0) a.argmax[m] = (int)amax_key_index(b);
         }
     }
-    __syncthreads();
+    csync();
     if (tid == 0) {
         if (!aborted) {
             // step_finish_kernel semantics (misc.cu)
@@ -1061,8 +1134,11 @@ __global__ void mk_pack_kernel(const PackArgs p) {
             const unsigned short* B0 = reinterpret_cast<const unsigned short*>(p.seg[s0].b);
             const unsigned short* S1 = reinterpret_cast<const unsigned short*>(p.seg[s1].s);
             const unsigned short* B1 = reinterpret_cast<const unsigned short*>(p.seg[s1].b);
-            sbw[2 * h] = (uint32_t)S0[(size_t)ra * KG + gl] | ((uint32_t)B0[(size_t)ra * KG + gl] << 16);
-            sbw[2 * h + 1] = (uint32_t)S1[(size_t)rb * KG + gl] | ((uint32_t)B1[(size_t)rb * KG + gl] << 16);
+            // scales times 2^24 (exact in bf16): the nibbles enter the tensor core as q * 2^-24
+            const uint32_t sa = f_to_bf16bits(u16_to_f(S0[(size_t)ra * KG + gl]) * QW_NIB_SCALE);
+            const uint32_t sc = f_to_bf16bits(u16_to_f(S1[(size_t)rb * KG + gl]) * QW_NIB_SCALE);
+            sbw[2 * h] = sa | ((uint32_t)B0[(size_t)ra * KG + gl] << 16);
+            sbw[2 * h + 1] = sc | ((uint32_t)B1[(size_t)rb * KG + gl] << 16);
         }
         *reinterpret_cast<uint4*>(d + 512 + 16 * lane) = make_uint4(sbw[0], sbw[1], sbw[2], sbw[3]);
     }
@@ -1091,10 +1167,7 @@ struct MkState {
     MkLin lm{};
     unsigned* sync = nullptr;
     unsigned long long* amax_cta = nullptr;
-    float* part_g = nullptr;
-    unsigned* tile_ctr = nullptr;
     int C = 0;
-    bool attr_set[6] = {false, false, false, false, false, false};
 };
 
 void mk_free(qw_model* m) {
@@ -1104,8 +1177,6 @@ void mk_free(qw_model* m) {
     if (s->d_layers) cudaFree(s->d_layers);
     if (s->sync) cudaFree(s->sync);
     if (s->amax_cta) cudaFree(s->amax_cta);
-    if (s->part_g) cudaFree(s->part_g);
-    if (s->tile_ctr) cudaFree(s->tile_ctr);
     delete s;
     m->mk = nullptr;
 }
@@ -1176,11 +1247,6 @@ void mk_prepare(qw_model* m) {
     QW_CUDA(cudaMalloc(&s->sync, 4 * sizeof(unsigned)));
     QW_CUDA(cudaMemsetAsync(s->sync, 0, 4 * sizeof(unsigned), m->stream));
     QW_CUDA(cudaMalloc(&s->amax_cta, (size_t)C * 8 * sizeof(unsigned long long)));
-    QW_CUDA(cudaMalloc(&s->part_g, (size_t)C * 2 * 256 * sizeof(float)));
-    int max_tiles = s->lm.n_tiles;
-    for (int k = 0; k < 4; ++k) max_tiles = std::max(max_tiles, s->layers[0].lin[k].n_tiles);
-    QW_CUDA(cudaMalloc(&s->tile_ctr, (size_t)max_tiles * sizeof(unsigned)));
-    QW_CUDA(cudaMemsetAsync(s->tile_ctr, 0, (size_t)max_tiles * sizeof(unsigned), m->stream));
     QW_CUDA(cudaStreamSynchronize(m->stream));
 }
 
@@ -1202,16 +1268,12 @@ size_t mk_union_bytes(const MkState* s, int M, int rows, int C) {
     return (u + 127) & ~(size_t)127;
 }
 
-template <int RMAX, int DEPTH>
-void mk_launch_d(qw_model* m, MkArgs& a, cudaStream_t st, size_t smem, int max_smem, bool& attr_set) {
-    if (!attr_set) {
-        QW_CUDA(cudaFuncSetAttribute(decode_step_kernel<RMAX, DEPTH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     max_smem));
-        attr_set = true;
-    }
+template <int RMAX, int R>
+void mk_launch_d(qw_model* m, MkArgs& a, cudaStream_t st, size_t smem, int max_smem) {
+    QW_CUDA(ensure_max_dyn_smem(decode_step_kernel<RMAX, R>, max_smem));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(m->mk->C);
-    cfg.blockDim = dim3(MK_NT);
+    cfg.blockDim = dim3(MK_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -1219,12 +1281,13 @@ void mk_launch_d(qw_model* m, MkArgs& a, cudaStream_t st, size_t smem, int max_s
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    QW_CUDA(cudaLaunchKernelEx(&cfg, decode_step_kernel<RMAX, DEPTH>, a));
+    QW_CUDA(cudaLaunchKernelEx(&cfg, decode_step_kernel<RMAX, R>, a));
 }
 
-// Ring depth 16 granules per warp when shared memory allows, else 8.
+// Ring stages of 8 granules per copy (two per compute warp) when shared memory
+// allows, else 4.
 template <int RMAX>
-bool mk_launch_t(qw_model* m, MkArgs& a, cudaStream_t st, int slot_idx) {
+bool mk_launch_t(qw_model* m, MkArgs& a, cudaStream_t st) {
     MkState* s = m->mk;
     int max_smem = 0;
     QW_CUDA(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device));
@@ -1232,22 +1295,22 @@ bool mk_launch_t(qw_model* m, MkArgs& a, cudaStream_t st, int slot_idx) {
     const int np = 4 * a.L + (a.logits_rows > 0 ? 1 : 0);
     const size_t misc_struct = (sizeof(MkMisc) + 127) & ~(size_t)127;
     const size_t misc = misc_struct + (((size_t)np * sizeof(PhaseInfo) + 127) & ~(size_t)127);
-    const long long room = (long long)max_smem - (long long)uni - (long long)misc;
-    const long long per_depth = (long long)MK_NW * GR_BYTES;
-    int depth = room >= 16 * per_depth ? 16 : (room >= 8 * per_depth ? 8 : 0);
-    // QW_MK_DEPTH=8 caps the ring depth (profiling / testing both kernel forms)
-    if (const char* e = std::getenv("QW_MK_DEPTH"))
-        if (std::atoi(e) == 8 && depth == 16) depth = 8;
-    if (depth == 0) return false;
-    a.depth = depth;
-    a.off_union = (unsigned)((size_t)MK_NW * depth * GR_BYTES);  // a multiple of 128
+    const size_t bars = 2 * MK_NW * MK_NSLOT * sizeof(uint64_t);  // full + empty stage barriers (512 B)
+    const long long room = (long long)max_smem - (long long)uni - (long long)misc - (long long)bars;
+    const long long per_r = (long long)MK_NW * MK_NSLOT * GR_BYTES;
+    int r = room >= 8 * per_r ? 8 : (room >= 4 * per_r ? 4 : 0);
+    // QW_MK_STAGE=4 caps the stage size (profiling / testing both kernel forms)
+    if (const char* e = std::getenv("QW_MK_STAGE"))
+        if (std::atoi(e) == 4 && r == 8) r = 4;
+    if (r == 0) return false;
+    a.off_union = (unsigned)((size_t)MK_NW * MK_NSLOT * r * GR_BYTES + bars);  // a multiple of 128
     a.off_misc = a.off_union + (unsigned)uni;
     a.off_tab = a.off_misc + (unsigned)misc_struct;
     const size_t smem = a.off_misc + misc;
-    if (depth == 16)
-        mk_launch_d<RMAX, 16>(m, a, st, smem, max_smem, s->attr_set[2 * slot_idx]);
+    if (r == 8)
+        mk_launch_d<RMAX, 8>(m, a, st, smem, max_smem);
     else
-        mk_launch_d<RMAX, 8>(m, a, st, smem, max_smem, s->attr_set[2 * slot_idx + 1]);
+        mk_launch_d<RMAX, 4>(m, a, st, smem, max_smem);
     return true;
 }
 
@@ -1323,15 +1386,20 @@ bool mk_forward(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_mo
     a.out = out;
     a.gate = gate;
     a.sync = s->sync;
-    a.part_g = s->part_g;
-    a.tile_ctr = s->tile_ctr;
     a.err = m->d_err;
     a.trace = m->trace;
     a.trace_mid = m->trace_mid;
     a.trace_attn = m->trace_attn;
-    if (R <= 8) return mk_launch_t<8>(m, a, st, 0);
-    if (R <= 16) return mk_launch_t<16>(m, a, st, 1);
-    return mk_launch_t<32>(m, a, st, 2);
+    if (R <= 8) return mk_launch_t<8>(m, a, st);
+    if (R <= 16) return mk_launch_t<16>(m, a, st);
+    return mk_launch_t<32>(m, a, st);
 }
 
 }  // namespace qw
+
+#ifdef QW_MK_PROFILE
+// Profile builds: copy the persistent kernel's timing stamps to host memory.
+extern "C" __attribute__((visibility("default"))) int qw_debug_mk_prof(void* dst, size_t bytes) {
+    return cudaMemcpyFromSymbol(dst, qw::g_mk_prof, bytes) == cudaSuccess ? 0 : -6;
+}
+#endif
