@@ -313,6 +313,16 @@ QW_DEV void attn_decode_body(const AttnArgs& a, DecSmem<RMAX>& sm, const int kvh
     const int nact = min(nsplit, (T + TILE - 1) / TILE);
     float* mb = reinterpret_cast<float*>(&sm.kt[0][0][0]);
     float* lb = mb + nsplit * R;
+    // decode rows (R <= KQ, one row per thread): the row's split partials are
+    // fetched together with the split statistics, one memory round trip
+    constexpr int PMAX = 20;
+    const bool prefetch = R <= KQ && nact <= PMAX;
+    float pre[PMAX];
+    if (prefetch && kq < R) {
+#pragma unroll
+        for (int s2 = 0; s2 < PMAX; ++s2)
+            pre[s2] = s2 < nact ? __ldcg(&a.part[(((size_t)kvh * nsplit + s2) * RMAX + kq) * (D + 2) + d]) : 0.f;
+    }
     for (int idx = tid; idx < nact * R; idx += NT) {
         const int s2 = idx / R, r = idx - s2 * R;
         const float* pp = a.part + (((size_t)kvh * nsplit + s2) * RMAX + r) * (D + 2);
@@ -334,6 +344,23 @@ QW_DEV void attn_decode_body(const AttnArgs& a, DecSmem<RMAX>& sm, const int kvh
         sm.lrow[tid] = Lsum;
     }
     sync();
+    if (prefetch) {
+        if (kq < R) {
+            const int r = kq;
+            float O = 0.f;
+#pragma unroll
+            for (int s2 = 0; s2 < PMAX; ++s2) {
+                if (s2 < nact) {
+                    const float wgt = mb[s2 * R + r];
+                    O = fmaf(wgt != 0.f ? pre[s2] : 0.f, wgt, O);
+                }
+            }
+            const int gi = r / S, i = r - gi * S;
+            a.out[(size_t)i * a.ldo + (kvh * G + gi) * D + d] = f2bf(O / sm.lrow[r]);
+        }
+        if (tid == 0) a.counters[kvh] = 0u;
+        return;
+    }
     // thread = (dim, row group); per row, up to 16 splits' partials are loaded together
     for (int r = kq; r < R; r += KQ) {
         float O = 0.f;

@@ -1,0 +1,297 @@
+// Decode / verify attention inside the persistent decode kernel
+// (crates/base-mlx-core/src/model/qwen3.rs:398-518: q_norm / k_norm, RoPE,
+// in-place KV write, GQA SDPA with the causal mask of :629-653).
+//
+// Work item = (kv head, split): split s covers the 128 key positions
+// [128 s, 128 s + 128) -- fixed boundaries, so a row's summation order does
+// not depend on the sequence length or on the number of rows in the launch (a
+// (k+1)-row verify equals k+1 single-row decodes bit for bit).  The item
+// serves the G = Hq / Hkv query heads of its kv head for the S new rows
+// (R = G S rows).  Its cached keys / values arrive by two bulk copies (the
+// rows are contiguous in the [kv head][position][128] cache), issued while
+// the CTA still waits for the other CTAs' q|k|v; the new positions' k / v
+// are normalised, rotated and written to the cache by the item that owns
+// them and placed into the tile directly.
+//
+//   scores  thread = (key, row quarter); the key's dot products walk the 16
+//           dimension chunks starting at chunk (key mod 16), so a warp's 32
+//           keys read 16 different bank groups (2-way conflicts at most);
+//   softmax one warp per row over the item's 128 keys;
+//   P.V     thread = (dimension, row quarter), keys in order -- no
+//           cross-thread combine;
+// then an unnormalised partial (max, sum, o[128]) per row goes to global
+// memory and the last item of the kv head to arrive merges the splits in
+// split order, fetching every split's statistics and its row's partial
+// outputs in one round trip.
+#pragma once
+#include "attn_decode.cuh"
+
+// diagnostics: globaltimer stamp k of the item (a.prof[k], thread 0)
+#define ATTN_STAMP(k)                                                                       \
+    do {                                                                                    \
+        if (a.prof && tid == 0) {                                                           \
+            unsigned long long t_;                                                          \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                          \
+            a.prof[(k)] = t_;                                                               \
+        }                                                                                   \
+    } while (0)
+
+namespace qw {
+namespace attn {
+
+constexpr int SPLIT_KEYS = 128;
+
+template <int RMAX>
+struct SplitSmem {
+    uint64_t bar;                        // the item's bulk copies of cached K and V
+    int last;
+    float mrow[RMAX], lrow[RMAX];
+    __align__(16) float cs[RMAX][HALF];  // RoPE cos / sin rows of the S new positions
+    __align__(16) float sn[RMAX][HALF];
+    __align__(16) bf16 qn[D], kn[D];     // q_norm / k_norm weights
+    __align__(16) bf16 qs[RMAX][D];      // roped queries (bf16 values, as the reference rounds them)
+    __align__(16) float sc[RMAX][SPLIT_KEYS];  // scores, then probabilities
+    __align__(16) bf16 kt[SPLIT_KEYS][D];
+    __align__(16) bf16 vt[SPLIT_KEYS][D];
+};
+
+// Splits covering positions [0, T).
+QW_DEV int split_count(int T) { return (T + SPLIT_KEYS - 1) / SPLIT_KEYS; }
+
+// Issue the bulk copies of the item's cached rows [j0, min(j0 + 128, off)) of
+// K and V (thread 0; the barrier completes when both land) and fetch the step's
+// RoPE rows and the q/k norm weights (every thread; NT = 512).  None of it
+// depends on this step's q|k|v, so it runs before the phase barrier; the
+// caller syncs before any thread waits or reads.
+template <int RMAX>
+QW_DEV void split_preload(const AttnArgs& a, SplitSmem<RMAX>& sm, int kvh, int split, int off, int tid) {
+    for (int i = tid; i < a.S * HALF; i += 512) {
+        const int r = i / HALF, c = i - r * HALF;
+        sm.cs[r][c] = a.rope_cos[(size_t)(off + r) * HALF + c];
+        sm.sn[r][c] = a.rope_sin[(size_t)(off + r) * HALF + c];
+    }
+    if (tid < D) sm.qn[tid] = a.q_norm_w[tid];
+    else if (tid < 2 * D) sm.kn[tid - D] = a.k_norm_w[tid - D];
+    if (tid != 0) return;
+    mbar_init(&sm.bar, 1);
+    fence_mbar_init();
+    const int j0 = split * SPLIT_KEYS;
+    const int nold = max(0, min(j0 + SPLIT_KEYS, off) - j0);
+    const uint32_t bytes = (uint32_t)nold * D * 2;
+    mbar_arrive_expect_tx(&sm.bar, 2 * bytes);
+    if (nold > 0) {
+        const size_t base = ((size_t)kvh * a.max_pos + j0) * D;
+        bulk_g2s(&sm.kt[0][0], a.kcache + base, bytes, &sm.bar);
+        bulk_g2s(&sm.vt[0][0], a.vcache + base, bytes, &sm.bar);
+    }
+}
+
+// One (kv head, split) item with NT threads (NT = 512).  `preloaded`: the
+// cached rows were issued by split_preload (else this issues them).
+template <int RMAX, int NT, typename Sync>
+QW_DEV void split_body(const AttnArgs& a, SplitSmem<RMAX>& sm, const int kvh, const int split, const int nsplit,
+                       const int off, const int tid, Sync sync, bool preloaded) {
+    static_assert(NT == 512, "thread mapping assumes 512 threads");
+    constexpr int RQ = (RMAX + 3) / 4;  // rows per row quarter
+    const int lane = tid & 31, warp = tid >> 5;
+    const int S = a.S, G = a.Hq / a.Hkv, R = G * S;
+    const int T = off + S;
+    const int j0 = split * SPLIT_KEYS;
+    const int j1 = min(j0 + SPLIT_KEYS, T);
+    if (T > a.max_pos || R > RMAX) {
+        if (tid == 0) atomicOr(a.err, T > a.max_pos ? QW_DERR_KV_RANGE : QW_DERR_SHAPE);
+        return;
+    }
+    if (!preloaded) {
+        split_preload<RMAX>(a, sm, kvh, split, off, tid);
+        sync();
+    }
+    // queries of the G heads: q_norm + RoPE (warp per row)
+    for (int r = warp; r < R; r += NT / 32) {
+        const int gi = r / S, i = r - gi * S;
+        const int h = kvh * G + gi, pos = off + i;
+        float o[4];
+        (void)pos;
+        norm_rope_row(a.q + (size_t)i * a.ldq + h * D, sm.qn, a.eps, sm.cs[i], sm.sn[i], lane, o);
+        *reinterpret_cast<uint32_t*>(&sm.qs[r][2 * lane]) = pack_bf16x2(o[0], o[1]);
+        *reinterpret_cast<uint32_t*>(&sm.qs[r][HALF + 2 * lane]) = pack_bf16x2(o[2], o[3]);
+    }
+    // new positions inside this split: k_norm + RoPE, cache write, tile row
+    for (int p = max(off, j0) + warp; p < j1; p += NT / 32) {
+        const int i = p - off;
+        float o[4];
+        norm_rope_row(a.k + (size_t)i * a.ldk + kvh * D, sm.kn, a.eps, sm.cs[i], sm.sn[i], lane, o);
+        const uint32_t k01 = pack_bf16x2(o[0], o[1]), k23 = pack_bf16x2(o[2], o[3]);
+        bf16* kd = a.kcache + ((size_t)kvh * a.max_pos + p) * D;
+        *reinterpret_cast<uint32_t*>(kd + 2 * lane) = k01;
+        *reinterpret_cast<uint32_t*>(kd + HALF + 2 * lane) = k23;
+        *reinterpret_cast<uint32_t*>(&sm.kt[p - j0][2 * lane]) = k01;
+        *reinterpret_cast<uint32_t*>(&sm.kt[p - j0][HALF + 2 * lane]) = k23;
+        const uint2 vv = __ldcg(reinterpret_cast<const uint2*>(a.v + (size_t)i * a.ldv + kvh * D + 4 * lane));
+        *reinterpret_cast<uint2*>(a.vcache + ((size_t)kvh * a.max_pos + p) * D + 4 * lane) = vv;
+        *reinterpret_cast<uint2*>(&sm.vt[p - j0][4 * lane]) = vv;
+    }
+    ATTN_STAMP(1);
+    // cached rows landed (bounded wait)
+    if (!mbar_wait_bounded(&sm.bar, 0) && tid == 0) atomicOr(a.err, QW_DERR_TIMEOUT);
+    sync();
+    ATTN_STAMP(2);
+
+    // scores: thread = (key k, row quarter rq), rows rq, rq + 4, ...
+    {
+        const int k = tid & (SPLIT_KEYS - 1), rq = tid >> 7;
+        const int j = j0 + k;
+        // four partial sums per row (chunk step c -> set c & 3), added in a fixed order:
+        // short dependency chains, the same summation order for every launch
+        float acc[RQ][4];
+#pragma unroll
+        for (int q = 0; q < RQ; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
+        if (j < j1) {
+#pragma unroll
+            for (int c = 0; c < D / 8; ++c) {
+                const int dc = (c + k) & 15;
+                const uint4 u = *reinterpret_cast<const uint4*>(&sm.kt[k][dc * 8]);
+                const float kf[8] = {bits_lo_f(u.x), bits_hi_f(u.x), bits_lo_f(u.y), bits_hi_f(u.y),
+                                     bits_lo_f(u.z), bits_hi_f(u.z), bits_lo_f(u.w), bits_hi_f(u.w)};
+#pragma unroll
+                for (int q = 0; q < RQ; ++q) {
+                    const int r = rq + 4 * q;
+                    if (r < R) {
+                        const uint4 qv = *reinterpret_cast<const uint4*>(&sm.qs[r][dc * 8]);
+                        float s = acc[q][c & 3];
+                        s = fmaf(bits_lo_f(qv.x), kf[0], s); s = fmaf(bits_hi_f(qv.x), kf[1], s);
+                        s = fmaf(bits_lo_f(qv.y), kf[2], s); s = fmaf(bits_hi_f(qv.y), kf[3], s);
+                        s = fmaf(bits_lo_f(qv.z), kf[4], s); s = fmaf(bits_hi_f(qv.z), kf[5], s);
+                        s = fmaf(bits_lo_f(qv.w), kf[6], s); s = fmaf(bits_hi_f(qv.w), kf[7], s);
+                        acc[q][c & 3] = s;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < RQ; ++q) {
+            const int r = rq + 4 * q;
+            if (r < R) {
+                const int i = r % S;
+                const bool ok = (j < j1) && (j <= off + i);
+                const float dot = (acc[q][0] + acc[q][1]) + (acc[q][2] + acc[q][3]);
+                sm.sc[r][k] = ok ? dot * a.scale : -INFINITY;
+            }
+        }
+    }
+    sync();
+    ATTN_STAMP(5);
+    // softmax statistics and probabilities, one warp per row (keys lane, lane + 32, ...)
+    for (int r = warp; r < R; r += NT / 32) {
+        float s4[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) s4[u] = sm.sc[r][lane + 32 * u];
+        const float mx = warp_max(fmaxf(fmaxf(s4[0], s4[1]), fmaxf(s4[2], s4[3])));
+        float ps = 0.f;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const float p = mx == -INFINITY ? 0.f : expf(s4[u] - mx);
+            sm.sc[r][lane + 32 * u] = p;
+            ps += p;
+        }
+        ps = warp_sum(ps);
+        if (lane == 0) {
+            sm.mrow[r] = mx;
+            sm.lrow[r] = ps;
+        }
+    }
+    sync();
+    ATTN_STAMP(3);
+    // P.V: thread = (dim d, row quarter rq); keys in order
+    const int d = tid & (D - 1), rq = tid >> 7;
+    // four partial sums per row (key kk -> set kk & 3), added in a fixed order
+    float oa[RQ][4];
+#pragma unroll
+    for (int q = 0; q < RQ; ++q) oa[q][0] = oa[q][1] = oa[q][2] = oa[q][3] = 0.f;
+    const int nk = j1 - j0;
+    for (int k4 = 0; k4 < nk; k4 += 4) {
+        float vv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) vv[u] = k4 + u < nk ? bf2f(sm.vt[k4 + u][d]) : 0.f;
+#pragma unroll
+        for (int q = 0; q < RQ; ++q) {
+            const int r = rq + 4 * q;
+            if (r < R) {
+                const float4 p4 = *reinterpret_cast<const float4*>(&sm.sc[r][k4]);
+                const float pp[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (k4 + u < nk) oa[q][u] = fmaf(pp[u], vv[u], oa[q][u]);
+            }
+        }
+    }
+    float o_acc[RQ];
+#pragma unroll
+    for (int q = 0; q < RQ; ++q) o_acc[q] = (oa[q][0] + oa[q][1]) + (oa[q][2] + oa[q][3]);
+    // partial (max, sum, o) of every row
+    const size_t pbase = ((size_t)kvh * nsplit + split) * RMAX;
+#pragma unroll
+    for (int q = 0; q < RQ; ++q) {
+        const int r = rq + 4 * q;
+        if (r < R) a.part[(pbase + r) * (D + 2) + d] = o_acc[q];
+    }
+    if (tid < R) {
+        a.part[(pbase + tid) * (D + 2) + D] = sm.mrow[tid];
+        a.part[(pbase + tid) * (D + 2) + D + 1] = sm.lrow[tid];
+    }
+    sync();
+    ATTN_STAMP(4);
+    if (tid == 0) sm.last = (atom_add_acq_rel(&a.counters[kvh], 1u) == (unsigned)(nsplit - 1));
+    sync();
+    ATTN_STAMP(7);
+    if (!sm.last) return;
+
+    // merge (last split of this kv head): weights e^(m_s - max), sums in split
+    // order.  Thread (d, rq) merges rows rq, rq + 4, ...; the first PMAX
+    // splits' statistics and partial outputs are fetched in one round trip
+    // (every split up to 1024 keys), later splits batch by batch.
+    constexpr int PMAX = 8;
+    auto fetch = [&](int s2, int r, float& m_, float& l_, float& o_) {
+        const float* pp = &a.part[(((size_t)kvh * nsplit + s2) * RMAX + r) * (D + 2)];
+        m_ = __ldcg(pp + D);
+        l_ = __ldcg(pp + D + 1);
+        o_ = __ldcg(pp + d);
+    };
+    for (int q = 0; q < RQ; ++q) {
+        const int r = rq + 4 * q;
+        if (r >= R) break;
+        float m0[PMAX], l0[PMAX], o0[PMAX];
+#pragma unroll
+        for (int u = 0; u < PMAX; ++u) {
+            m0[u] = -INFINITY;
+            l0[u] = o0[u] = 0.f;
+            if (u < nsplit) fetch(u, r, m0[u], l0[u], o0[u]);
+        }
+        float M = -INFINITY;
+#pragma unroll
+        for (int u = 0; u < PMAX; ++u) M = fmaxf(M, m0[u]);
+        for (int s2 = PMAX; s2 < nsplit; ++s2) M = fmaxf(M, __ldcg(&a.part[(((size_t)kvh * nsplit + s2) * RMAX + r) * (D + 2) + D]));
+        float O = 0.f, L = 0.f;
+#pragma unroll
+        for (int u = 0; u < PMAX; ++u) {
+            if (u < nsplit) {
+                const float wgt = m0[u] == -INFINITY ? 0.f : expf(m0[u] - M);
+                L = fmaf(l0[u], wgt, L);
+                O = fmaf(wgt != 0.f ? o0[u] : 0.f, wgt, O);
+            }
+        }
+        for (int s2 = PMAX; s2 < nsplit; ++s2) {
+            float m_, l_, o_;
+            fetch(s2, r, m_, l_, o_);
+            const float wgt = m_ == -INFINITY ? 0.f : expf(m_ - M);
+            L = fmaf(l_, wgt, L);
+            O = fmaf(wgt != 0.f ? o_ : 0.f, wgt, O);
+        }
+        const int gi = r / S, i = r - gi * S;
+        a.out[(size_t)i * a.ldo + (kvh * G + gi) * D + d] = f2bf(O / L);
+    }
+    if (tid == 0) a.counters[kvh] = 0u;
+}
+
+}  // namespace attn
+}  // namespace qw

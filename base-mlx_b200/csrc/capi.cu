@@ -342,6 +342,14 @@ int qw_forward_trace(qw_model* m, qw_cache* c, const uint32_t* ids, int n, uint1
     });
 }
 
+int qw_debug_decode_stamps(const qw_model* m, void* dst_host, size_t bytes, size_t* written) {
+    return guard([&] {
+        need(m && dst_host && written, "model/dst/written");
+        QW_CUDA(cudaSetDevice(m->device));
+        *written = qw::mk_prof_read(m, dst_host, bytes);
+    });
+}
+
 int qw_generate_greedy(qw_model* m, const uint32_t* prompt, int n_prompt, int max_new, const uint32_t* eos,
                        int n_eos, uint32_t* out, int* n_out, qw_gen_stats* stats) {
     return guard([&] {

@@ -10,11 +10,10 @@
 // engine.rs:197-201) and the greedy step bookkeeping.
 //
 // Grid = one CTA per SM (cooperative launch: all CTAs are resident) of 16
-// compute warps and one producer warp.  Phases are separated by a grid-wide
-// arrival counter; every wait is bounded (2 s of globaltimer), after which the
-// launch sets QW_DERR_TIMEOUT, raises an abort flag that makes every other wait
-// return, drains its copies and exits.  The compute warps synchronise among
-// themselves with a named barrier (the producer warp never joins it).
+// warps.  Phases are separated by a grid-wide arrival counter; every wait is
+// bounded (2 s of globaltimer), after which the launch sets QW_DERR_TIMEOUT,
+// raises an abort flag that makes every other wait return, drains its copies
+// and exits.
 //
 // Weight stream.  At model load every quantized linear is repacked into
 // 576-byte granules (16 rows x 64 inputs).  Bytes 0..511 hold the nibbles so
@@ -31,20 +30,21 @@
 // and every warp an equal contiguous sixteenth of the CTA's (tile, group)
 // pairs; tile partial sums are combined across warps in warp order (results
 // do not depend on the number of rows).
-// Weight stream: weights never depend on activations, so the producer warp
-// (lane w serving compute warp w) walks warp w's granule sequence across tile,
-// phase and layer boundaries and copies it, R granules (4.6 KB) per bulk copy
-// (cp.async.bulk, completion counted on an mbarrier), into a private ring of
-// two stages per compute warp; the compute warp releases a stage through a
-// second mbarrier.  HBM keeps streaming while the compute warps wait at a
-// phase barrier, and no compute warp spends issue slots on copies.
+// Weight stream: weights never depend on activations, so each warp walks its
+// own granule sequence across tile, phase and layer boundaries and copies it,
+// R granules (2.3 KB) per bulk copy (cp.async.bulk through the TMA engine,
+// completion counted on an mbarrier), into a private ring of four stages: the
+// moment the warp has consumed a stage, its lane 0 issues the copy of the
+// stage four ahead into the freed slot.  HBM keeps streaming while the warps
+// wait at a phase barrier, a copy costs the warp a handful of instructions per
+// 2.3 KB, and nothing polls for free slots.
 #include <cuda_fp16.h>
 
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>
 
-#include "attn_decode.cuh"
+#include "attn_split.cuh"
 #include "model.h"
 #include "smem_attr.h"
 
@@ -57,17 +57,19 @@ namespace {
 #endif
 constexpr int MK_NW = QW_MK_NW;           // compute warps
 constexpr int MK_NT = MK_NW * 32;         // compute threads (the named barrier's count)
-constexpr int MK_THREADS = MK_NT + 32;    // + the producer warp
-constexpr int MK_NSLOT = 2;               // ring stages per compute warp
+constexpr int MK_NSLOT = 4;               // ring stages per warp
 constexpr int GR_BYTES = 576;  // one granule: 512 B nibbles + 64 B scales/biases
 // The GEMV phases stage their activations past the head of the shared union,
-// which holds the attention tile mbarriers (attn::DecSmem::tbar, written by
+// which holds the attention item's mbarrier (attn::SplitSmem::bar, written by
 // asynchronous cp.async arrivals): staged data never shares bytes with a
 // barrier that an arrival could still update.
 constexpr size_t MK_UNI_RESERVED = 128;
 constexpr int XW = 36;         // words per (group, column) block of staged activations (32 + 4 pad)
 constexpr int SEEDF = 2;       // floats per (group, quad t) entry: sum(x) of columns 2t, 2t+1
 constexpr unsigned long long MK_TIMEOUT_NS = 2000000000ull;
+#ifndef QW_MK_POLL_NS
+#define QW_MK_POLL_NS 64  // back-off between polls of the phase counter
+#endif
 
 enum { K_QKV = 0, K_O = 1, K_GU = 2, K_DOWN = 3 };
 
@@ -114,6 +116,7 @@ struct MkArgs {
     bf16* trace;     // diagnostics: residual stream after the embedding and every layer, [L + 1][M][H]
     bf16* trace_mid;   // diagnostics: residual after each attention block, [L][M][H]
     bf16* trace_attn;  // diagnostics: attention output of each layer, [L][M][QD]
+    unsigned long long* prof;  // diagnostics: phase timing stamps (see MK_STAMP), or null
     unsigned off_union, off_misc, off_tab;
 };
 
@@ -125,6 +128,7 @@ struct MkMisc {
     unsigned long long amax[8];
     int bad;
     int last;
+    int seq;  // the cache's sequence length at launch (constant until the last CTA's bookkeeping)
 };
 
 // ---- device helpers -------------------------------------------------------
@@ -177,12 +181,15 @@ QW_DEV int range_lo(int c, int N, int C) { return (int)(((long long)c * N) / C);
 // memory so that walking the granule stream needs no global loads.
 struct PhaseInfo {
     const unsigned char* w;  // packed granules of the whole linear
+    const bf16* norm;        // a norm weight read by this layer's steps: q|k|v phase: input RMSNorm;
+                             // o phase: q_norm; gate|up phase: post-attention RMSNorm; down phase:
+                             // k_norm; lm_head phase: the final norm
     int tg0, tg1;            // this CTA's tile-groups
     int KG, R16;
     int N;                   // tile-groups in the phase
     int seg_stride;
 };
-static_assert(sizeof(PhaseInfo) == 32, "PhaseInfo layout");
+static_assert(sizeof(PhaseInfo) == 40, "PhaseInfo layout");
 
 QW_DEV void warp_range(const PhaseInfo& P, int warp, int& wa, int& wb) {
     const int n = P.tg1 - P.tg0;
@@ -190,12 +197,9 @@ QW_DEV void warp_range(const PhaseInfo& P, int warp, int& wa, int& wb) {
     wb = P.tg0 + ((warp + 1) * n) / MK_NW;
 }
 
-QW_DEV void mbar_arrive_cta(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-// Bounded mbarrier wait (4 s of globaltimer, or the launch's abort flag).
-QW_DEV bool mbar_wait_mk(uint64_t* bar, uint32_t parity, const unsigned* abort_flag) {
-    if (mbar_try_wait(bar, parity)) return true;
+// Bounded mbarrier wait (4 s of globaltimer, or the launch's abort flag); the
+// slow path is out of line so the weight loop keeps its registers.
+__device__ __noinline__ bool mbar_wait_mk_slow(uint64_t* bar, uint32_t parity, const unsigned* abort_flag) {
     const unsigned long long t0 = globaltimer();
     for (unsigned it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
@@ -204,6 +208,9 @@ QW_DEV bool mbar_wait_mk(uint64_t* bar, uint32_t parity, const unsigned* abort_f
             if (globaltimer() - t0 > 2 * MK_TIMEOUT_NS) return false;
         }
     }
+}
+QW_DEV bool mbar_wait_mk(uint64_t* bar, uint32_t parity, const unsigned* abort_flag) {
+    return mbar_try_wait(bar, parity) || mbar_wait_mk_slow(bar, parity, abort_flag);
 }
 
 QW_DEV bool mbar_test(uint64_t* bar, uint32_t parity) {
@@ -215,83 +222,49 @@ QW_DEV bool mbar_test(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// The shared-memory reads of a ring slot (generic proxy) are ordered before the
+// bulk copy (async proxy) that refills it.
+QW_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// Producer lane w (of 16): copies compute warp w's granules, phase after phase,
-// into its ring (R granules per stage, a stage never spans two phases).  Stage
-// s goes to slot s % MK_NSLOT once the compute warp has released the slot's
-// previous stage.  The lanes poll their release barriers without blocking and
-// the warp never waits on one lane's barrier while another lane could copy;
-// after a round without progress it sleeps briefly, leaving issue slots to the
-// compute warps.  Before returning it waits until every copy it issued has
-// landed, so the CTA never exits with a copy in flight.
+// A compute warp's weight stream: where its next bulk copy starts.  Stage s of
+// the warp's sequence (R granules, never spanning two phases) goes to ring slot
+// s % MK_NSLOT; the warp's lane 0 issues it right after the warp has consumed
+// stage s - MK_NSLOT from that slot, so copies run MK_NSLOT stages ahead of
+// the computation, across tile, phase and layer boundaries (weights never
+// depend on activations), and no thread ever polls for a free slot.
+struct IssueCur {
+    int pi;          // phase of the next copy (np: stream exhausted)
+    int gi, ge;      // next granule and end of the warp's range in that phase
+    unsigned stage;  // stages issued so far
+};
+
+// Advance to the next non-empty range of warp w, from phase c.pi on.
+QW_DEV void issue_enter(IssueCur& c, const PhaseInfo* tab, int np, int w) {
+    for (; c.pi < np; ++c.pi) {
+        int wa, wb;
+        warp_range(tab[c.pi], w, wa, wb);
+        c.gi = wa * tab[c.pi].R16;
+        c.ge = wb * tab[c.pi].R16;
+        if (c.gi < c.ge) return;
+    }
+}
+
+// Lane 0: issue the warp's next stage, if the stream has one (out of line: it
+// runs once per stage and keeps its registers out of the weight loop).
 template <int R>
-QW_DEV void producer_loop(const MkArgs& a, const PhaseInfo* tab, int np, int lane, unsigned char* ring,
-                          uint64_t* fullb, uint64_t* emptyb) {
-    const int w = lane < MK_NW ? lane : 0;
-    unsigned char* wring = ring + (size_t)w * MK_NSLOT * R * GR_BYTES;
-    uint64_t* fb = fullb + w * MK_NSLOT;
-    uint64_t* eb = emptyb + w * MK_NSLOT;
-    unsigned stage = 0;
-    int pi = 0, gi = 0, ge = 0;
-    // next non-empty range of this lane's warp, from phase pi on
-    auto enter = [&]() {
-        for (; pi < np; ++pi) {
-            int wa, wb;
-            warp_range(tab[pi], w, wa, wb);
-            gi = wa * tab[pi].R16;
-            ge = wb * tab[pi].R16;
-            if (gi < ge) return;
-        }
-    };
-    if (lane < MK_NW) enter();
-    bool active = lane < MK_NW && pi < np;
-    bool failed = false;
-    unsigned long long t_last = globaltimer();
-    unsigned idle = 0;
-    while (__any_sync(0xffffffffu, active)) {
-        bool progress = false;
-        if (active) {
-            const unsigned slot = stage % MK_NSLOT;
-            if (stage < MK_NSLOT || mbar_test(&eb[slot], ((stage / MK_NSLOT) - 1) & 1)) {
-                const int n = min(R, ge - gi);
-                mbar_arrive_expect_tx(&fb[slot], (uint32_t)(n * GR_BYTES));
-                bulk_g2s(wring + (size_t)slot * R * GR_BYTES, tab[pi].w + (size_t)gi * GR_BYTES,
-                         (uint32_t)(n * GR_BYTES), &fb[slot]);
-                gi += n;
-                ++stage;
-                if (gi >= ge) {
-                    ++pi;
-                    enter();
-                    active = pi < np;
-                }
-                progress = true;
-            }
-        }
-        if (__any_sync(0xffffffffu, progress)) {
-            idle = 0;
-        } else if ((++idle & 1023u) == 0) {
-            // rarely: the abort flag (a global read) and the time bound
-            const unsigned long long now = globaltimer();
-            if (idle == 1024u) t_last = now;
-            if (*reinterpret_cast<const volatile unsigned*>(a.sync + 2) || now - t_last > 2 * MK_TIMEOUT_NS) {
-                failed = !*reinterpret_cast<const volatile unsigned*>(a.sync + 2);
-                break;
-            }
-        } else {
-            __nanosleep(20);
-        }
-    }
-    if (failed && lane == 0) {
-        atomicOr(a.err, QW_DERR_TIMEOUT);
-        atomicExch(a.sync + 2, 1u);
-    }
-    if (lane < MK_NW) {
-        for (unsigned s2 = stage > MK_NSLOT ? stage - MK_NSLOT : 0; s2 < stage; ++s2) {
-            // landed, or consumed (the slot's phase has moved on): returns at once
-            const unsigned long long t0 = globaltimer();
-            while (!mbar_test(&fb[s2 % MK_NSLOT], (s2 / MK_NSLOT) & 1))
-                if (globaltimer() - t0 > 2 * MK_TIMEOUT_NS) break;
-        }
+__device__ __noinline__ void issue_next(IssueCur& c, const PhaseInfo* tab, int np, int w, unsigned char* ring, uint64_t* fullb) {
+    if (c.pi >= np) return;
+    const unsigned slot = c.stage % MK_NSLOT;
+    uint64_t* fb = fullb + w * MK_NSLOT + slot;
+    const int n = min(R, c.ge - c.gi);
+    mbar_arrive_expect_tx(fb, (uint32_t)(n * GR_BYTES));
+    bulk_g2s(ring + ((size_t)w * MK_NSLOT + slot) * R * GR_BYTES, tab[c.pi].w + (size_t)c.gi * GR_BYTES,
+             (uint32_t)(n * GR_BYTES), fb);
+    c.gi += n;
+    ++c.stage;
+    if (c.gi >= c.ge) {
+        ++c.pi;
+        issue_enter(c, tab, np, w);
     }
 }
 
@@ -364,10 +337,22 @@ QW_DEV void stage_seeds(float sum, bool valid, int gl, int m, int j, float* seed
     if (valid && j == 0) seeds[(size_t)(gl * 4 + (m >> 1)) * SEEDF + (m & 1)] = tot;
 }
 
-QW_DEV void apply_norm(const StageSrc& s, float r, int k, float (&v)[16]) {
+QW_DEV void load_norm16(const StageSrc& s, int k, uint32_t (&W)[8]) {
     const uint4* wp = reinterpret_cast<const uint4*>(s.norm + k);
     const uint4 w0 = wp[0], w1 = wp[1];
-    const uint32_t W[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    W[0] = w0.x; W[1] = w0.y; W[2] = w0.z; W[3] = w0.w;
+    W[4] = w1.x; W[5] = w1.y; W[6] = w1.z; W[7] = w1.w;
+}
+QW_DEV void apply_norm_w(const uint32_t (&W)[8], float r, float (&v)[16]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        v[2 * i] = bfr(__fmul_rn(__fmul_rn(v[2 * i], r), bits_lo_f(W[i])));
+        v[2 * i + 1] = bfr(__fmul_rn(__fmul_rn(v[2 * i + 1], r), bits_hi_f(W[i])));
+    }
+}
+QW_DEV void apply_norm(const StageSrc& s, float r, int k, float (&v)[16]) {
+    uint32_t W[8];
+    load_norm16(s, k, W);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         v[2 * i] = bfr(__fmul_rn(__fmul_rn(v[2 * i], r), bits_lo_f(W[i])));
@@ -416,7 +401,7 @@ QW_DEV void unpack16(const uint32_t (&X)[8], float (&v)[16]) {
     }
 }
 
-// Barrier of the compute warps only (named barrier 1; the producer warp never joins).
+// Block barrier of the 16 warps (named barrier 1).
 QW_DEV void csync() { asm volatile("bar.sync 1, %0;" ::"n"(MK_NT) : "memory"); }
 
 QW_DEV void stage_acts(const MkArgs& a, const StageSrc& s, int K, int Mx, uint32_t* xs, float* seeds, float* sq,
@@ -424,80 +409,49 @@ QW_DEV void stage_acts(const MkArgs& a, const StageSrc& s, int K, int Mx, uint32
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int KG = K / 64;
     const int units = KG * Mx * 4;
-    if (s.norm && units <= 2 * MK_NT) {
-        // RMSNorm in one pass over x: each thread keeps its (at most two) units
-        // in registers while the per-row sums of squares are reduced
-        uint32_t X0[8], X1[8];
-        int gl0 = 0, m0 = 0, j0 = 0, gl1 = 0, m1 = 0, j1 = 0;
-        const int u0 = tid, u1 = tid + MK_NT;
-        if (u0 < units) {
-            unit_coords(u0, Mx, gl0, m0, j0);
-            load16_packed(a, s, m0, gl0 * 64 + 16 * j0, X0);
-            sq[u0] = sumsq_packed(X0);
-        }
-        if (u1 < units) {
-            unit_coords(u1, Mx, gl1, m1, j1);
-            load16_packed(a, s, m1, gl1 * 64 + 16 * j1, X1);
-            sq[u1] = sumsq_packed(X1);
+    if (s.norm) {
+        // RMSNorm statistics, the same summation order for every row count:
+        // per-unit sums of squares, then per row its units lane-strided and a
+        // fixed shuffle tree.  With one unit per thread the unit (values and
+        // norm weights, fetched together: one memory round trip) stays in
+        // registers for the second pass; otherwise the second pass reloads.
+        const bool keep = units <= MK_NT;
+        uint32_t X0[8], W0[8];
+        int gl0 = 0, m0 = 0, j0 = 0;
+        for (int u = tid; u < units; u += MK_NT) {
+            int gl, m, j;
+            unit_coords(u, Mx, gl, m, j);
+            uint32_t X[8];
+            load16_packed(a, s, m, gl * 64 + 16 * j, X);
+            if (keep) {
+                load_norm16(s, gl * 64 + 16 * j, W0);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) X0[i] = X[i];
+                gl0 = gl;
+                m0 = m;
+                j0 = j;
+            }
+            sq[u] = sumsq_packed(X);
         }
         csync();
         if (warp < Mx) {
-            // row `warp`: its KG*4 units, lane-strided, then a fixed shuffle tree
             float q = 0.f;
             for (int i = lane; i < KG * 4; i += 32) q += sq[((i >> 2) * Mx + warp) * 4 + (i & 3)];
             q = warp_sum(q);
             if (lane == 0) mm.rnorm[warp] = 1.0f / sqrtf(q / (float)K + a.eps);
         }
         csync();
-        float sum0 = 0.f, sum1 = 0.f;
-        if (u0 < units) {
-            float v[16];
-            unpack16(X0, v);
-            apply_norm(s, mm.rnorm[m0], gl0 * 64 + 16 * j0, v);
-            sum0 = stage_unit(v, gl0, m0, j0, Mx, xs);
-        }
-        stage_seeds(sum0, u0 < units, gl0, m0, j0, seeds);
-        if (u1 - lane < units) {  // warp-uniform: some lane of this warp has a unit
-            if (u1 < units) {
+        if (keep) {
+            float sum0 = 0.f;
+            if (tid < units) {
                 float v[16];
-                unpack16(X1, v);
-                apply_norm(s, mm.rnorm[m1], gl1 * 64 + 16 * j1, v);
-                sum1 = stage_unit(v, gl1, m1, j1, Mx, xs);
+                unpack16(X0, v);
+                apply_norm_w(W0, mm.rnorm[m0], v);
+                sum0 = stage_unit(v, gl0, m0, j0, Mx, xs);
             }
-            stage_seeds(sum1, u1 < units, gl1, m1, j1, seeds);
+            stage_seeds(sum0, tid < units, gl0, m0, j0, seeds);
+            return;
         }
-        return;
-    }
-    if (s.norm) {
-        // RMSNorm statistics: fp32 sum of squares per row
-        float ss[8];
-#pragma unroll
-        for (int m = 0; m < 8; ++m) ss[m] = 0.f;
-        for (int k = tid * 16; k < K; k += MK_NT * 16) {
-#pragma unroll
-            for (int m = 0; m < 8; ++m) {
-                if (m < Mx) {
-                    float v[16];
-                    load16(a, s, m, k, v);
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) ss[m] = fmaf(v[i], v[i], ss[m]);
-                }
-            }
-        }
-#pragma unroll
-        for (int m = 0; m < 8; ++m) {
-            if (m < Mx) {
-                const float w = warp_sum(ss[m]);
-                if (lane == 0) mm.ssq[warp][m] = w;
-            }
-        }
-        csync();
-        if (tid < Mx) {
-            float tot = 0.f;
-            for (int w = 0; w < MK_NW; ++w) tot += mm.ssq[w][tid];
-            mm.rnorm[tid] = 1.0f / sqrtf(tot / (float)K + a.eps);
-        }
-        csync();
     }
     for (int ub = 0; ub < units; ub += MK_NT) {
         const int u = ub + tid;
@@ -521,6 +475,7 @@ QW_DEV bool cta_wait(const MkArgs& a, unsigned target, MkMisc& mm) {
         const unsigned long long t0 = globaltimer();
         unsigned it = 0;
         while ((int)(ld_acquire_u32(a.sync) - target) < 0) {
+            __nanosleep(QW_MK_POLL_NS);
             if ((++it & 31u) == 0) {
                 if (*reinterpret_cast<volatile unsigned*>(a.sync + 2)) {
                     mm.bad = 1;
@@ -623,27 +578,142 @@ QW_DEV void store_elem(const MkArgs& a, bool lm, int row, int m, const float (&v
     }
 }
 
-// ---- optional timing stamps (builds with -DQW_MK_PROFILE only) --------------
-// Thread 0 of each CTA records globaltimer at points of every phase:
-// g_mk_prof[cta][phase][k], k = 0 after the phase barrier, 1 after activation
-// staging, 2 first weight stage ready, 3 own weight loop done, 4 all warps'
-// loops done, 5 epilogue done, 6 before arriving.  Read with qw_debug_mk_prof.
-#ifdef QW_MK_PROFILE
+// ---- optional timing stamps --------------------------------------------------
+// With a stamp buffer (MkArgs::prof, set by the QW_MK_PROFILE environment
+// variable), thread 0 of each CTA records globaltimer at points of every
+// phase: prof[(cta * MK_PROF_PHASES + phase) * 8 + k], k = 0 after the phase
+// barrier, 1 after activation staging, 2 first weight stage ready, 3 own
+// weight loop done, 4 all warps' loops done, 5 epilogue done, 6 before
+// arriving.  Phase 5l + {0..4} = layer l's q|k|v, attention, o, gate|up, down;
+// 5L = lm_head.  Read back with qw_debug_mk_prof.
 constexpr int MK_PROF_PHASES = 4 * 64 * 2 + 2;
-__device__ unsigned long long g_mk_prof[160][MK_PROF_PHASES][8];
-#define MK_STAMP(ph, k) \
-    do { \
-        if (threadIdx.x == 0 && (ph) < MK_PROF_PHASES) g_mk_prof[blockIdx.x][(ph)][(k)] = globaltimer(); \
+#define MK_STAMP(ph, k)                                                                                      \
+    do {                                                                                                     \
+        if (a.prof && threadIdx.x == 0 && (ph) < MK_PROF_PHASES)                                             \
+            a.prof[((size_t)blockIdx.x * MK_PROF_PHASES + (ph)) * 8 + (k)] = globaltimer();                  \
     } while (0)
-#else
-#define MK_STAMP(ph, k) \
-    do { \
-    } while (0)
-#endif
 
 template <int KIND>
-__device__ __noinline__ void gemv_epilogue(const MkArgs& a, const PhaseInfo& P, int Mx, const float* red, bool lm,
+QW_DEV void gemv_epilogue(const MkArgs& a, const PhaseInfo& P, int Mx, const float* red, bool lm,
                                            MkMisc& mm);
+
+// Explicit shared-memory accesses on 32-bit shared addresses (the weight loop
+// below is a separate function: a generic pointer would cost it the shared path).
+QW_DEV uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+QW_DEV uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+QW_DEV float2 lds64f(uint32_t a) {
+    float2 v;
+    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a));
+    return v;
+}
+QW_DEV void sts128f(uint32_t a, float x, float y, float z, float w) {
+    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(x), "f"(y), "f"(z), "f"(w) : "memory");
+}
+
+// Where a warp's weight loop reads and writes in shared memory (32-bit shared addresses).
+struct LoopSmem {
+    uint32_t xs;     // this lane's staged activations of group 0 (column min(g, M-1), quad t)
+    uint32_t seeds;  // this lane's sum(x) entry of group 0
+    uint32_t col;    // bytes between the staged activations of consecutive groups
+    uint32_t ring;   // this warp's ring
+    uint32_t fb;     // this warp's stage barriers
+    uint32_t red;    // this warp's partials: segment s, sub-tile u at red + (s * R16 + u) * 512 + 16 * lane
+};
+
+// The warp's weight loop over granules [gi, gend) of the phase (tile segments
+// end every per_tile granules): waits for its ring stages, computes four
+// granules per batch (their weights loaded together), writes one partial per
+// tile segment, and has lane 0 refill every consumed slot with the stage
+// MK_NSLOT ahead.  Granules enter their sub-tile's accumulator in phase order.
+// Out of line, so the kernel's own live state never competes with the loop
+// for registers.
+template <int KIND, int R>
+__device__ __noinline__ void gemv_loop(const unsigned* abort_flag, int* err, const LoopSmem sm, int gi, const int gend,
+                                       const int per_tile, const int KG, unsigned* stage_io, IssueCur* ic,
+                                       const PhaseInfo* tab, int np, unsigned char* ring, uint64_t* fullb,
+                                       unsigned long long* prof_slot) {
+    constexpr int R16 = KIND == K_GU ? 2 : 1;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2;
+    unsigned stage = *stage_io;
+    int seg_end = (gi / per_tile + 1) * per_tile;
+    uint32_t red = sm.red + 16 * lane;
+    float acc[R16][4];
+#pragma unroll
+    for (int u = 0; u < R16; ++u) acc[u][0] = acc[u][1] = acc[u][2] = acc[u][3] = 0.f;
+    auto flush = [&]() {
+#pragma unroll
+        for (int u = 0; u < R16; ++u) {
+            sts128f(red + u * 512, acc[u][0], acc[u][1], acc[u][2], acc[u][3]);
+            acc[u][0] = acc[u][1] = acc[u][2] = acc[u][3] = 0.f;
+        }
+        red += R16 * 512;
+    };
+    bool first = true;
+    while (gi < gend) {
+        const int n = min(R, gend - gi);
+        const uint32_t slot = stage % MK_NSLOT;
+        uint64_t* bar = reinterpret_cast<uint64_t*>(fullb) + warp * MK_NSLOT + slot;
+        if (!mbar_wait_mk(bar, (stage / MK_NSLOT) & 1, abort_flag)) {
+            if (lane == 0) {
+                atomicOr(err, QW_DERR_TIMEOUT);
+                atomicExch(const_cast<unsigned*>(abort_flag), 1u);
+            }
+            break;
+        }
+        if (first && prof_slot && lane == 0) *prof_slot = globaltimer();
+        first = false;
+        const uint32_t sp = sm.ring + slot * (R * GR_BYTES);
+        // a stage starts at an even granule when R16 == 2 (ranges and stages are whole pairs)
+        int gl = (gi / R16) % KG;
+        uint4 xa = lds128(sm.xs + gl * sm.col), xb = lds128(sm.xs + gl * sm.col + 16);
+        float2 sx = lds64f(sm.seeds + gl * 32);
+        uint4 wv[R];
+#pragma unroll
+        for (int j = 0; j < R; ++j)
+            if (j < n) wv[j] = lds128(sp + j * GR_BYTES + 16 * lane);
+#pragma unroll
+        for (int j = 0; j < R; ++j) {
+            if (j < n) {
+                if (gi + j == seg_end) {
+                    flush();
+                    seg_end += per_tile;
+                }
+                if (j > 0 && (R16 == 1 || (j & 1) == 0)) {
+                    if (++gl == KG) gl = 0;
+                    xa = lds128(sm.xs + gl * sm.col);
+                    xb = lds128(sm.xs + gl * sm.col + 16);
+                    sx = lds64f(sm.seeds + gl * 32);
+                }
+                GAct x;
+                x.xa = xa;
+                x.xb = xb;
+                x.sx = sx;
+                float c[4];
+                granule_mma(wv[j], x, c);
+                const uint2 sb = lds64(sp + j * GR_BYTES + 512 + 8 * g);
+                granule_epi(sb, c, sx, acc[R16 == 2 ? (j & 1) : 0]);
+            }
+        }
+        // the slot is free: refill it with the stage MK_NSLOT ahead
+        __syncwarp();
+        if (lane == 0) {
+            fence_proxy_async_smem();
+            issue_next<R>(*ic, tab, np, warp, ring, fullb);
+        }
+        gi += n;
+        ++stage;
+    }
+    flush();
+    *stage_io = stage;
+}
 
 // One GEMV phase: each warp computes its granule range from its ring, writing
 // one partial per tile segment to shared memory (red: [warp][segment][sub][128]);
@@ -652,9 +722,9 @@ __device__ __noinline__ void gemv_epilogue(const MkArgs& a, const PhaseInfo& P, 
 // granules' own mma chains are independent, so this costs no latency): the
 // summation order depends only on the warp's range, never on the stage size R.
 template <int KIND, int R>
-__device__ __noinline__ void gemv_phase(const MkArgs& a, const PhaseInfo& P, int Mx, uint32_t* xs, float* seeds, float* red,
-                       unsigned& stage, unsigned char* ring, uint64_t* fullb, uint64_t* emptyb, bool lm, MkMisc& mm,
-                       int prof_id) {
+QW_DEV void gemv_phase(const MkArgs& a, const PhaseInfo& P, int Mx, uint32_t* xs, float* seeds, float* red,
+                       unsigned& stage, unsigned char* ring, uint64_t* fullb, IssueCur& ic, const PhaseInfo* tab,
+                       int np, bool lm, MkMisc& mm, int prof_id) {
     (void)prof_id;
     constexpr int R16 = KIND == K_GU ? 2 : 1;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -667,7 +737,6 @@ __device__ __noinline__ void gemv_phase(const MkArgs& a, const PhaseInfo& P, int
     const float* seeds_lane = seeds + (size_t)t * SEEDF;
     const unsigned char* wring = ring + (size_t)warp * MK_NSLOT * R * GR_BYTES;
     uint64_t* fb = fullb + warp * MK_NSLOT;
-    uint64_t* eb = emptyb + warp * MK_NSLOT;
 
     int wa, wb;
     warp_range(P, warp, wa, wb);
@@ -676,70 +745,17 @@ __device__ __noinline__ void gemv_phase(const MkArgs& a, const PhaseInfo& P, int
         mm.wr[warp] = make_int2(wa - P.tg0, wb - P.tg0);
     }
     const int per_tile = KG * R16;  // granules of one tile
-    int gi = wa * R16;              // phase-local index of the warp's next granule
-    const int gend = wb * R16;
-    int seg = 0;
-    int seg_end = (gi / per_tile + 1) * per_tile;
-    float acc[R16][4];
-#pragma unroll
-    for (int u = 0; u < R16; ++u) acc[u][0] = acc[u][1] = acc[u][2] = acc[u][3] = 0.f;
-    auto flush = [&]() {
-        float* r0 = red + ((size_t)(warp * seg_stride + seg) * R16 * 32 + lane) * 4;
-#pragma unroll
-        for (int u = 0; u < R16; ++u) {
-            *reinterpret_cast<float4*>(r0 + u * 128) = make_float4(acc[u][0], acc[u][1], acc[u][2], acc[u][3]);
-            acc[u][0] = acc[u][1] = acc[u][2] = acc[u][3] = 0.f;
-        }
-        ++seg;
-    };
-    while (gi < gend) {
-        const int n = min(R, gend - gi);
-        const unsigned slot = stage % MK_NSLOT;
-        if (!mbar_wait_mk(&fb[slot], (stage / MK_NSLOT) & 1, a.sync + 2)) {
-            if (lane == 0) {
-                atomicOr(a.err, QW_DERR_TIMEOUT);
-                atomicExch(a.sync + 2, 1u);
-            }
-            break;
-        }
-        if (gi == wa * R16) MK_STAMP(prof_id, 2);
-        const unsigned char* sp = wring + (size_t)slot * R * GR_BYTES;
-        // a stage starts at an even granule when R16 == 2 (ranges and stages are whole pairs)
-        int gl = (gi / R16) % KG;
-        GAct x = load_act(xs_lane, seeds_lane, gl, col_stride);
-        // four granules at a time (their weights in registers), the batches not unrolled
-#pragma unroll 1
-        for (int j0 = 0; j0 < n; j0 += 4) {
-            uint4 wv[4];
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj)
-                if (j0 + jj < n) wv[jj] = *reinterpret_cast<const uint4*>(sp + (j0 + jj) * GR_BYTES + 16 * lane);
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-                const int j = j0 + jj;
-                if (j < n) {
-                    if (gi + j == seg_end) {
-                        flush();
-                        seg_end += per_tile;
-                    }
-                    if (j > 0 && (R16 == 1 || (jj & 1) == 0)) {
-                        if (++gl == KG) gl = 0;
-                        x = load_act(xs_lane, seeds_lane, gl, col_stride);
-                    }
-                    float c[4];
-                    granule_mma(wv[jj], x, c);
-                    const uint2 sb = *reinterpret_cast<const uint2*>(sp + j * GR_BYTES + 512 + 8 * g);
-                    granule_epi(sb, c, x.sx, acc[R16 == 2 ? (jj & 1) : 0]);
-                }
-            }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cta(&eb[slot]);
-        gi += n;
-        ++stage;
-    }
+    LoopSmem ls;
+    ls.xs = smem_u32(xs_lane);
+    ls.seeds = smem_u32(seeds_lane);
+    ls.col = (uint32_t)col_stride * 4;
+    ls.ring = smem_u32(wring);
+    ls.fb = smem_u32(fb);
+    ls.red = smem_u32(red + (size_t)warp * seg_stride * R16 * 128);
+    if (wa < wb)
+        gemv_loop<KIND, R>(a.sync + 2, a.err, ls, wa * R16, wb * R16, per_tile, KG, &stage, &ic, tab, np, ring,
+                           fullb, a.prof ? a.prof + ((size_t)blockIdx.x * MK_PROF_PHASES + prof_id) * 8 + 2 : nullptr);
     MK_STAMP(prof_id, 3);
-    flush();
     csync();
     MK_STAMP(prof_id, 4);
     gemv_epilogue<KIND>(a, P, Mx, red, lm, mm);
@@ -748,7 +764,7 @@ __device__ __noinline__ void gemv_phase(const MkArgs& a, const PhaseInfo& P, int
 
 // The CTA's outputs of one GEMV phase from the warps' tile-segment partials.
 template <int KIND>
-__device__ __noinline__ void gemv_epilogue(const MkArgs& a, const PhaseInfo& P, int Mx, const float* red, bool lm,
+QW_DEV void gemv_epilogue(const MkArgs& a, const PhaseInfo& P, int Mx, const float* red, bool lm,
                                            MkMisc& mm) {
     constexpr int R16 = KIND == K_GU ? 2 : 1;
     const int tid = threadIdx.x, lane = tid & 31;
@@ -808,13 +824,12 @@ __device__ __noinline__ void gemv_epilogue(const MkArgs& a, const PhaseInfo& P, 
 
 // ---- the kernel ------------------------------------------------------------
 template <int RMAX, int R>
-__global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const __grid_constant__ MkArgs a) {
+__global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const __grid_constant__ MkArgs a) {
     extern __shared__ __align__(128) unsigned char sm[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     MkMisc& mm = *reinterpret_cast<MkMisc*>(sm + a.off_misc);
     unsigned char* ring = sm;
     uint64_t* fullb = reinterpret_cast<uint64_t*>(sm + (size_t)MK_NW * MK_NSLOT * R * GR_BYTES);
-    uint64_t* emptyb = fullb + MK_NW * MK_NSLOT;
     unsigned char* uni = sm + a.off_union;
     const int C = gridDim.x;
 
@@ -823,17 +838,15 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const __grid
     if (tid == 0) {
         mm.bad = 0;
         mm.last = 0;
-        for (int i = 0; i < MK_NW * MK_NSLOT; ++i) {
-            mbar_init(&fullb[i], 1);
-            mbar_init(&emptyb[i], 1);
-        }
+        mm.seq = *a.seq_len;
+        for (int i = 0; i < MK_NW * MK_NSLOT; ++i) mbar_init(&fullb[i], 1);
         fence_mbar_init();
     }
 
     // this CTA's share of every GEMV phase
     PhaseInfo* tab = reinterpret_cast<PhaseInfo*>(sm + a.off_tab);
     const int np = n_gemv_phases(a);
-    for (int pi = tid; pi < np; pi += MK_THREADS) {
+    for (int pi = tid; pi < np; pi += MK_NT) {
         const MkLin lin = phase_lin(a, pi);
         PhaseInfo P;
         P.w = lin.w;
@@ -844,34 +857,44 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const __grid
         P.KG = lin.KG;
         P.R16 = lin.R16;
         P.seg_stride = lin.seg_stride;
+        if (pi >= 4 * a.L) {
+            P.norm = a.final_norm;
+        } else {
+            const MkLayer& Ly = a.layers[pi >> 2];
+            const int k = pi & 3;
+            P.norm = k == K_QKV ? Ly.in_norm : k == K_O ? Ly.q_norm : k == K_GU ? Ly.post_norm : Ly.k_norm;
+        }
         tab[pi] = P;
     }
-    // the last barrier of all MK_THREADS threads: the phase table and the stage
-    // barriers are ready before the producer warp reads them
-    __syncthreads();
+    __syncthreads();  // the phase table and the stage barriers are ready
 
-    if (warp == MK_NW) {
-        // the producer warp: lane w streams compute warp w's weights
-        producer_loop<R>(a, tab, np, lane, ring, fullb, emptyb);
-        return;
+    // every warp starts its weight stream: the first MK_NSLOT stages in flight
+    IssueCur ic{0, 0, 0, 0u};
+    unsigned stage = 0;  // stages consumed
+    if (lane == 0) {
+        issue_enter(ic, tab, np, warp);
+        for (int i = 0; i < MK_NSLOT; ++i) issue_next<R>(ic, tab, np, warp, ring, fullb);
     }
-    unsigned stage = 0;
 
     const int M = a.M;
     unsigned arrivals = 0;  // completed phases (grid barrier target = arrivals * C)
     bool ok = true;
     for (int l = 0; l < a.L && ok; ++l) {
-        const MkLayer& Ly = a.layers[l];
+        // this layer's norm weights, from the shared-memory phase table
+#define in_norm (tab[4 * l + K_QKV].norm)
+#define q_norm (tab[4 * l + K_O].norm)
+#define post_norm (tab[4 * l + K_GU].norm)
+#define k_norm (tab[4 * l + K_DOWN].norm)
         // ---- q|k|v (x = embedding rows at layer 0)
         {
-            const MkLin lin = Ly.lin[K_QKV];
+            const PhaseInfo& lin = tab[4 * l + K_QKV];
             uint32_t* xs = reinterpret_cast<uint32_t*>(uni + MK_UNI_RESERVED);
             float* seeds = reinterpret_cast<float*>(uni + MK_UNI_RESERVED + (size_t)lin.KG * M * XW * 4);
             float* red = seeds + (size_t)lin.KG * 4 * SEEDF;
             if (l > 0) ok = cta_wait(a, arrivals * C, mm);
             if (!ok) break;
             MK_STAMP(5 * l, 0);
-            StageSrc s{l == 0 ? nullptr : a.x, a.H, 0, Ly.in_norm};
+            StageSrc s{l == 0 ? nullptr : a.x, a.H, 0, in_norm};
             stage_acts(a, s, a.H, M, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
             if (l == 0 && blockIdx.x == 0) {
                 // the residual stream starts as the embedding rows
@@ -896,18 +919,23 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const __grid
             if (l > 0 && a.trace && blockIdx.x == 0) trace_copy(a, l);
             csync();
             MK_STAMP(5 * l, 1);
-            gemv_phase<K_QKV, R>(a, tab[4 * l + K_QKV], M, xs, seeds, red, stage, ring, fullb, emptyb, false, mm,
+            gemv_phase<K_QKV, R>(a, tab[4 * l + K_QKV], M, xs, seeds, red, stage, ring, fullb, ic, tab, np, false, mm,
                                  5 * l + 0);
             // the attention tiles' cached K/V rows do not depend on this step:
             // start loading them before waiting for the other CTAs' q|k|v
             csync();
-            if ((int)blockIdx.x < a.aa.Hkv * a.aa.nsplit) {
-                AttnArgs aa = a.aa;
-                aa.kcache = a.kc0 + (size_t)l * a.kv_layer_elems;
-                aa.vcache = a.vc0 + (size_t)l * a.kv_layer_elems;
-                attn::attn_decode_preload<RMAX, MK_NT>(aa, *reinterpret_cast<attn::DecSmem<RMAX>*>(uni),
-                                                       blockIdx.x / a.aa.nsplit, blockIdx.x % a.aa.nsplit,
-                                                       a.aa.nsplit, tid, CSync{});
+            {
+                // this CTA's first attention item: issue its cached K/V rows now
+                const int nsp = attn::split_count(mm.seq + M);
+                if ((int)blockIdx.x < a.aa.Hkv * nsp) {
+                    AttnArgs aa = a.aa;
+                    aa.q_norm_w = q_norm;
+                    aa.k_norm_w = k_norm;
+                    aa.kcache = a.kc0 + (size_t)l * a.kv_layer_elems;
+                    aa.vcache = a.vc0 + (size_t)l * a.kv_layer_elems;
+                    attn::split_preload<RMAX>(aa, *reinterpret_cast<attn::SplitSmem<RMAX>*>(uni),
+                                              blockIdx.x / nsp, blockIdx.x % nsp, mm.seq, tid);
+                }
             }
             MK_STAMP(5 * l, 6);
             cta_arrive(a);
@@ -918,24 +946,28 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const __grid
             ok = cta_wait(a, arrivals * C, mm);
             if (!ok) break;
             MK_STAMP(5 * l + 1, 0);
-            if ((int)blockIdx.x < a.aa.Hkv * a.aa.nsplit) {
+            {
+                const int nsp = attn::split_count(mm.seq + M);
                 AttnArgs aa = a.aa;
-                aa.q_norm_w = Ly.q_norm;
-                aa.k_norm_w = Ly.k_norm;
+                aa.q_norm_w = q_norm;
+                aa.k_norm_w = k_norm;
                 aa.kcache = a.kc0 + (size_t)l * a.kv_layer_elems;
                 aa.vcache = a.vc0 + (size_t)l * a.kv_layer_elems;
-                attn::DecSmem<RMAX>& asm_ = *reinterpret_cast<attn::DecSmem<RMAX>*>(uni);
-                attn::attn_decode_body<RMAX, MK_NT>(aa, asm_, blockIdx.x / a.aa.nsplit, blockIdx.x % a.aa.nsplit,
-                                                    a.aa.nsplit, tid, CSync{}, true);
+                aa.prof = a.prof ? a.prof + ((size_t)blockIdx.x * MK_PROF_PHASES + 5 * l + 1) * 8 : nullptr;
+                attn::SplitSmem<RMAX>& asm_ = *reinterpret_cast<attn::SplitSmem<RMAX>*>(uni);
+                for (int it = blockIdx.x; it < a.aa.Hkv * nsp; it += C) {
+                    attn::split_body<RMAX, MK_NT>(aa, asm_, it / nsp, it % nsp, nsp, mm.seq, tid, CSync{},
+                                                  it == (int)blockIdx.x);
+                    csync();
+                }
             }
-            MK_STAMP(5 * l + 1, 5);
             MK_STAMP(5 * l + 1, 6);
             cta_arrive(a);
             ++arrivals;
         }
         // ---- o_proj + residual
         {
-            const MkLin lin = Ly.lin[K_O];
+            const PhaseInfo& lin = tab[4 * l + K_O];
             uint32_t* xs = reinterpret_cast<uint32_t*>(uni + MK_UNI_RESERVED);
             float* seeds = reinterpret_cast<float*>(uni + MK_UNI_RESERVED + (size_t)lin.KG * M * XW * 4);
             float* red = seeds + (size_t)lin.KG * 4 * SEEDF;
@@ -947,7 +979,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const __grid
             stage_acts(a, s, a.QD, M, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
             csync();
             MK_STAMP(5 * l + 2, 1);
-            gemv_phase<K_O, R>(a, tab[4 * l + K_O], M, xs, seeds, red, stage, ring, fullb, emptyb, false, mm,
+            gemv_phase<K_O, R>(a, tab[4 * l + K_O], M, xs, seeds, red, stage, ring, fullb, ic, tab, np, false, mm,
                                  5 * l + 2);
             MK_STAMP(5 * l + 2, 6);
             cta_arrive(a);
@@ -955,7 +987,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const __grid
         }
         // ---- gate|up + SwiGLU
         {
-            const MkLin lin = Ly.lin[K_GU];
+            const PhaseInfo& lin = tab[4 * l + K_GU];
             uint32_t* xs = reinterpret_cast<uint32_t*>(uni + MK_UNI_RESERVED);
             float* seeds = reinterpret_cast<float*>(uni + MK_UNI_RESERVED + (size_t)lin.KG * M * XW * 4);
             float* red = seeds + (size_t)lin.KG * 4 * SEEDF;
@@ -963,11 +995,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const __grid
             if (!ok) break;
             MK_STAMP(5 * l + 3, 0);
             if (a.trace && blockIdx.x == 0) trace_copy_n(a.x, a.trace_mid + (size_t)l * a.M * a.H, a.M * a.H);
-            StageSrc s{a.x, a.H, 0, Ly.post_norm};
+            StageSrc s{a.x, a.H, 0, post_norm};
             stage_acts(a, s, a.H, M, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
             csync();
             MK_STAMP(5 * l + 3, 1);
-            gemv_phase<K_GU, R>(a, tab[4 * l + K_GU], M, xs, seeds, red, stage, ring, fullb, emptyb, false, mm,
+            gemv_phase<K_GU, R>(a, tab[4 * l + K_GU], M, xs, seeds, red, stage, ring, fullb, ic, tab, np, false, mm,
                                  5 * l + 3);
             MK_STAMP(5 * l + 3, 6);
             cta_arrive(a);
@@ -975,7 +1007,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const __grid
         }
         // ---- down + residual
         {
-            const MkLin lin = Ly.lin[K_DOWN];
+            const PhaseInfo& lin = tab[4 * l + K_DOWN];
             uint32_t* xs = reinterpret_cast<uint32_t*>(uni + MK_UNI_RESERVED);
             float* seeds = reinterpret_cast<float*>(uni + MK_UNI_RESERVED + (size_t)lin.KG * M * XW * 4);
             float* red = seeds + (size_t)lin.KG * 4 * SEEDF;
@@ -986,16 +1018,20 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const __grid
             stage_acts(a, s, a.I, M, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
             csync();
             MK_STAMP(5 * l + 4, 1);
-            gemv_phase<K_DOWN, R>(a, tab[4 * l + K_DOWN], M, xs, seeds, red, stage, ring, fullb, emptyb, false, mm,
+            gemv_phase<K_DOWN, R>(a, tab[4 * l + K_DOWN], M, xs, seeds, red, stage, ring, fullb, ic, tab, np, false, mm,
                                  5 * l + 4);
             MK_STAMP(5 * l + 4, 6);
             cta_arrive(a);
             ++arrivals;
         }
     }
+#undef in_norm
+#undef q_norm
+#undef post_norm
+#undef k_norm
     // ---- final norm -> lm_head -> per-CTA argmax
     if (ok && a.logits_rows > 0) {
-        const MkLin lin = a.lm;
+        const PhaseInfo& lin = tab[4 * a.L];
         const int rows = a.logits_rows;
         uint32_t* xs = reinterpret_cast<uint32_t*>(uni + MK_UNI_RESERVED);
         float* seeds = reinterpret_cast<float*>(uni + MK_UNI_RESERVED + (size_t)lin.KG * rows * XW * 4);
@@ -1004,17 +1040,24 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(const __grid
         MK_STAMP(5 * a.L, 0);
         if (ok && a.trace && blockIdx.x == 0) trace_copy(a, a.L);
         if (ok) {
-            StageSrc s{a.x, a.H, M - rows, a.final_norm};
+            StageSrc s{a.x, a.H, M - rows, tab[4 * a.L].norm};
             stage_acts(a, s, a.H, rows, xs, seeds, red + (size_t)MK_NW * lin.seg_stride * lin.R16 * 128, mm);
             csync();
             MK_STAMP(5 * a.L, 1);
-            gemv_phase<K_O, R>(a, tab[4 * a.L], rows, xs, seeds, red, stage, ring, fullb, emptyb, true, mm, 5 * a.L);
+            gemv_phase<K_O, R>(a, tab[4 * a.L], rows, xs, seeds, red, stage, ring, fullb, ic, tab, np, true, mm, 5 * a.L);
             MK_STAMP(5 * a.L, 6);
         }
     }
-    // no copy may still be landing in shared memory when the CTA exits (the
-    // producer warp waits for its own bulk copies)
+    // no copy may still be landing in shared memory when the CTA exits: after an
+    // abort, wait (bounded) for the bulk copies this warp issued but never consumed
     cp_async_wait<0>();
+    if (lane == 0) {
+        for (unsigned s2 = stage; s2 < ic.stage; ++s2) {
+            const unsigned long long t0 = globaltimer();
+            while (!mbar_test(&fullb[warp * MK_NSLOT + s2 % MK_NSLOT], (s2 / MK_NSLOT) & 1))
+                if (globaltimer() - t0 > 2 * MK_TIMEOUT_NS) break;
+        }
+    }
     csync();
 
     // ---- last CTA: argmax over CTAs, step bookkeeping, counter reset
@@ -1166,6 +1209,7 @@ struct MkState {
     std::vector<MkLayer> layers;
     MkLin lm{};
     unsigned* sync = nullptr;
+    unsigned long long* prof = nullptr;  // QW_MK_PROFILE: phase timing stamps
     unsigned long long* amax_cta = nullptr;
     int C = 0;
 };
@@ -1176,6 +1220,7 @@ void mk_free(qw_model* m) {
     if (s->packed) cudaFree(s->packed);
     if (s->d_layers) cudaFree(s->d_layers);
     if (s->sync) cudaFree(s->sync);
+    if (s->prof) cudaFree(s->prof);
     if (s->amax_cta) cudaFree(s->amax_cta);
     delete s;
     m->mk = nullptr;
@@ -1247,17 +1292,22 @@ void mk_prepare(qw_model* m) {
     QW_CUDA(cudaMalloc(&s->sync, 4 * sizeof(unsigned)));
     QW_CUDA(cudaMemsetAsync(s->sync, 0, 4 * sizeof(unsigned), m->stream));
     QW_CUDA(cudaMalloc(&s->amax_cta, (size_t)C * 8 * sizeof(unsigned long long)));
+    if (std::getenv("QW_MK_PROFILE")) {
+        const size_t pb = (size_t)C * MK_PROF_PHASES * 8 * sizeof(unsigned long long);
+        QW_CUDA(cudaMalloc(&s->prof, pb));
+        QW_CUDA(cudaMemsetAsync(s->prof, 0, pb, m->stream));
+    }
     QW_CUDA(cudaStreamSynchronize(m->stream));
 }
 
 namespace {
 
-static_assert(offsetof(attn::DecSmem<8>, tbar) + sizeof(uint64_t) * 2 <= MK_UNI_RESERVED,
+static_assert(offsetof(attn::SplitSmem<8>, bar) + sizeof(uint64_t) <= MK_UNI_RESERVED,
               "attention mbarriers must sit in the reserved head of the union");
 
 template <int RMAX>
 size_t mk_union_bytes(const MkState* s, int M, int rows, int C) {
-    size_t u = sizeof(attn::DecSmem<RMAX>);
+    size_t u = sizeof(attn::SplitSmem<RMAX>);
     // staged x', seeds, per-warp partials and (RMSNorm phases) per-unit sums of squares
     auto need = [&](const MkLin& lin, int Mx, bool norm) {
         return (size_t)lin.KG * Mx * XW * 4 + (size_t)lin.KG * 4 * SEEDF * 4 +
@@ -1273,7 +1323,7 @@ void mk_launch_d(qw_model* m, MkArgs& a, cudaStream_t st, size_t smem, int max_s
     QW_CUDA(ensure_max_dyn_smem(decode_step_kernel<RMAX, R>, max_smem));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(m->mk->C);
-    cfg.blockDim = dim3(MK_THREADS);
+    cfg.blockDim = dim3(MK_NT);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -1284,8 +1334,8 @@ void mk_launch_d(qw_model* m, MkArgs& a, cudaStream_t st, size_t smem, int max_s
     QW_CUDA(cudaLaunchKernelEx(&cfg, decode_step_kernel<RMAX, R>, a));
 }
 
-// Ring stages of 8 granules per copy (two per compute warp) when shared memory
-// allows, else 4.
+// Ring stages of 4 granules per copy (four per warp) when shared memory
+// allows, else 2.
 template <int RMAX>
 bool mk_launch_t(qw_model* m, MkArgs& a, cudaStream_t st) {
     MkState* s = m->mk;
@@ -1295,26 +1345,35 @@ bool mk_launch_t(qw_model* m, MkArgs& a, cudaStream_t st) {
     const int np = 4 * a.L + (a.logits_rows > 0 ? 1 : 0);
     const size_t misc_struct = (sizeof(MkMisc) + 127) & ~(size_t)127;
     const size_t misc = misc_struct + (((size_t)np * sizeof(PhaseInfo) + 127) & ~(size_t)127);
-    const size_t bars = 2 * MK_NW * MK_NSLOT * sizeof(uint64_t);  // full + empty stage barriers (512 B)
+    const size_t bars = MK_NW * MK_NSLOT * sizeof(uint64_t);  // stage barriers (512 B)
     const long long room = (long long)max_smem - (long long)uni - (long long)misc - (long long)bars;
     const long long per_r = (long long)MK_NW * MK_NSLOT * GR_BYTES;
-    int r = room >= 8 * per_r ? 8 : (room >= 4 * per_r ? 4 : 0);
-    // QW_MK_STAGE=4 caps the stage size (profiling / testing both kernel forms)
+    int r = room >= 4 * per_r ? 4 : (room >= 2 * per_r ? 2 : 0);
+    // QW_MK_STAGE=2 caps the stage size (profiling / testing both kernel forms)
     if (const char* e = std::getenv("QW_MK_STAGE"))
-        if (std::atoi(e) == 4 && r == 8) r = 4;
+        if (std::atoi(e) == 2 && r == 4) r = 2;
     if (r == 0) return false;
     a.off_union = (unsigned)((size_t)MK_NW * MK_NSLOT * r * GR_BYTES + bars);  // a multiple of 128
     a.off_misc = a.off_union + (unsigned)uni;
     a.off_tab = a.off_misc + (unsigned)misc_struct;
     const size_t smem = a.off_misc + misc;
-    if (r == 8)
-        mk_launch_d<RMAX, 8>(m, a, st, smem, max_smem);
-    else
+    if (r == 4)
         mk_launch_d<RMAX, 4>(m, a, st, smem, max_smem);
+    else
+        mk_launch_d<RMAX, 2>(m, a, st, smem, max_smem);
     return true;
 }
 
 }  // namespace
+
+size_t mk_prof_read(const qw_model* m, void* dst, size_t bytes) {
+    const MkState* s = m->mk;
+    if (!s || !s->prof) return 0;
+    const size_t pb = (size_t)s->C * MK_PROF_PHASES * 8 * sizeof(unsigned long long);
+    if (bytes < pb) return 0;
+    QW_CUDA(cudaMemcpy(dst, s->prof, pb, cudaMemcpyDeviceToHost));
+    return pb;
+}
 
 bool mk_forward(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_mode, bool store_logits,
                 int* d_argmax, cudaStream_t st, StepCtl* ctl, int* next_tok, int* out, const int* gate) {
@@ -1326,6 +1385,9 @@ bool mk_forward(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_mo
     if (R > 32) return false;
     const int rows = logits_mode == 0 ? 0 : (logits_mode == 2 ? S : 1);
     if (rows > w.cap_logits || S > w.cap_rows) return false;
+    // attention partials: [kv head][128-key split][32 rows] must fit the workspace's
+    // [kv head][2 * SMs][64 rows] buffer
+    if ((long long)((c->max_pos + attn::SPLIT_KEYS - 1) / attn::SPLIT_KEYS) * 32 > 2LL * m->num_sms * 64) return false;
 
     MkArgs a;
     std::memset(&a, 0, sizeof(a));
@@ -1390,6 +1452,7 @@ bool mk_forward(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_mo
     a.trace = m->trace;
     a.trace_mid = m->trace_mid;
     a.trace_attn = m->trace_attn;
+    a.prof = s->prof;
     if (R <= 8) return mk_launch_t<8>(m, a, st);
     if (R <= 16) return mk_launch_t<16>(m, a, st);
     return mk_launch_t<32>(m, a, st);
@@ -1397,9 +1460,3 @@ bool mk_forward(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_mo
 
 }  // namespace qw
 
-#ifdef QW_MK_PROFILE
-// Profile builds: copy the persistent kernel's timing stamps to host memory.
-extern "C" __attribute__((visibility("default"))) int qw_debug_mk_prof(void* dst, size_t bytes) {
-    return cudaMemcpyFromSymbol(dst, qw::g_mk_prof, bytes) == cudaSuccess ? 0 : -6;
-}
-#endif

@@ -83,6 +83,7 @@ struct AttnArgs {
     bf16* out; int ldo;   // [S, Hq*128]
     int nsplit;
     int* err;
+    unsigned long long* prof;  // persistent kernel diagnostics: this item's timing stamps, or null
 };
 cudaError_t launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl);
 // prefill: q/k norm + rope + cache write for all S rows, roped q to qout

@@ -158,6 +158,8 @@ qw_cache* cache_for_generate(qw_model* m, int need_pos);
 // decode_mk.cu: persistent decode step (S <= 8 rows, one GPU)
 void mk_prepare(qw_model* m);
 void mk_free(qw_model* m);
+// QW_MK_PROFILE diagnostics: copy the persistent kernel's stamp buffer; bytes copied (0 when absent)
+size_t mk_prof_read(const qw_model* m, void* dst, size_t bytes);
 // false when the step does not fit the persistent kernel (the caller runs the kernel chain)
 bool mk_forward(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_mode, bool store_logits,
                 int* d_argmax, cudaStream_t st, StepCtl* ctl, int* next_tok, int* out, const int* gate);

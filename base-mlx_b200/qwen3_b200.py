@@ -125,6 +125,7 @@ SIGNATURES = {
     "qw_kv_read": [P, I, I, U16P, I, I],
     "qw_forward": [P, P, U32P, I, I, U16P, U32P],
     "qw_forward_trace": [P, P, U32P, I, U16P, U16P, U16P, U16P, U32P],
+    "qw_debug_decode_stamps": [P, P, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)],
     "qw_generate_greedy": [P, U32P, I, I, U32P, I, U32P, ctypes.POINTER(I), ctypes.POINTER(GenStats)],
     "qw_generate_sampled": [P, U32P, I, I, ctypes.c_float, ctypes.c_float, ctypes.c_uint64, I, U32P, I, U32P,
                             ctypes.POINTER(I), ctypes.POINTER(GenStats)],

@@ -15,9 +15,11 @@ dequantised weights vs the C loop) differ by up to ~0.15 in 4B logits.
   the oracle recomputes each stage (attention block; o_proj + residual; MLP
   block + residual) from the GPU's own input to that stage and cached K/V.
   Bound per stage: max |difference| <= 0.05 x RMS of the oracle's output (about
-  two bf16 ulps of a 3-sigma element) and >= 90% of elements bit-identical
-  (the MLP stage holds two GEMVs: a flipped rounding of one SiLU*up element
-  moves every down_proj output by far less than an ulp, yet re-rounds some);
+  two bf16 ulps of a 3-sigma element); >= 97% of elements bit-identical for
+  the attention and o_proj stages, >= 80% for the MLP stage, which holds two
+  GEMVs: fp32 summation order re-rounds a few gate/up outputs, and each such
+  SiLU*up flip moves every down_proj output by far less than an ulp, yet
+  together they re-round a share of them (measured 90-100%);
   the lm_head on the GPU's final residual within 2e-2 max-abs of the oracle's
   logits, same argmax.
 * 64 greedy tokens, teacher-forced (the whole path): the GPU decodes 64 tokens
@@ -90,8 +92,8 @@ def test_layers_teacher_forced(case):
     for li, st in rows:
         print("  ", li, [(round(a, 4), round(b, 4)) for a, b in st])
     for li, st in rows:
-        for stage, (rel, same) in zip(("attention", "o_proj", "mlp"), st):
-            assert rel <= 0.05 and same >= 0.90, (li, stage, rel, same)
+        for stage, (rel, same), min_same in zip(("attention", "o_proj", "mlp"), st, (0.97, 0.97, 0.80)):
+            assert rel <= 0.05 and same >= min_same, (li, stage, rel, same)
     # the head on the GPU's own final residual
     lg_ref = ref_c.head(res[L])[0]
     d = np.abs(lg_ref - logits)
