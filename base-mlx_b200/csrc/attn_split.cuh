@@ -13,12 +13,12 @@
 // are normalised, rotated and written to the cache by the item that owns
 // them and placed into the tile directly.
 //
-//   scores  thread = (key, row quarter); the key's dot products walk the 16
-//           dimension chunks starting at chunk (key mod 16), so a warp's 32
-//           keys read 16 different bank groups (2-way conflicts at most);
+//   scores  thread = (key, dimension quarter): 32 dims of one key against every
+//           row, quarter sums joined by a fixed shuffle tree;
 //   softmax one warp per row over the item's 128 keys;
-//   P.V     thread = (dimension, row quarter), keys in order -- no
-//           cross-thread combine;
+//   P.V     thread = (dimension pair, key eighth): 16 keys in order per row,
+//           the eight key-eighth sums joined in key order through shared
+//           memory;
 // then an unnormalised partial (max, sum, o[128]) per row goes to global
 // memory and the last item of the kv head to arrive merges the splits in
 // split order, fetching every split's statistics and its row's partial
@@ -137,44 +137,56 @@ QW_DEV void split_body(const AttnArgs& a, SplitSmem<RMAX>& sm, const int kvh, co
     sync();
     ATTN_STAMP(2);
 
-    // scores: thread = (key k, row quarter rq), rows rq, rq + 4, ...
+    // scores: thread = (key k = 8 warp + lane / 4, dimension quarter qq = lane & 3).
+    // Quarter qq covers dims [32 qq, 32 qq + 32) as four 16-byte chunks, visited
+    // from chunk (2 (k & 1) + qq / 2) & 3 on, so the eight lanes of a quarter-warp
+    // read eight different bank groups of K and a warp's query reads are one
+    // 128-byte wavefront.  Each row's four quarter sums meet in a fixed shuffle
+    // tree, (q0 + q1) + (q2 + q3), identical in all four lanes.
     {
-        const int k = tid & (SPLIT_KEYS - 1), rq = tid >> 7;
+        const int qq = lane & 3, kk = lane >> 2;
+        const int k = warp * 8 + kk;
         const int j = j0 + k;
-        // four partial sums per row (chunk step c -> set c & 3), added in a fixed order:
-        // short dependency chains, the same summation order for every launch
-        float acc[RQ][4];
+        const int rot = 2 * (kk & 1) + (qq >> 1);
+        float kf[4][8];
 #pragma unroll
-        for (int q = 0; q < RQ; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
-        if (j < j1) {
+        for (int c = 0; c < 4; ++c) {
+            const int dc = 4 * qq + ((c + rot) & 3);
+            const uint4 u = *reinterpret_cast<const uint4*>(&sm.kt[k][dc * 8]);
+            kf[c][0] = bits_lo_f(u.x); kf[c][1] = bits_hi_f(u.x); kf[c][2] = bits_lo_f(u.y); kf[c][3] = bits_hi_f(u.y);
+            kf[c][4] = bits_lo_f(u.z); kf[c][5] = bits_hi_f(u.z); kf[c][6] = bits_lo_f(u.w); kf[c][7] = bits_hi_f(u.w);
+        }
+        for (int r0 = 0; r0 < R; r0 += 4) {
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int c = 0; c < D / 8; ++c) {
-                const int dc = (c + k) & 15;
-                const uint4 u = *reinterpret_cast<const uint4*>(&sm.kt[k][dc * 8]);
-                const float kf[8] = {bits_lo_f(u.x), bits_hi_f(u.x), bits_lo_f(u.y), bits_hi_f(u.y),
-                                     bits_lo_f(u.z), bits_hi_f(u.z), bits_lo_f(u.w), bits_hi_f(u.w)};
+            for (int rr = 0; rr < 4; ++rr) {
+                if (r0 + rr < R) {
 #pragma unroll
-                for (int q = 0; q < RQ; ++q) {
-                    const int r = rq + 4 * q;
-                    if (r < R) {
-                        const uint4 qv = *reinterpret_cast<const uint4*>(&sm.qs[r][dc * 8]);
-                        float s = acc[q][c & 3];
-                        s = fmaf(bits_lo_f(qv.x), kf[0], s); s = fmaf(bits_hi_f(qv.x), kf[1], s);
-                        s = fmaf(bits_lo_f(qv.y), kf[2], s); s = fmaf(bits_hi_f(qv.y), kf[3], s);
-                        s = fmaf(bits_lo_f(qv.z), kf[4], s); s = fmaf(bits_hi_f(qv.z), kf[5], s);
-                        s = fmaf(bits_lo_f(qv.w), kf[6], s); s = fmaf(bits_hi_f(qv.w), kf[7], s);
-                        acc[q][c & 3] = s;
+                    for (int c = 0; c < 4; ++c) {
+                        const int dc = 4 * qq + ((c + rot) & 3);
+                        const uint4 qv = *reinterpret_cast<const uint4*>(&sm.qs[r0 + rr][dc * 8]);
+                        float s = acc[rr];
+                        s = fmaf(bits_lo_f(qv.x), kf[c][0], s); s = fmaf(bits_hi_f(qv.x), kf[c][1], s);
+                        s = fmaf(bits_lo_f(qv.y), kf[c][2], s); s = fmaf(bits_hi_f(qv.y), kf[c][3], s);
+                        s = fmaf(bits_lo_f(qv.z), kf[c][4], s); s = fmaf(bits_hi_f(qv.z), kf[c][5], s);
+                        s = fmaf(bits_lo_f(qv.w), kf[c][6], s); s = fmaf(bits_hi_f(qv.w), kf[c][7], s);
+                        acc[rr] = s;
                     }
                 }
             }
-        }
 #pragma unroll
-        for (int q = 0; q < RQ; ++q) {
-            const int r = rq + 4 * q;
+            for (int rr = 0; rr < 4; ++rr) {
+                float t = acc[rr];
+                t += __shfl_xor_sync(0xffffffffu, t, 1);
+                t += __shfl_xor_sync(0xffffffffu, t, 2);
+                acc[rr] = t;
+            }
+            // lane qq stores row r0 + qq
+            const int r = r0 + qq;
             if (r < R) {
+                const float dot = qq == 0 ? acc[0] : (qq == 1 ? acc[1] : (qq == 2 ? acc[2] : acc[3]));
                 const int i = r % S;
                 const bool ok = (j < j1) && (j <= off + i);
-                const float dot = (acc[q][0] + acc[q][1]) + (acc[q][2] + acc[q][3]);
                 sm.sc[r][k] = ok ? dot * a.scale : -INFINITY;
             }
         }
@@ -202,39 +214,60 @@ QW_DEV void split_body(const AttnArgs& a, SplitSmem<RMAX>& sm, const int kvh, co
     }
     sync();
     ATTN_STAMP(3);
-    // P.V: thread = (dim d, row quarter rq); keys in order
-    const int d = tid & (D - 1), rq = tid >> 7;
-    // four partial sums per row (key kk -> set kk & 3), added in a fixed order
-    float oa[RQ][4];
+    // P.V: thread = (dimension pair dp, key eighth ke): keys 16 ke .. 16 ke + 15 in
+    // order for rows in groups of 8; the eight key-eighth sums of a (row, dim) meet
+    // in shared memory (the K tile's space) in key order.
+    const size_t pbase = ((size_t)kvh * nsplit + split) * RMAX;
+    {
+        const int nk = j1 - j0;
+        const int dp = (warp & 1) * 32 + lane, ke = warp >> 1;
+        float* red = reinterpret_cast<float*>(&sm.kt[0][0]);  // [8 ke][8 rows][128]
+        static_assert(sizeof(sm.kt) >= 8 * 8 * D * sizeof(float), "P.V reduction buffer");
+        float2 vv[16];
 #pragma unroll
-    for (int q = 0; q < RQ; ++q) oa[q][0] = oa[q][1] = oa[q][2] = oa[q][3] = 0.f;
-    const int nk = j1 - j0;
-    for (int k4 = 0; k4 < nk; k4 += 4) {
-        float vv[4];
+        for (int t = 0; t < 16; ++t) {
+            const int key = ke * 16 + t;
+            const uint32_t w2 = *reinterpret_cast<const uint32_t*>(&sm.vt[key][2 * dp]);
+            vv[t] = key < nk ? make_float2(bits_lo_f(w2), bits_hi_f(w2)) : make_float2(0.f, 0.f);
+        }
+        const int d = tid & (D - 1), rq = tid >> 7;
+        for (int r0 = 0; r0 < R; r0 += 8) {
+            float o[8][2];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) vv[u] = k4 + u < nk ? bf2f(sm.vt[k4 + u][d]) : 0.f;
+            for (int rr = 0; rr < 8; ++rr) {
+                o[rr][0] = o[rr][1] = 0.f;
+                if (r0 + rr < R) {
 #pragma unroll
-        for (int q = 0; q < RQ; ++q) {
-            const int r = rq + 4 * q;
-            if (r < R) {
-                const float4 p4 = *reinterpret_cast<const float4*>(&sm.sc[r][k4]);
-                const float pp[4] = {p4.x, p4.y, p4.z, p4.w};
+                    for (int t4 = 0; t4 < 4; ++t4) {
+                        const float4 p4 = *reinterpret_cast<const float4*>(&sm.sc[r0 + rr][ke * 16 + 4 * t4]);
+                        const float pp[4] = {p4.x, p4.y, p4.z, p4.w};
 #pragma unroll
-                for (int u = 0; u < 4; ++u)
-                    if (k4 + u < nk) oa[q][u] = fmaf(pp[u], vv[u], oa[q][u]);
+                        for (int u = 0; u < 4; ++u) {
+                            o[rr][0] = fmaf(pp[u], vv[4 * t4 + u].x, o[rr][0]);
+                            o[rr][1] = fmaf(pp[u], vv[4 * t4 + u].y, o[rr][1]);
+                        }
+                    }
+                }
+            }
+            if (r0 > 0) sync();  // the previous row group's sums have been read
+#pragma unroll
+            for (int rr = 0; rr < 8; ++rr)
+                if (r0 + rr < R)
+                    *reinterpret_cast<float2*>(&red[(ke * 8 + rr) * D + 2 * dp]) = make_float2(o[rr][0], o[rr][1]);
+            sync();
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const int rr = rq + 4 * q, r = r0 + rr;
+                if (r < R) {
+                    float sum = red[rr * D + d];
+#pragma unroll
+                    for (int e = 1; e < 8; ++e) sum += red[(e * 8 + rr) * D + d];
+                    a.part[(pbase + r) * (D + 2) + d] = sum;
+                }
             }
         }
     }
-    float o_acc[RQ];
-#pragma unroll
-    for (int q = 0; q < RQ; ++q) o_acc[q] = (oa[q][0] + oa[q][1]) + (oa[q][2] + oa[q][3]);
-    // partial (max, sum, o) of every row
-    const size_t pbase = ((size_t)kvh * nsplit + split) * RMAX;
-#pragma unroll
-    for (int q = 0; q < RQ; ++q) {
-        const int r = rq + 4 * q;
-        if (r < R) a.part[(pbase + r) * (D + 2) + d] = o_acc[q];
-    }
+    // partial statistics (max, sum) of every row
     if (tid < R) {
         a.part[(pbase + tid) * (D + 2) + D] = sm.mrow[tid];
         a.part[(pbase + tid) * (D + 2) + D + 1] = sm.lrow[tid];
@@ -251,6 +284,7 @@ QW_DEV void split_body(const AttnArgs& a, SplitSmem<RMAX>& sm, const int kvh, co
     // splits' statistics and partial outputs are fetched in one round trip
     // (every split up to 1024 keys), later splits batch by batch.
     constexpr int PMAX = 8;
+    const int d = tid & (D - 1), rq = tid >> 7;
     auto fetch = [&](int s2, int r, float& m_, float& l_, float& o_) {
         const float* pp = &a.part[(((size_t)kvh * nsplit + s2) * RMAX + r) * (D + 2)];
         m_ = __ldcg(pp + D);

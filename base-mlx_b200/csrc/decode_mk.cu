@@ -57,7 +57,9 @@ namespace {
 #endif
 constexpr int MK_NW = QW_MK_NW;           // compute warps
 constexpr int MK_NT = MK_NW * 32;         // compute threads (the named barrier's count)
-constexpr int MK_NSLOT = 4;               // ring stages per warp
+constexpr int MK_NSLOT = 4;               // stage barriers per warp (the most stages a ring has)
+// ring stages per warp for stages of R granules (the ring holds 16 granules, 8 for R = 2)
+__host__ __device__ constexpr int mk_ns(int R) { return R >= 8 ? 2 : 4; }
 constexpr int GR_BYTES = 576;  // one granule: 512 B nibbles + 64 B scales/biases
 // The GEMV phases stage their activations past the head of the shared union,
 // which holds the attention item's mbarrier (attn::SplitSmem::bar, written by
@@ -120,6 +122,18 @@ struct MkArgs {
     unsigned off_union, off_misc, off_tab;
 };
 
+// A compute warp's weight stream: where its next bulk copy starts.  Stage s of
+// the warp's sequence (R granules, never spanning two phases) goes to ring slot
+// s % NS (NS = mk_ns(R)); the warp's lane 0 issues it right after the warp has
+// consumed stage s - NS from that slot, so copies run NS stages ahead of
+// the computation, across tile, phase and layer boundaries (weights never
+// depend on activations), and no thread ever polls for a free slot.
+struct IssueCur {
+    int pi;          // phase of the next copy (np: stream exhausted)
+    int gi, ge;      // next granule and end of the warp's range in that phase
+    unsigned stage;  // stages issued so far
+};
+
 struct MkMisc {
     int wft[MK_NW];  // first tile (CTA-local) of each warp's range in the current phase
     int2 wr[MK_NW];  // each warp's range of tile-groups in the current phase, CTA-relative
@@ -129,6 +143,7 @@ struct MkMisc {
     int bad;
     int last;
     int seq;  // the cache's sequence length at launch (constant until the last CTA's bookkeeping)
+    IssueCur ic[MK_NW];  // each warp's weight-stream cursor (lane 0)
 };
 
 // ---- device helpers -------------------------------------------------------
@@ -226,18 +241,6 @@ QW_DEV bool mbar_test(uint64_t* bar, uint32_t parity) {
 // bulk copy (async proxy) that refills it.
 QW_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// A compute warp's weight stream: where its next bulk copy starts.  Stage s of
-// the warp's sequence (R granules, never spanning two phases) goes to ring slot
-// s % MK_NSLOT; the warp's lane 0 issues it right after the warp has consumed
-// stage s - MK_NSLOT from that slot, so copies run MK_NSLOT stages ahead of
-// the computation, across tile, phase and layer boundaries (weights never
-// depend on activations), and no thread ever polls for a free slot.
-struct IssueCur {
-    int pi;          // phase of the next copy (np: stream exhausted)
-    int gi, ge;      // next granule and end of the warp's range in that phase
-    unsigned stage;  // stages issued so far
-};
-
 // Advance to the next non-empty range of warp w, from phase c.pi on.
 QW_DEV void issue_enter(IssueCur& c, const PhaseInfo* tab, int np, int w) {
     for (; c.pi < np; ++c.pi) {
@@ -254,11 +257,12 @@ QW_DEV void issue_enter(IssueCur& c, const PhaseInfo* tab, int np, int w) {
 template <int R>
 __device__ __noinline__ void issue_next(IssueCur& c, const PhaseInfo* tab, int np, int w, unsigned char* ring, uint64_t* fullb) {
     if (c.pi >= np) return;
-    const unsigned slot = c.stage % MK_NSLOT;
+    constexpr int NS = mk_ns(R);
+    const unsigned slot = c.stage % NS;
     uint64_t* fb = fullb + w * MK_NSLOT + slot;
     const int n = min(R, c.ge - c.gi);
     mbar_arrive_expect_tx(fb, (uint32_t)(n * GR_BYTES));
-    bulk_g2s(ring + ((size_t)w * MK_NSLOT + slot) * R * GR_BYTES, tab[c.pi].w + (size_t)c.gi * GR_BYTES,
+    bulk_g2s(ring + ((size_t)w * NS + slot) * R * GR_BYTES, tab[c.pi].w + (size_t)c.gi * GR_BYTES,
              (uint32_t)(n * GR_BYTES), fb);
     c.gi += n;
     ++c.stage;
@@ -581,16 +585,17 @@ QW_DEV void store_elem(const MkArgs& a, bool lm, int row, int m, const float (&v
 // ---- optional timing stamps --------------------------------------------------
 // With a stamp buffer (MkArgs::prof, set by the QW_MK_PROFILE environment
 // variable), thread 0 of each CTA records globaltimer at points of every
-// phase: prof[(cta * MK_PROF_PHASES + phase) * 8 + k], k = 0 after the phase
+// phase: prof[(cta * MK_PROF_PHASES + phase) * MK_PROF_SLOTS + k], k = 0 after the phase
 // barrier, 1 after activation staging, 2 first weight stage ready, 3 own
 // weight loop done, 4 all warps' loops done, 5 epilogue done, 6 before
-// arriving.  Phase 5l + {0..4} = layer l's q|k|v, attention, o, gate|up, down;
+// arriving, 8 weight loop entered (warp 0), 9 weight loop left (warp 0).  Phase 5l + {0..4} = layer l's q|k|v, attention, o, gate|up, down;
 // 5L = lm_head.  Read back with qw_debug_mk_prof.
 constexpr int MK_PROF_PHASES = 4 * 64 * 2 + 2;
+constexpr int MK_PROF_SLOTS = 16;
 #define MK_STAMP(ph, k)                                                                                      \
     do {                                                                                                     \
         if (a.prof && threadIdx.x == 0 && (ph) < MK_PROF_PHASES)                                             \
-            a.prof[((size_t)blockIdx.x * MK_PROF_PHASES + (ph)) * 8 + (k)] = globaltimer();                  \
+            a.prof[((size_t)blockIdx.x * MK_PROF_PHASES + (ph)) * MK_PROF_SLOTS + (k)] = globaltimer();      \
     } while (0)
 
 template <int KIND>
@@ -632,17 +637,17 @@ struct LoopSmem {
 // end every per_tile granules): waits for its ring stages, computes four
 // granules per batch (their weights loaded together), writes one partial per
 // tile segment, and has lane 0 refill every consumed slot with the stage
-// MK_NSLOT ahead.  Granules enter their sub-tile's accumulator in phase order.
+// NS ahead.  Granules enter their sub-tile's accumulator in phase order.
 // Out of line, so the kernel's own live state never competes with the loop
 // for registers.
 template <int KIND, int R>
-__device__ __noinline__ void gemv_loop(const unsigned* abort_flag, int* err, const LoopSmem sm, int gi, const int gend,
-                                       const int per_tile, const int KG, unsigned* stage_io, IssueCur* ic,
+__device__ __noinline__ unsigned gemv_loop(const unsigned* abort_flag, int* err, const LoopSmem sm, int gi, const int gend,
+                                       const int per_tile, const int KG, unsigned stage, IssueCur* ic,
                                        const PhaseInfo* tab, int np, unsigned char* ring, uint64_t* fullb,
                                        unsigned long long* prof_slot) {
     constexpr int R16 = KIND == K_GU ? 2 : 1;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2;
-    unsigned stage = *stage_io;
+    constexpr int NS = mk_ns(R);
     int seg_end = (gi / per_tile + 1) * per_tile;
     uint32_t red = sm.red + 16 * lane;
     float acc[R16][4];
@@ -657,11 +662,12 @@ __device__ __noinline__ void gemv_loop(const unsigned* abort_flag, int* err, con
         red += R16 * 512;
     };
     bool first = true;
+    if (prof_slot && threadIdx.x == 0) prof_slot[6] = globaltimer();
     while (gi < gend) {
         const int n = min(R, gend - gi);
-        const uint32_t slot = stage % MK_NSLOT;
+        const uint32_t slot = stage % NS;
         uint64_t* bar = reinterpret_cast<uint64_t*>(fullb) + warp * MK_NSLOT + slot;
-        if (!mbar_wait_mk(bar, (stage / MK_NSLOT) & 1, abort_flag)) {
+        if (!mbar_wait_mk(bar, (stage / NS) & 1, abort_flag)) {
             if (lane == 0) {
                 atomicOr(err, QW_DERR_TIMEOUT);
                 atomicExch(const_cast<unsigned*>(abort_flag), 1u);
@@ -675,34 +681,40 @@ __device__ __noinline__ void gemv_loop(const unsigned* abort_flag, int* err, con
         int gl = (gi / R16) % KG;
         uint4 xa = lds128(sm.xs + gl * sm.col), xb = lds128(sm.xs + gl * sm.col + 16);
         float2 sx = lds64f(sm.seeds + gl * 32);
-        uint4 wv[R];
+        // the stage's granules in batches of at most 4 (weights of a batch loaded together)
+        constexpr int RB = R > 4 ? 4 : R;
+#pragma unroll 1
+        for (int jb = 0; jb < n; jb += RB) {
+            uint4 wv[RB];
 #pragma unroll
-        for (int j = 0; j < R; ++j)
-            if (j < n) wv[j] = lds128(sp + j * GR_BYTES + 16 * lane);
+            for (int j = 0; j < RB; ++j)
+                if (jb + j < n) wv[j] = lds128(sp + (jb + j) * GR_BYTES + 16 * lane);
 #pragma unroll
-        for (int j = 0; j < R; ++j) {
-            if (j < n) {
-                if (gi + j == seg_end) {
-                    flush();
-                    seg_end += per_tile;
+            for (int j = 0; j < RB; ++j) {
+                const int jj = jb + j;
+                if (jj < n) {
+                    if (gi + jj == seg_end) {
+                        flush();
+                        seg_end += per_tile;
+                    }
+                    if (jj > 0 && (R16 == 1 || (jj & 1) == 0)) {
+                        if (++gl == KG) gl = 0;
+                        xa = lds128(sm.xs + gl * sm.col);
+                        xb = lds128(sm.xs + gl * sm.col + 16);
+                        sx = lds64f(sm.seeds + gl * 32);
+                    }
+                    GAct x;
+                    x.xa = xa;
+                    x.xb = xb;
+                    x.sx = sx;
+                    float c[4];
+                    granule_mma(wv[j], x, c);
+                    const uint2 sb = lds64(sp + jj * GR_BYTES + 512 + 8 * g);
+                    granule_epi(sb, c, sx, acc[R16 == 2 ? (j & 1) : 0]);
                 }
-                if (j > 0 && (R16 == 1 || (j & 1) == 0)) {
-                    if (++gl == KG) gl = 0;
-                    xa = lds128(sm.xs + gl * sm.col);
-                    xb = lds128(sm.xs + gl * sm.col + 16);
-                    sx = lds64f(sm.seeds + gl * 32);
-                }
-                GAct x;
-                x.xa = xa;
-                x.xb = xb;
-                x.sx = sx;
-                float c[4];
-                granule_mma(wv[j], x, c);
-                const uint2 sb = lds64(sp + j * GR_BYTES + 512 + 8 * g);
-                granule_epi(sb, c, sx, acc[R16 == 2 ? (j & 1) : 0]);
             }
         }
-        // the slot is free: refill it with the stage MK_NSLOT ahead
+        // the slot is free: refill it with the stage NS ahead
         __syncwarp();
         if (lane == 0) {
             fence_proxy_async_smem();
@@ -712,7 +724,8 @@ __device__ __noinline__ void gemv_loop(const unsigned* abort_flag, int* err, con
         ++stage;
     }
     flush();
-    *stage_io = stage;
+    if (prof_slot && threadIdx.x == 0) prof_slot[7] = globaltimer();
+    return stage;
 }
 
 // One GEMV phase: each warp computes its granule range from its ring, writing
@@ -735,7 +748,7 @@ QW_DEV void gemv_phase(const MkArgs& a, const PhaseInfo& P, int Mx, uint32_t* xs
     const int col_stride = Mx * XW;
     const uint32_t* xs_lane = xs + (size_t)mcol * XW + t * 8;
     const float* seeds_lane = seeds + (size_t)t * SEEDF;
-    const unsigned char* wring = ring + (size_t)warp * MK_NSLOT * R * GR_BYTES;
+    const unsigned char* wring = ring + (size_t)warp * mk_ns(R) * R * GR_BYTES;
     uint64_t* fb = fullb + warp * MK_NSLOT;
 
     int wa, wb;
@@ -753,8 +766,8 @@ QW_DEV void gemv_phase(const MkArgs& a, const PhaseInfo& P, int Mx, uint32_t* xs
     ls.fb = smem_u32(fb);
     ls.red = smem_u32(red + (size_t)warp * seg_stride * R16 * 128);
     if (wa < wb)
-        gemv_loop<KIND, R>(a.sync + 2, a.err, ls, wa * R16, wb * R16, per_tile, KG, &stage, &ic, tab, np, ring,
-                           fullb, a.prof ? a.prof + ((size_t)blockIdx.x * MK_PROF_PHASES + prof_id) * 8 + 2 : nullptr);
+        stage = gemv_loop<KIND, R>(a.sync + 2, a.err, ls, wa * R16, wb * R16, per_tile, KG, stage, &ic, tab, np, ring,
+                           fullb, a.prof ? a.prof + ((size_t)blockIdx.x * MK_PROF_PHASES + prof_id) * MK_PROF_SLOTS + 2 : nullptr);
     MK_STAMP(prof_id, 3);
     csync();
     MK_STAMP(prof_id, 4);
@@ -829,7 +842,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const __grid_cons
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     MkMisc& mm = *reinterpret_cast<MkMisc*>(sm + a.off_misc);
     unsigned char* ring = sm;
-    uint64_t* fullb = reinterpret_cast<uint64_t*>(sm + (size_t)MK_NW * MK_NSLOT * R * GR_BYTES);
+    uint64_t* fullb = reinterpret_cast<uint64_t*>(sm + (size_t)MK_NW * mk_ns(R) * R * GR_BYTES);
     unsigned char* uni = sm + a.off_union;
     const int C = gridDim.x;
 
@@ -868,12 +881,14 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const __grid_cons
     }
     __syncthreads();  // the phase table and the stage barriers are ready
 
-    // every warp starts its weight stream: the first MK_NSLOT stages in flight
-    IssueCur ic{0, 0, 0, 0u};
+    // every warp starts its weight stream: the first NS stages in flight (the
+    // warp's issue cursor lives in shared memory: only lane 0 touches it)
+    IssueCur& ic = mm.ic[warp];
     unsigned stage = 0;  // stages consumed
     if (lane == 0) {
+        ic = IssueCur{0, 0, 0, 0u};
         issue_enter(ic, tab, np, warp);
-        for (int i = 0; i < MK_NSLOT; ++i) issue_next<R>(ic, tab, np, warp, ring, fullb);
+        for (int i = 0; i < mk_ns(R); ++i) issue_next<R>(ic, tab, np, warp, ring, fullb);
     }
 
     const int M = a.M;
@@ -953,7 +968,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const __grid_cons
                 aa.k_norm_w = k_norm;
                 aa.kcache = a.kc0 + (size_t)l * a.kv_layer_elems;
                 aa.vcache = a.vc0 + (size_t)l * a.kv_layer_elems;
-                aa.prof = a.prof ? a.prof + ((size_t)blockIdx.x * MK_PROF_PHASES + 5 * l + 1) * 8 : nullptr;
+                aa.prof = a.prof ? a.prof + ((size_t)blockIdx.x * MK_PROF_PHASES + 5 * l + 1) * MK_PROF_SLOTS : nullptr;
                 attn::SplitSmem<RMAX>& asm_ = *reinterpret_cast<attn::SplitSmem<RMAX>*>(uni);
                 for (int it = blockIdx.x; it < a.aa.Hkv * nsp; it += C) {
                     attn::split_body<RMAX, MK_NT>(aa, asm_, it / nsp, it % nsp, nsp, mm.seq, tid, CSync{},
@@ -1054,7 +1069,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const __grid_cons
     if (lane == 0) {
         for (unsigned s2 = stage; s2 < ic.stage; ++s2) {
             const unsigned long long t0 = globaltimer();
-            while (!mbar_test(&fullb[warp * MK_NSLOT + s2 % MK_NSLOT], (s2 / MK_NSLOT) & 1))
+            while (!mbar_test(&fullb[warp * MK_NSLOT + s2 % mk_ns(R)], (s2 / mk_ns(R)) & 1))
                 if (globaltimer() - t0 > 2 * MK_TIMEOUT_NS) break;
         }
     }
@@ -1293,7 +1308,7 @@ void mk_prepare(qw_model* m) {
     QW_CUDA(cudaMemsetAsync(s->sync, 0, 4 * sizeof(unsigned), m->stream));
     QW_CUDA(cudaMalloc(&s->amax_cta, (size_t)C * 8 * sizeof(unsigned long long)));
     if (std::getenv("QW_MK_PROFILE")) {
-        const size_t pb = (size_t)C * MK_PROF_PHASES * 8 * sizeof(unsigned long long);
+        const size_t pb = (size_t)C * MK_PROF_PHASES * MK_PROF_SLOTS * sizeof(unsigned long long);
         QW_CUDA(cudaMalloc(&s->prof, pb));
         QW_CUDA(cudaMemsetAsync(s->prof, 0, pb, m->stream));
     }
@@ -1334,8 +1349,8 @@ void mk_launch_d(qw_model* m, MkArgs& a, cudaStream_t st, size_t smem, int max_s
     QW_CUDA(cudaLaunchKernelEx(&cfg, decode_step_kernel<RMAX, R>, a));
 }
 
-// Ring stages of 4 granules per copy (four per warp) when shared memory
-// allows, else 2.
+// Ring of 16 granules per warp in stages of 4 (or 8), or 8 granules in stages
+// of 2, as the phases' sizes and shared memory allow.
 template <int RMAX>
 bool mk_launch_t(qw_model* m, MkArgs& a, cudaStream_t st) {
     MkState* s = m->mk;
@@ -1347,17 +1362,32 @@ bool mk_launch_t(qw_model* m, MkArgs& a, cudaStream_t st) {
     const size_t misc = misc_struct + (((size_t)np * sizeof(PhaseInfo) + 127) & ~(size_t)127);
     const size_t bars = MK_NW * MK_NSLOT * sizeof(uint64_t);  // stage barriers (512 B)
     const long long room = (long long)max_smem - (long long)uni - (long long)misc - (long long)bars;
-    const long long per_r = (long long)MK_NW * MK_NSLOT * GR_BYTES;
-    int r = room >= 4 * per_r ? 4 : (room >= 2 * per_r ? 2 : 0);
-    // QW_MK_STAGE=2 caps the stage size (profiling / testing both kernel forms)
-    if (const char* e = std::getenv("QW_MK_STAGE"))
-        if (std::atoi(e) == 2 && r == 4) r = 2;
+    // ring bytes for stages of r granules
+    auto ring_bytes = [](int r) { return (long long)MK_NW * mk_ns(r) * r * GR_BYTES; };
+    // Stage size: the loops stream faster with larger stages, but the weight
+    // loop's register footprint then leaves the kernel body fewer registers
+    // across the call (its spills cost a round trip per phase).  Measured on
+    // Qwen3-4B / 0.6B: stages of 4 where a warp's share of a layer phase
+    // averages 4 granules or more, else 2.  QW_MK_STAGE = 2 / 4 / 8 forces a
+    // form (profiling, testing every kernel form).
+    const MkLayer& L0 = s->layers[0];
+    long long gran = 0;
+    for (int k = 0; k < 4; ++k) gran += (long long)L0.lin[k].n_tiles * L0.lin[k].KG * L0.lin[k].R16;
+    const double per_warp = (double)gran / 4.0 / ((double)s->C * MK_NW);
+    int r = per_warp >= 4.0 ? 4 : 2;
+    if (const char* e = std::getenv("QW_MK_STAGE")) {
+        const int want = std::atoi(e);
+        if (want == 2 || want == 4 || want == 8) r = want;
+    }
+    if (room < ring_bytes(r)) r = room >= ring_bytes(2) ? 2 : 0;
     if (r == 0) return false;
-    a.off_union = (unsigned)((size_t)MK_NW * MK_NSLOT * r * GR_BYTES + bars);  // a multiple of 128
+    a.off_union = (unsigned)(ring_bytes(r) + bars);  // a multiple of 128
     a.off_misc = a.off_union + (unsigned)uni;
     a.off_tab = a.off_misc + (unsigned)misc_struct;
     const size_t smem = a.off_misc + misc;
-    if (r == 4)
+    if (r == 8)
+        mk_launch_d<RMAX, 8>(m, a, st, smem, max_smem);
+    else if (r == 4)
         mk_launch_d<RMAX, 4>(m, a, st, smem, max_smem);
     else
         mk_launch_d<RMAX, 2>(m, a, st, smem, max_smem);
@@ -1369,7 +1399,7 @@ bool mk_launch_t(qw_model* m, MkArgs& a, cudaStream_t st) {
 size_t mk_prof_read(const qw_model* m, void* dst, size_t bytes) {
     const MkState* s = m->mk;
     if (!s || !s->prof) return 0;
-    const size_t pb = (size_t)s->C * MK_PROF_PHASES * 8 * sizeof(unsigned long long);
+    const size_t pb = (size_t)s->C * MK_PROF_PHASES * MK_PROF_SLOTS * sizeof(unsigned long long);
     if (bytes < pb) return 0;
     QW_CUDA(cudaMemcpy(dst, s->prof, pb, cudaMemcpyDeviceToHost));
     return pb;

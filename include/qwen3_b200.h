@@ -164,11 +164,12 @@ QW_API int qw_forward_trace(qw_model* m, qw_cache* c, const uint32_t* ids_host, 
 /* Diagnostics: timing stamps of the last persistent decode-step launch, when
  * the model was created with the environment variable QW_MK_PROFILE set
  * (otherwise *written = 0).  Layout: uint64 globaltimer ns
- * [cta][phase][8], 514 phases per CTA (phase 5l + {0..4} = layer l's q|k|v,
+ * [cta][phase][16], 514 phases per CTA (phase 5l + {0..4} = layer l's q|k|v,
  * attention, o_proj, gate|up, down_proj; 5L = lm_head; slot k = 0 phase
  * barrier passed, 1 staging done, 2 first weight stage ready, 3 own weight
- * loop done, 4 all warps done, 5 epilogue done, 6 arriving).  No reference
- * counterpart. */
+ * loop done, 4 all warps done, 5 epilogue done, 6 arriving, 8 / 9 weight loop
+ * entered / left by warp 0; attention items use slots 1-7 for their steps).
+ * No reference counterpart. */
 QW_API int qw_debug_decode_stamps(const qw_model* m, void* dst_host, size_t bytes, size_t* written);
 
 /* ---- generation --------------------------------------------------------- */
