@@ -12,19 +12,28 @@ N(0,0.02) quantized to MLX affine 4-bit g64) generated on the device.
             device; prefill excluded), summed over the K timed steps and all ranks.
 * e2e    -- the same metric through the C ABI with host buffers, timed on the
             host exactly like main.rs: wall(generate 300) - wall(generate 1).
-* roofline -- the dominant kernel (qgemv, the quantized GEMV: ~3/4 of a decode
-            step in the ncu launch list) timed with CUDA events over the 4B
-            decode shapes on rotating weight copies (> L2), bytes = N*K*0.5625
-            + activations, against the measured HBM copy bandwidth.
+* roofline -- the dominant kernel, decode_step_kernel (the persistent decode
+            step: every layer + lm_head in one launch, one launch per token):
+            algorithmic bytes per launch (quantized weights + K/V at the mean
+            KV length) over its mean duration from the library's CUDA events,
+            against the measured HBM copy bandwidth.
 * cpu_baseline -- the oracle's CPU restatement of the same path (C qmatmul +
-            numpy), rank 0 at N=1 only, on a bounded sample (see `sample`).
+            numpy), rank 0 at N=1 only, on a bounded sample of the workload:
+            greedy decode steps at the start and at the end of the 512..811
+            KV range (caches pre-filled with seeded K/V; see `sample`).
+* extras  -- config2_qmatmul (the standalone quantized matmul at M = 1, 5,
+            128, 2048), spec (config 4 at forced acceptance p = 0, 0.5, 0.8,
+            1), config1 (Qwen3-0.6B 128 + 128), sampled_decode; at N > 1
+            tp_decode (config 5: Qwen3-32B split over all N ranks).
 
---impl reference times that CPU restatement alone (the reference itself is
-Rust over MLX/Metal and cannot be built or run on this machine).
+--impl reference times that CPU restatement alone on the same configuration
+(the reference itself is Rust over MLX/Metal and cannot be built or run on
+this machine; `mlx_probe` records the import attempt).
 
 Multi-GPU: Qwen3-4B fits one GPU, so N GPUs run N independent replicas
 (weak scaling, no collective on the data path); value is the sum over ranks
-divided by the slowest rank's time.
+divided by the slowest rank's time.  The tensor-parallel path is measured in
+the same run as tp_decode.
 """
 from __future__ import annotations
 
@@ -148,30 +157,56 @@ def prompt_ids(vocab: int) -> np.ndarray:
 # ----------------------------------------------------------------- CPU leg ---
 
 class CpuModel:
-    """The oracle's CPU restatement of Qwen3-4B (C qmatmul + numpy) on seeded weights."""
+    """The oracle's CPU restatement (C qmatmul + numpy) of one benchmark model on
+    seeded weights, decoding at the benchmark's KV positions: the cache is filled
+    with seeded bf16 K/V rows up to the sample's first position (standing in for
+    the prefill, which the decode metric excludes), then greedy decode steps are
+    timed."""
 
-    def __init__(self):
+    def __init__(self, cfg=None, prompt_len=PROMPT_LEN, decode_tokens=DECODE_TOKENS):
         from oracle import synth
         from oracle.qwen3_ref import Qwen3Ref
-        cfg = dict(synth.QWEN3_4B)
+        self.cfg = dict(cfg or synth.QWEN3_4B)
+        self.prompt_len, self.decode_tokens = prompt_len, decode_tokens
         t0 = time.time()
-        self.ref = Qwen3Ref(cfg, synth.build_tensors(cfg, SEED, "ones", fast=True), backend="c")
+        self.ref = Qwen3Ref(self.cfg, synth.build_tensors(self.cfg, SEED, "ones", fast=True), backend="c")
         self.build_s = time.time() - t0
-        self.prompt = prompt_ids(cfg["vocab_size"])[:4].tolist()
+        self.start_tok = int(prompt_ids(self.cfg["vocab_size"])[0])
 
-    def sample(self, decode_tokens: int):
-        """4-token prefill (untimed), then `decode_tokens` timed greedy steps; tok/s."""
-        cache = self.ref.new_cache(64)
-        tok = int(np.argmax(self.ref.forward(self.prompt, cache)))
-        t0 = time.time()
-        for _ in range(decode_tokens):
-            tok = int(np.argmax(self.ref.forward([tok], cache)))
-        return decode_tokens / (time.time() - t0)
+    def _cache_at(self, pos: int, room: int):
+        from oracle import numerics as nm
+        c = self.ref.new_cache(pos + room)
+        rng = np.random.default_rng(SEED + pos)
+        for li in range(self.cfg["num_hidden_layers"]):
+            for arr in (c.k[li], c.v[li]):
+                arr[:, :pos, :] = nm.bf16_round(rng.standard_normal(arr[:, :pos, :].shape, dtype=np.float32))
+        c.seq_len = pos
+        return c
 
-    def describe(self, decode_tokens: int) -> str:
-        return (f"oracle CPU restatement (C qmatmul + numpy), Qwen3-4B seeded weights, 4-token prefill then "
-                f"{decode_tokens} timed greedy decode steps at KV length 5-{4 + decode_tokens} (the GPU workload "
-                f"decodes at 512-812; attention is <5% of a 4B decode step's work); weight build "
+    def windows(self, n: int):
+        """First KV positions of the two timed windows: the start and the end of the
+        workload's decode range [prompt_len, prompt_len + decode_tokens)."""
+        return (self.prompt_len, self.prompt_len + self.decode_tokens - n)
+
+    def sample(self, n: int) -> float:
+        """n greedy decode steps in each window (caches filled untimed); tok/s."""
+        secs, toks = 0.0, 0
+        for p0 in self.windows(n):
+            cache = self._cache_at(p0, n + 1)
+            tok = self.start_tok
+            t0 = time.time()
+            for _ in range(n):
+                tok = int(np.argmax(self.ref.forward([tok], cache)))
+            secs += time.time() - t0
+            toks += n
+        return toks / secs
+
+    def describe(self, n: int) -> str:
+        w = self.windows(n)
+        return (f"oracle CPU restatement (C qmatmul, all host threads, + numpy) of {self.cfg['hidden_size']}-hidden "
+                f"Qwen3 on seeded weights: {n} timed greedy decode steps at KV positions {w[0]}-{w[0] + n - 1} and "
+                f"{w[1]}-{w[1] + n - 1} (the start and end of the workload's {self.prompt_len}+{self.decode_tokens} "
+                f"decode range; caches pre-filled with seeded bf16 K/V, untimed); weight build "
                 f"{self.build_s:.1f}s not timed")
 
 
@@ -180,10 +215,28 @@ def cpu_sample(decode_tokens: int, threads: int):
     return cm.sample(decode_tokens), threads, cm.describe(decode_tokens)
 
 
+def mlx_probe() -> str:
+    """Whether the reference's runtime (MLX) imports on this host."""
+    r = subprocess.run([sys.executable, "-c", "import mlx.core"], capture_output=True, text=True)
+    return "import mlx.core: ok" if r.returncode == 0 else \
+        "import mlx.core: " + (r.stderr.strip().splitlines() or ["failed"])[-1]
+
+
+def workload_config(world: int) -> dict:
+    """The benchmark configuration both arms report."""
+    return {"workload": "config3: Qwen3-4B 4-bit g64, batch 1, 512-token prompt, greedy decode 300, "
+                        "KV pre-allocated 4096 (bf16)",
+            "model": "Qwen3-4B (random init)", "prompt_len": PROMPT_LEN,
+            "decode_tokens": DECODE_TOKENS, "kv_prealloc": KV_PREALLOC,
+            "parallelism": f"replicas x{world}",
+            "l2": "no flush: every decode step streams 2.26 GB of weights (> 126 MB L2)"}
+
+
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
+    from oracle import synth
     threads = os.cpu_count() or 1
     cm = CpuModel()
     per_step = []
@@ -193,47 +246,55 @@ def run_reference(args):
             per_step.append(v)
     desc = cm.describe(args.ref_tokens)
     value = float(np.mean(per_step))
+    # config 1 (Qwen3-0.6B, 128-token prompt, greedy decode 128) on the same CPU path
+    c1 = CpuModel(synth.QWEN3_0_6B, 128, 128)
+    c1.sample(2)
+    c1_val = c1.sample(args.ref_tokens)
     line = {"metric": METRIC, "impl": "reference", "value": round(value, 4), "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": round(value / REF_TOK_S, 4), "dtype": "u4xbf16->f32", "data": "synthetic",
-            "config": {"workload": "config3: Qwen3-4B 4-bit g64, batch 1, greedy decode", "model": "Qwen3-4B",
-                       "prompt_len": PROMPT_LEN, "decode_tokens": DECODE_TOKENS},
+            "config": workload_config(world),
             "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": threads, "kind": "port",
                              "sample": desc},
             "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "config1_cpu": {"tok_s": round(c1_val, 4), "sample": c1.describe(args.ref_tokens)},
+            "mlx_probe": mlx_probe(),
             "note": "flakerimi/base-mlx is Rust over mlx-rs/MLX Metal: no Rust toolchain, no MLX and no Metal here, "
-                    "so the timed reference is the repository's CPU restatement of the same path (oracle/)"}
+                    "so the timed reference is the repository's CPU restatement of the same path (oracle/); each "
+                    "step is a bounded sample of the configured workload (cpu_baseline.sample)"}
     print(json.dumps(line), flush=True)
 
 
 # ----------------------------------------------------------------- GPU leg ---
 
-def qgemv_roofline(q, torch, info, peak_gbs):
-    """Time the decode GEMV kernel over one layer's 4B shapes + lm_head on
-    rotating weight copies (> L2) in a CUDA graph; return achieved GB/s."""
+def qgemv_roofline(q, torch, info, peak_gbs, M=1, with_flops=False):
+    """Time the standalone quantized matmul at M rows (the decode GEMV kernel for
+    M <= 8) over one layer's 4B shapes + lm_head on rotating weight copies (> L2)
+    in a CUDA graph; return achieved GB/s (weights + activations in + outputs)."""
     lib = q.lib()
     dev = torch.device("cuda")
     H, I, V = info.hidden, info.intermediate, info.vocab
     QD, KD = info.num_heads * info.head_dim, info.num_kv_heads * info.head_dim
     shapes = [(H, QD + 2 * KD), (QD, H), (H, 2 * I), (I, H), (H, V)]
-    total_bytes, launches = 0.0, []
+    total_bytes, total_flops, launches = 0.0, 0.0, []
     bufs = []
     for K, N in shapes:
         nrep = max(2, int(300e6 // (N * K * 0.5625)) + 1)
         w = torch.randint(-2 ** 31, 2 ** 31 - 1, (nrep, N, K // 8), dtype=torch.int32, device=dev)
         s = (torch.rand(nrep, N, K // 64, device=dev) * 0.01).to(torch.bfloat16)
         b = (torch.rand(nrep, N, K // 64, device=dev) * -0.01).to(torch.bfloat16)
-        x = torch.randn(1, K, device=dev).to(torch.bfloat16)
-        y = torch.empty(1, N, device=dev, dtype=torch.bfloat16)
+        x = torch.randn(M, K, device=dev).to(torch.bfloat16)
+        y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
         bufs.append((w, s, b, x, y))
         for i in range(nrep):
             launches.append((x.data_ptr(), w[i].data_ptr(), s[i].data_ptr(), b[i].data_ptr(), y.data_ptr(), N, K))
-        total_bytes += nrep * (N * K * 0.5625 + 2 * K + 2 * N)
+        total_bytes += nrep * (N * K * 0.5625 + M * (2 * K + 2 * N))
+        total_flops += nrep * 2.0 * M * N * K
     st = torch.cuda.Stream()
     with torch.cuda.stream(st):
         def run_all():
             for (xp, wp, sp, bp, yp, N, K) in launches:
-                q.check(lib.qw_quantized_matmul(xp, wp, sp, bp, yp, 1, N, K, 64, 4, st.cuda_stream))
+                q.check(lib.qw_quantized_matmul(xp, wp, sp, bp, yp, M, N, K, 64, 4, st.cuda_stream))
         run_all()
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
@@ -252,6 +313,8 @@ def qgemv_roofline(q, torch, info, peak_gbs):
     achieved = total_bytes / sec / 1e9
     del bufs, g
     torch.cuda.empty_cache()
+    if with_flops:
+        return achieved, len(launches), total_bytes / len(launches), total_flops / sec / 1e12
     return achieved, len(launches), total_bytes / len(launches)
 
 
@@ -407,27 +470,43 @@ def run_ours(args):
                                    "frac": round(ach / peak, 4),
                                    "kernel": "qw_quantized_matmul (standalone op, M=1), 4B layer shapes + lm_head",
                                    "bytes_per_launch": int(per_launch), "launches_timed": nl}
+        # config 2: the standalone op at the benchmark's row counts, rotating weight copies (> L2)
+        c2 = {"M=1": {"GB/s": round(ach, 1), "frac_hbm": round(ach / peak, 4)}}
+        for Mr in (5, 128):
+            a2, _, _, tf2 = qgemv_roofline(q, torch, info, peak, M=Mr, with_flops=True)
+            c2[f"M={Mr}"] = {"GB/s": round(a2, 1), "frac_hbm": round(a2 / peak, 4), "TFLOP/s": round(tf2, 2),
+                             "frac_tensor": round(tf2 / tensor_peak()[0], 4)}
+        c2["M=2048"] = {"TFLOP/s": round(tf, 1), "frac_tensor": round(tf / tpk, 4)}
+        extra["config2_qmatmul"] = {"shapes": "Qwen3-4B q|k|v, o_proj, gate|up, down_proj, lm_head (K, N)",
+                                    "rows": c2, "peak_gbs": peak, "peak_tflops": tpk}
         if world == 1 and not args.no_cpu:
             v, cores, desc = cpu_sample(args.cpu_tokens, os.cpu_count() or 1)
             cpu = {"value": round(v, 4), "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
+    if rank == 0 and world == 1:
+        # single-GPU extras (at N > 1 the other GPUs would idle meanwhile)
         if args.spec:
             extra["spec"] = spec_measure(q, m, prompt, cfg)
+        extra["config1"] = config1_measure(q)
         # sampled decode (temperature 0.7, top-p 0.95: the reference's SamplingParams defaults):
         # the device pick after every step on the same model and prompt
         rs = m.generate_sampled(prompt, DECODE_TOKENS, temperature=0.7, top_p=0.95, seed=SEED, eos=[1 << 30])
         extra["sampled_decode"] = {"tok_s": round((rs.completion_tokens - 1) / (rs.decode_ms / 1e3), 2),
                                    "temperature": 0.7, "top_p": 0.95, "tokens": rs.completion_tokens}
+    m.close()
+    if world > 1 and not args.no_tp:
+        # config 5 at tp = N on the same ranks: one Qwen3-32B sequence split over all GPUs
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        tp_line = tp_decode_core(2, 3, dist, rank, world, local)
+        if rank == 0:
+            extra["tp_decode"] = {k: tp_line[k] for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup",
+                                                          "scaling", "config", "roofline", "decode_ms_per_token",
+                                                          "ttft_ms", "ranks_agree_on_tokens")}
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(region_max * 1e3 / args.steps, 3),
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": round(value / REF_TOK_S, 3),
                 "dtype": "u4xbf16->f32", "data": "synthetic (seeded random-init weights and prompt ids)",
-                "config": {"workload": "config3: Qwen3-4B 4-bit g64, batch 1, 512-token prompt, greedy decode 300, "
-                                       "KV pre-allocated 4096 (bf16)",
-                           "model": "Qwen3-4B (random init)", "prompt_len": PROMPT_LEN,
-                           "decode_tokens": DECODE_TOKENS, "kv_prealloc": KV_PREALLOC,
-                           "parallelism": f"replicas x{world}",
-                           "l2": "no flush: every decode step streams 2.26 GB of weights (> 126 MB L2)"},
+                "config": workload_config(world),
                 "roofline": roof, "cpu_baseline": cpu,
                 "e2e": {"value": round(e2e_value, 2), "unit": "tok/s",
                         "h2d_bytes_per_step": PROMPT_LEN * 4, "d2h_bytes_per_step": DECODE_TOKENS * 4 + 40},
@@ -438,18 +517,17 @@ def run_ours(args):
                 "gen_tok_s_incl_prefill": round(gen_tokens_all / (region_max), 2)}
         line.update(extra)
         print(json.dumps(line), flush=True)
-    m.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
 
 
 def spec_measure(q, target, prompt, cfg4):
-    """Config 4: 4B target + 0.6B draft, k=4, forced acceptance p in {0.8, 1.0}."""
+    """Config 4: 4B target + 0.6B draft, k=4, forced acceptance p in {0, 0.5, 0.8, 1}."""
     draft = q.Qwen3.init_random(dict(CFG_0_6B), SEED + 1, norm_mode="ones", device=0)
     plain = target.generate_greedy(prompt, DECODE_TOKENS)
     out = {"k": 4, "plain_decode_tok_s": round((plain.completion_tokens - 1) / (plain.decode_ms / 1e3), 2)}
-    for p in (0.8, 1.0):
+    for p in (0.0, 0.5, 0.8, 1.0):
         q.speculative_generate(target, draft, prompt, DECODE_TOKENS, k=4, force_p=p, seed=7, forced=plain.tokens)
         res, st = q.speculative_generate(target, draft, prompt, DECODE_TOKENS, k=4, force_p=p, seed=7,
                                          forced=plain.tokens)
@@ -462,6 +540,22 @@ def spec_measure(q, target, prompt, cfg4):
         out[f"p{p}"]["speedup_vs_plain"] = round(out[f"p{p}"]["tok_s"] / out["plain_decode_tok_s"], 3)
     draft.close()
     return out
+
+
+def config1_measure(q):
+    """Config 1: Qwen3-0.6B, 128-token prompt, greedy decode of 128 (decode tok/s
+    as main.rs defines it, CUDA events inside the library)."""
+    m = q.Qwen3.init_random(dict(CFG_0_6B), SEED, norm_mode="ones", device=0)
+    prompt = prompt_ids(CFG_0_6B["vocab_size"])[:128]
+    for _ in range(3):
+        m.generate_greedy(prompt, 128, eos=[1 << 30])
+    rs = [m.generate_greedy(prompt, 128, eos=[1 << 30]) for _ in range(5)]
+    dec = sum(r.decode_ms for r in rs) / 1e3
+    n = sum(r.completion_tokens - 1 for r in rs)
+    m.close()
+    return {"workload": "config1: Qwen3-0.6B 4-bit g64, batch 1, 128-token prompt, greedy decode 128",
+            "decode_tok_s": round(n / dec, 2), "decode_ms_per_token": round(dec * 1e3 / n, 4),
+            "ttft_ms": round(sum(r.prefill_ms for r in rs) / len(rs), 3), "runs": len(rs)}
 
 
 def profile_qmm(spec: str) -> None:
@@ -531,7 +625,6 @@ def run_tp_decode(args):
     bandwidth, sets their cost."""
     import datetime
     import torch
-    import qwen3_b200 as q
     rank, world, local = dist_env()
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     os.environ.setdefault("NCCL_SOCKET_IFNAME", "lo")
@@ -541,6 +634,19 @@ def run_tp_decode(args):
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
     torch.cuda.set_device(local)
+    line = tp_decode_core(args.steps, args.warmup, dist, rank, world, local)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def tp_decode_core(steps, warmup, dist, rank, world, local):
+    """The config-5 measurement over an initialised process group (or none at
+    world 1); returns the JSON line's dict on rank 0, None elsewhere."""
+    import torch
+    import qwen3_b200 as q
     cfg = dict(CFG_32B)
     m = q.Qwen3.init_random(cfg, SEED, norm_mode="ones", device=local, tp_rank=rank, tp_size=world)
     if world > 1:
@@ -552,14 +658,14 @@ def run_tp_decode(args):
         if dist is not None:
             dist.barrier()
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         m.generate_greedy(prompt, TP_DECODE_TOKENS)
     barrier()
     results = []
     with ClockSampler(local) as clk:
         barrier()
         t0 = time.perf_counter()
-        for _ in range(args.steps):
+        for _ in range(steps):
             results.append(m.generate_greedy(prompt, TP_DECODE_TOKENS))
         barrier()
         region = time.perf_counter() - t0
@@ -567,15 +673,18 @@ def run_tp_decode(args):
     prefill_ms = sum(r.prefill_ms for r in results)
     dec_tokens = sum(max(r.completion_tokens - 1, 0) for r in results)
     toks = results[-1].tokens
-    vals = torch.tensor([decode_ms, prefill_ms, region], dtype=torch.float64)
+    nccl_group = dist is not None and dist.get_backend() == "nccl"
+    vals = torch.tensor([decode_ms, prefill_ms, region], dtype=torch.float64,
+                        device="cuda" if nccl_group else "cpu")
     agree = True
     if dist is not None:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
         got = [None] * world
         dist.all_gather_object(got, toks)
         agree = all(g == toks for g in got)
-    decode_ms_max, prefill_ms_max, region_max = (float(v) for v in vals)
+    decode_ms_max, prefill_ms_max, region_max = (float(v) for v in vals.cpu())
     value = dec_tokens / (decode_ms_max / 1e3)
+    line = None
     if rank == 0:
         info = m.info
         H, I, V, L = info.hidden, info.intermediate, info.vocab, info.num_layers
@@ -587,8 +696,8 @@ def run_tp_decode(args):
         gbs = per_rank / tok_s / 1e9
         peak, peak_kind = peaks()
         line = {"metric": "Qwen3-32B 4-bit batch-1 tensor-parallel greedy decode tok/s", "value": round(value, 2),
-                "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": round(region_max * 1e3 / args.steps, 3), "higher_is_better": True,
+                "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warmup,
+                "ms_per_step": round(region_max * 1e3 / steps, 3), "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "u4xbf16->f32",
                 "data": "synthetic (seeded random-init weights and prompt ids)",
                 "config": {"workload": f"config5: Qwen3-32B 4-bit g64 (untied lm_head), batch 1, "
@@ -603,11 +712,9 @@ def run_tp_decode(args):
                 "decode_ms_per_token": round(decode_ms_max / max(dec_tokens, 1), 4),
                 "ttft_ms": round(prefill_ms_max / len(results), 3),
                 "ranks_agree_on_tokens": agree, "clocks": clk.summary()}
-        print(json.dumps(line), flush=True)
     m.close()
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+    barrier()
+    return line
 
 
 def main():
@@ -628,6 +735,7 @@ def main():
                     help="profiling workload for ncu: a sampled generation of N tokens; prints no bench line")
     ap.add_argument("--profile-qmm", default="", metavar="M,K,N",
                     help="profiling workload for ncu: three quantized matmuls of one shape; prints no bench line")
+    ap.add_argument("--no-tp", action="store_true", help="at N > 1, skip the tp_decode (config 5) measurement")
     ap.add_argument("--tp-decode", action="store_true",
                     help="Qwen3-32B tensor-parallel decode (config 5) over the torchrun ranks; one JSON line")
     args = ap.parse_args()
