@@ -379,6 +379,86 @@ int qw_generate_greedy(qw_model* m, const uint32_t* prompt, int n_prompt, int ma
     });
 }
 
+int qw_forward_batch(qw_model* m, qw_cache* const* caches, int nseq, const uint32_t* ids, uint16_t* logits_out,
+                     uint32_t* argmax_out) {
+    return guard([&] {
+        need(m && caches && ids, "model/caches/ids");
+        need(nseq >= 1 && nseq <= 8, "nseq must be 1..8");
+        need(m->tp_size == 1, "batched decode runs on one GPU (tp_size 1)");
+        for (int b = 0; b < nseq; ++b) {
+            need(caches[b] != nullptr, "null cache");
+            need(caches[b]->m == m, "cache belongs to another model");
+            for (int b2 = 0; b2 < b; ++b2) need(caches[b2] != caches[b], "a cache appears twice in the batch");
+            if (caches[b]->seq_len + 1 > caches[b]->max_pos)
+                throw qw::Error(QW_ERR_KV_EXHAUSTED, "KV cache exhausted: requested " +
+                                                         std::to_string(caches[b]->seq_len + 1) + " positions, max " +
+                                                         std::to_string(caches[b]->max_pos));
+        }
+        check_ids(m, ids, nseq);
+        QW_CUDA(cudaSetDevice(m->device));
+        qw::ensure_workspace(m, nseq, nseq);
+        std::vector<int> h(ids, ids + nseq);
+        cudaStream_t st = m->stream;
+        QW_CUDA(cudaMemcpyAsync(m->ws.ids, h.data(), (size_t)nseq * 4, cudaMemcpyHostToDevice, st));
+        // sub-batches of at most mk_batch_rows sequences, sizes balanced
+        const int cap = qw::mk_batch_rows(m);
+        if (cap < 1) throw qw::Error(QW_ERR_UNSUPPORTED, "this model does not fit the batched decode step");
+        const int nch = (nseq + cap - 1) / cap;
+        std::vector<int> am(nseq);
+        for (int ci = 0, b0 = 0; ci < nch; ++ci) {
+            const int nc = nseq / nch + (ci < nseq % nch ? 1 : 0);
+            qw::MkBatch mb{caches + b0, nc, nullptr, b0, nseq, ci == nch - 1};
+            if (!qw::mk_forward(m, caches[b0], m->ws.ids + b0, nc, 2, logits_out != nullptr, m->ws.argmax, st,
+                                nullptr, nullptr, nullptr, nullptr, &mb))
+                throw qw::Error(QW_ERR_UNSUPPORTED, "this model / batch does not fit the batched decode step");
+            if (logits_out)
+                QW_CUDA(cudaMemcpyAsync(logits_out + (size_t)b0 * m->vocab_l, m->ws.logits,
+                                        (size_t)nc * m->vocab_l * 2, cudaMemcpyDeviceToHost, st));
+            QW_CUDA(cudaMemcpyAsync(am.data() + b0, m->ws.argmax, (size_t)nc * 4, cudaMemcpyDeviceToHost, st));
+            b0 += nc;
+        }
+        QW_CUDA(cudaStreamSynchronize(st));
+        for (int b = 0; b < nseq; ++b) caches[b]->seq_len += 1;
+        qw::check_device_err(m);
+        if (argmax_out)
+            for (int b = 0; b < nseq; ++b) argmax_out[b] = (uint32_t)am[b];
+    });
+}
+
+int qw_generate_greedy_batch(qw_model* m, qw_cache* const* caches, int nseq, const uint32_t* prompts,
+                             const int* n_prompt, int max_new, const uint32_t* eos, int n_eos, uint32_t* out,
+                             int* n_out, qw_gen_stats* stats) {
+    return guard([&] {
+        need(m && caches && prompts && n_prompt && out && n_out, "model/caches/prompts/out");
+        need(nseq >= 1 && nseq <= 8, "nseq must be 1..8");
+        need(m->tp_size == 1, "batched decode runs on one GPU (tp_size 1)");
+        const int mn = std::max(max_new, 1);
+        std::vector<std::vector<int>> pr(nseq);
+        size_t off = 0;
+        int longest = 0;
+        for (int b = 0; b < nseq; ++b) {
+            need(caches[b] != nullptr && caches[b]->m == m, "cache missing or of another model");
+            need(n_prompt[b] >= 1, "empty prompt");
+            check_ids(m, prompts + off, n_prompt[b]);
+            pr[b].assign(prompts + off, prompts + off + n_prompt[b]);
+            off += (size_t)n_prompt[b];
+            longest = std::max(longest, n_prompt[b]);
+        }
+        QW_CUDA(cudaSetDevice(m->device));
+        qw::ensure_workspace(m, longest, 8);
+        std::vector<std::vector<int>> outs;
+        qw_gen_stats s;
+        std::memset(&s, 0, sizeof(s));
+        qw::generate_greedy_batch_dev(m, caches, nseq, pr, mn, eos_list(m, eos, n_eos), outs, &s, m->stream);
+        for (int b = 0; b < nseq; ++b) {
+            n_out[b] = (int)outs[b].size();
+            for (size_t i = 0; i < outs[b].size(); ++i) out[(size_t)b * mn + i] = (uint32_t)outs[b][i];
+        }
+        if (stats) *stats = s;
+        qw::check_device_err(m);
+    });
+}
+
 int qw_generate_sampled(qw_model* m, const uint32_t* prompt, int n_prompt, int max_new, float temperature,
                         float top_p, uint64_t seed, int same_draw, const uint32_t* eos, int n_eos, uint32_t* out,
                         int* n_out, qw_gen_stats* stats) {

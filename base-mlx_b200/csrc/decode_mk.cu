@@ -88,6 +88,14 @@ struct MkLayer {
     const bf16 *in_norm, *post_norm, *q_norm, *k_norm;
 };
 
+// One sequence of a batched step: its cache and sequence length.
+struct MkSeq {
+    bf16 *kc0, *vc0;        // layer 0's K / V cache
+    int* seq_len;           // device sequence length
+    int max_pos;
+    size_t kv_layer_elems;  // elements per layer of one cache
+};
+
 struct MkArgs {
     const MkLayer* layers;
     int L;
@@ -119,6 +127,16 @@ struct MkArgs {
     bf16* trace_mid;   // diagnostics: residual after each attention block, [L][M][H]
     bf16* trace_attn;  // diagnostics: attention output of each layer, [L][M][QD]
     unsigned long long* prof;  // diagnostics: phase timing stamps (see MK_STAMP), or null
+    // batched step (nseq > 0): row m is the one new token of sequence m, which
+    // attends to its own cache at its own position; otherwise the M rows are
+    // consecutive positions of one sequence (kc0 / vc0 / seq_len above)
+    int nseq;
+    MkSeq seqs[8];
+    size_t part_seq_stride;  // attention partial floats per sequence
+    BatchCtl* bctl;
+    int b0;          // the launch's first sequence within the whole batch (bookkeeping index)
+    int btotal;      // sequences in the whole batch
+    int bfinalize;   // this launch completes the step (step count, done flag)
     unsigned off_union, off_misc, off_tab;
 };
 
@@ -144,6 +162,8 @@ struct MkMisc {
     int last;
     int seq;  // the cache's sequence length at launch (constant until the last CTA's bookkeeping)
     IssueCur ic[MK_NW];  // each warp's weight-stream cursor (lane 0)
+    int seqb[8];   // batched step: each sequence's length at launch
+    int ibase[9];  // batched step: first attention item of each sequence; ibase[nseq] = items
 };
 
 // ---- device helpers -------------------------------------------------------
@@ -524,14 +544,6 @@ struct GAct {
     uint4 xa, xb;  // (step 0, step 1) and (step 2, step 3) B fragment pairs
     float2 sx;
 };
-QW_DEV GAct load_act(const uint32_t* xs_lane, const float* seeds_lane, int gl, int col_stride) {
-    GAct r;
-    const uint32_t* xp = xs_lane + (size_t)gl * col_stride;
-    r.xa = *reinterpret_cast<const uint4*>(xp);
-    r.xb = *reinterpret_cast<const uint4*>(xp + 4);
-    r.sx = *reinterpret_cast<const float2*>(seeds_lane + (size_t)gl * 4 * SEEDF);
-    return r;
-}
 // One granule's four mma over the group's k-steps, one chain: c = 2^-24 * sum(q x)
 // per row (g, g+8) and column (2t, 2t+1).
 QW_DEV void granule_mma(const uint4 wv, const GAct& x, float (&c)[4]) {
@@ -835,6 +847,53 @@ QW_DEV void gemv_epilogue(const MkArgs& a, const PhaseInfo& P, int Mx, const flo
     }
 }
 
+// ---- attention items ---------------------------------------------------------
+// Items of one launch: (kv head, split) of the sequence, or, in a batched step,
+// (sequence, kv head, split) in sequence order.
+QW_DEV int attn_items(const MkArgs& a, const MkMisc& mm) {
+    return a.nseq > 0 ? mm.ibase[a.nseq] : a.aa.Hkv * attn::split_count(mm.seq + a.M);
+}
+// Item `it` of layer l: its kv head, split, split count, first new position and
+// the attention arguments of its sequence.
+struct AttnItem {
+    int kvh, split, nsp, off;
+};
+QW_DEV AttnItem attn_item(const MkArgs& a, const MkMisc& mm, int l, int it, const bf16* qn, const bf16* kn,
+                          AttnArgs& aa) {
+    aa = a.aa;
+    aa.q_norm_w = qn;
+    aa.k_norm_w = kn;
+    AttnItem r;
+    if (a.nseq == 0) {
+        r.off = mm.seq;
+        r.nsp = attn::split_count(mm.seq + a.M);
+        aa.kcache = a.kc0 + (size_t)l * a.kv_layer_elems;
+        aa.vcache = a.vc0 + (size_t)l * a.kv_layer_elems;
+        r.kvh = it / r.nsp;
+        r.split = it - r.kvh * r.nsp;
+        return r;
+    }
+    int b = 0;
+    while (b + 1 < a.nseq && it >= mm.ibase[b + 1]) ++b;
+    const int j = it - mm.ibase[b];
+    r.off = mm.seqb[b];
+    r.nsp = attn::split_count(r.off + 1);
+    r.kvh = j / r.nsp;
+    r.split = j - r.kvh * r.nsp;
+    const MkSeq& sq = a.seqs[b];
+    aa.q = a.q + (size_t)b * a.QD;
+    aa.k = a.k + (size_t)b * a.KD;
+    aa.v = a.v + (size_t)b * a.KD;
+    aa.out = a.attn + (size_t)b * a.QD;
+    aa.S = 1;
+    aa.max_pos = sq.max_pos;
+    aa.kcache = sq.kc0 + (size_t)l * sq.kv_layer_elems;
+    aa.vcache = sq.vc0 + (size_t)l * sq.kv_layer_elems;
+    aa.part = a.aa.part + (size_t)b * a.part_seq_stride;
+    aa.counters = a.aa.counters + (size_t)b * a.aa.Hkv;
+    return r;
+}
+
 // ---- the kernel ------------------------------------------------------------
 template <int RMAX, int R>
 __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const __grid_constant__ MkArgs a) {
@@ -847,11 +906,20 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const __grid_cons
     const int C = gridDim.x;
 
     // a finished greedy loop / spec loop turns the remaining replays into no-ops
-    if ((a.gate && *a.gate) || (a.ctl && a.ctl->done)) return;
+    if ((a.gate && *a.gate) || (a.ctl && a.ctl->done) || (a.bctl && a.bctl->done)) return;
     if (tid == 0) {
         mm.bad = 0;
         mm.last = 0;
-        mm.seq = *a.seq_len;
+        if (a.nseq > 0) {
+            mm.seq = 0;
+            mm.ibase[0] = 0;
+            for (int b = 0; b < a.nseq; ++b) {
+                mm.seqb[b] = *a.seqs[b].seq_len;
+                mm.ibase[b + 1] = mm.ibase[b] + a.aa.Hkv * attn::split_count(mm.seqb[b] + 1);
+            }
+        } else {
+            mm.seq = *a.seq_len;
+        }
         for (int i = 0; i < MK_NW * MK_NSLOT; ++i) mbar_init(&fullb[i], 1);
         fence_mbar_init();
     }
@@ -941,15 +1009,11 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const __grid_cons
             csync();
             {
                 // this CTA's first attention item: issue its cached K/V rows now
-                const int nsp = attn::split_count(mm.seq + M);
-                if ((int)blockIdx.x < a.aa.Hkv * nsp) {
-                    AttnArgs aa = a.aa;
-                    aa.q_norm_w = q_norm;
-                    aa.k_norm_w = k_norm;
-                    aa.kcache = a.kc0 + (size_t)l * a.kv_layer_elems;
-                    aa.vcache = a.vc0 + (size_t)l * a.kv_layer_elems;
-                    attn::split_preload<RMAX>(aa, *reinterpret_cast<attn::SplitSmem<RMAX>*>(uni),
-                                              blockIdx.x / nsp, blockIdx.x % nsp, mm.seq, tid);
+                if ((int)blockIdx.x < attn_items(a, mm)) {
+                    AttnArgs aa;
+                    const AttnItem ai = attn_item(a, mm, l, blockIdx.x, q_norm, k_norm, aa);
+                    attn::split_preload<RMAX>(aa, *reinterpret_cast<attn::SplitSmem<RMAX>*>(uni), ai.kvh, ai.split,
+                                              ai.off, tid);
                 }
             }
             MK_STAMP(5 * l, 6);
@@ -962,16 +1026,14 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const __grid_cons
             if (!ok) break;
             MK_STAMP(5 * l + 1, 0);
             {
-                const int nsp = attn::split_count(mm.seq + M);
-                AttnArgs aa = a.aa;
-                aa.q_norm_w = q_norm;
-                aa.k_norm_w = k_norm;
-                aa.kcache = a.kc0 + (size_t)l * a.kv_layer_elems;
-                aa.vcache = a.vc0 + (size_t)l * a.kv_layer_elems;
-                aa.prof = a.prof ? a.prof + ((size_t)blockIdx.x * MK_PROF_PHASES + 5 * l + 1) * MK_PROF_SLOTS : nullptr;
                 attn::SplitSmem<RMAX>& asm_ = *reinterpret_cast<attn::SplitSmem<RMAX>*>(uni);
-                for (int it = blockIdx.x; it < a.aa.Hkv * nsp; it += C) {
-                    attn::split_body<RMAX, MK_NT>(aa, asm_, it / nsp, it % nsp, nsp, mm.seq, tid, CSync{},
+                const int items = attn_items(a, mm);
+                for (int it = blockIdx.x; it < items; it += C) {
+                    AttnArgs aa;
+                    const AttnItem ai = attn_item(a, mm, l, it, q_norm, k_norm, aa);
+                    aa.prof = a.prof ? a.prof + ((size_t)blockIdx.x * MK_PROF_PHASES + 5 * l + 1) * MK_PROF_SLOTS
+                                     : nullptr;
+                    attn::split_body<RMAX, MK_NT>(aa, asm_, ai.kvh, ai.split, ai.nsp, ai.off, tid, CSync{},
                                                   it == (int)blockIdx.x);
                     csync();
                 }
@@ -1091,7 +1153,31 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const __grid_cons
     }
     csync();
     if (tid == 0) {
-        if (!aborted) {
+        if (!aborted && a.nseq > 0) {
+            // batched step: every sequence advanced by its one row
+            for (int b = 0; b < a.nseq; ++b) *a.seqs[b].seq_len += 1;
+            if (a.bctl) {
+                BatchCtl* bc = a.bctl;
+                for (int b = 0; b < a.nseq; ++b) {
+                    const int tok = a.argmax[b], g = a.b0 + b;
+                    if (!bc->stopped[g]) {
+                        bool eos = false;
+                        for (int i = 0; i < bc->n_eos; ++i) eos |= (bc->eos[i] == tok);
+                        if (eos)
+                            bc->stopped[g] = 1;
+                        else
+                            a.out[(size_t)g * bc->max_new + bc->n_out[g]++] = tok;
+                    }
+                    a.next_tok[g] = tok;
+                }
+                if (a.bfinalize) {
+                    bc->produced += 1;
+                    bool all = true;
+                    for (int g = 0; g < a.btotal; ++g) all &= bc->stopped[g] != 0;
+                    if (all || bc->produced >= bc->max_new) bc->done = 1;
+                }
+            }
+        } else if (!aborted) {
             // step_finish_kernel semantics (misc.cu)
             if (a.ctl == nullptr) {
                 *a.seq_len += M;
@@ -1114,7 +1200,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const __grid_cons
             }
         }
         if (aborted)
-            for (int h = 0; h < a.aa.Hkv; ++h) a.aa.counters[h] = 0u;
+            for (int h = 0; h < a.aa.Hkv * (a.nseq > 0 ? a.nseq : 1); ++h) a.aa.counters[h] = 0u;
         a.sync[0] = 0u;
         a.sync[1] = 0u;
         a.sync[2] = 0u;  // visible to the next launch at kernel completion
@@ -1396,6 +1482,30 @@ bool mk_launch_t(qw_model* m, MkArgs& a, cudaStream_t st) {
 
 }  // namespace
 
+int mk_batch_rows(qw_model* m) {
+    MkState* s = m->mk;
+    if (!s) return 0;
+    int max_smem = 0;
+    QW_CUDA(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device));
+    const int G = m->hq_l / m->hkv_l;
+    const int np = 4 * m->cfg.layers + 1;
+    const size_t misc = ((sizeof(MkMisc) + 127) & ~(size_t)127) + (((size_t)np * sizeof(PhaseInfo) + 127) & ~(size_t)127);
+    const size_t bars = MK_NW * MK_NSLOT * sizeof(uint64_t);
+    const size_t ring2 = (size_t)MK_NW * mk_ns(2) * 2 * GR_BYTES;
+    int best = 0;
+    for (int M = 1; M <= 8; ++M) {
+        const size_t uni = G <= 8 ? mk_union_bytes<8>(s, M, M, s->C)
+                                  : (G <= 16 ? mk_union_bytes<16>(s, M, M, s->C) : mk_union_bytes<32>(s, M, M, s->C));
+        if (uni + misc + bars + ring2 <= (size_t)max_smem) best = M;
+    }
+    // QW_MK_BATCH_ROWS caps it (testing the sub-batched form on small models)
+    if (const char* e = std::getenv("QW_MK_BATCH_ROWS")) {
+        const int cap = std::atoi(e);
+        if (cap >= 1 && cap < best) best = cap;
+    }
+    return best;
+}
+
 size_t mk_prof_read(const qw_model* m, void* dst, size_t bytes) {
     const MkState* s = m->mk;
     if (!s || !s->prof) return 0;
@@ -1406,18 +1516,29 @@ size_t mk_prof_read(const qw_model* m, void* dst, size_t bytes) {
 }
 
 bool mk_forward(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_mode, bool store_logits,
-                int* d_argmax, cudaStream_t st, StepCtl* ctl, int* next_tok, int* out, const int* gate) {
+                int* d_argmax, cudaStream_t st, StepCtl* ctl, int* next_tok, int* out, const int* gate,
+                const MkBatch* batch) {
     MkState* s = m->mk;
+    if (batch) {
+        if (batch->nseq < 1 || batch->nseq > 8) return false;
+        S = batch->nseq;
+        c = batch->caches[0];
+    }
     if (!s || S < 1 || S > 8) return false;
     const Config& cf = m->cfg;
     Workspace& w = m->ws;
-    const int G = m->hq_l / m->hkv_l, R = G * S;
+    const int G = m->hq_l / m->hkv_l, R = G * (batch ? 1 : S);
     if (R > 32) return false;
+    const int rmax = R <= 8 ? 8 : (R <= 16 ? 16 : 32);
     const int rows = logits_mode == 0 ? 0 : (logits_mode == 2 ? S : 1);
     if (rows > w.cap_logits || S > w.cap_rows) return false;
-    // attention partials: [kv head][128-key split][32 rows] must fit the workspace's
-    // [kv head][2 * SMs][64 rows] buffer
-    if ((long long)((c->max_pos + attn::SPLIT_KEYS - 1) / attn::SPLIT_KEYS) * 32 > 2LL * m->num_sms * 64) return false;
+    // attention partials: [sequence][kv head][128-key split][rmax rows][130] must fit
+    // the workspace's [kv head][2 * SMs][64 rows][130] buffer
+    int max_pos = c->max_pos;
+    if (batch)
+        for (int b = 0; b < batch->nseq; ++b) max_pos = std::max(max_pos, batch->caches[b]->max_pos);
+    const long long part_seq = (long long)m->hkv_l * ((max_pos + attn::SPLIT_KEYS - 1) / attn::SPLIT_KEYS) * rmax * 130;
+    if (part_seq * (batch ? batch->nseq : 1) > (long long)m->hkv_l * 2 * m->num_sms * 64 * 130) return false;
 
     MkArgs a;
     std::memset(&a, 0, sizeof(a));
@@ -1483,6 +1604,23 @@ bool mk_forward(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_mo
     a.trace_mid = m->trace_mid;
     a.trace_attn = m->trace_attn;
     a.prof = s->prof;
+    if (batch) {
+        a.nseq = batch->nseq;
+        a.bctl = batch->bctl;
+        a.b0 = batch->b0;
+        a.btotal = batch->btotal > 0 ? batch->btotal : batch->nseq;
+        a.bfinalize = batch->finalize ? 1 : 0;
+        a.part_seq_stride = (size_t)part_seq;
+        for (int b = 0; b < batch->nseq; ++b) {
+            const qw_cache* cb = batch->caches[b];
+            a.seqs[b].kc0 = cb->k;
+            a.seqs[b].vc0 = cb->v;
+            a.seqs[b].seq_len = cb->d_seq_len;
+            a.seqs[b].max_pos = cb->max_pos;
+            a.seqs[b].kv_layer_elems = (size_t)m->hkv_l * cb->max_pos * 128;
+        }
+        a.trace = a.trace_mid = a.trace_attn = nullptr;
+    }
     if (R <= 8) return mk_launch_t<8>(m, a, st);
     if (R <= 16) return mk_launch_t<16>(m, a, st);
     return mk_launch_t<32>(m, a, st);

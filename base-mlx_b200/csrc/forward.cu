@@ -286,6 +286,131 @@ void generate_greedy_dev(qw_model* m, qw_cache* c, int n_prompt, int max_new, co
     }
 }
 
+// Batched greedy decode (benchmark config 5 at batch 8): each sequence is
+// prefilled on its own (its first token from the prompt's last row), then one
+// captured batched step -- every sequence's newest token through the
+// persistent kernel as one row, each row attending to its own cache -- is
+// replayed max_new - 1 times.  The kernel's last CTA does the bookkeeping
+// (per-sequence EOS and output lists, next ids); once every sequence has
+// stopped the remaining replays do nothing.  Every row's arithmetic is the
+// single-sequence decode step's, so each sequence's tokens equal its batch-1
+// greedy run.
+void generate_greedy_batch_dev(qw_model* m, qw_cache* const* caches, int nseq, const std::vector<std::vector<int>>& prompts,
+                               int max_new, const std::vector<int>& eos, std::vector<std::vector<int>>& outs,
+                               qw_gen_stats* stats, cudaStream_t st) {
+    Workspace& w = m->ws;
+    if (nseq < 1 || nseq > 8) throw Error(QW_ERR_INVALID_ARG, "batch of 1..8 sequences");
+    if ((size_t)nseq * max_new > (size_t)w.out_cap) throw Error(QW_ERR_INVALID_ARG, "max_new too large");
+    for (int b = 0; b < nseq; ++b) {
+        qw_cache* c = caches[b];
+        const int n = (int)prompts[b].size();
+        if (n + max_new > c->max_pos)
+            throw Error(QW_ERR_KV_EXHAUSTED, "KV cache exhausted: requested " + std::to_string(n + max_new) +
+                                                 " positions, max " + std::to_string(c->max_pos));
+        for (int b2 = 0; b2 < b; ++b2)
+            if (caches[b2] == c) throw Error(QW_ERR_INVALID_ARG, "a cache appears twice in the batch");
+    }
+    cudaEvent_t e0, e1, e2;
+    QW_CUDA(cudaEventCreate(&e0));
+    QW_CUDA(cudaEventCreate(&e1));
+    QW_CUDA(cudaEventCreate(&e2));
+    QW_CUDA(cudaEventRecord(e0, st));
+    for (int b = 0; b < nseq; ++b) {
+        qw_cache* c = caches[b];
+        const int zero = 0, n = (int)prompts[b].size();
+        QW_CUDA(cudaMemcpyAsync(c->d_seq_len, &zero, sizeof(int), cudaMemcpyHostToDevice, st));
+        c->seq_len = 0;
+        QW_CUDA(cudaMemcpyAsync(w.ids, prompts[b].data(), (size_t)n * 4, cudaMemcpyHostToDevice, st));
+        forward_dev(m, c, w.ids, n, 1, false, w.next_tok + b, st, nullptr, nullptr, nullptr);
+    }
+    int first[8];
+    QW_CUDA(cudaMemcpyAsync(first, w.next_tok, (size_t)nseq * 4, cudaMemcpyDeviceToHost, st));
+    QW_CUDA(cudaStreamSynchronize(st));
+    BatchCtl bc;
+    std::memset(&bc, 0, sizeof(bc));
+    bc.produced = 1;
+    bc.max_new = max_new;
+    bc.n_eos = (int)std::min<size_t>(eos.size(), 8);
+    for (int i = 0; i < bc.n_eos; ++i) bc.eos[i] = eos[i];
+    bool all = true;
+    for (int b = 0; b < nseq; ++b) {
+        bool is_eos = false;
+        for (int i = 0; i < bc.n_eos; ++i) is_eos |= bc.eos[i] == first[b];
+        bc.stopped[b] = is_eos;
+        if (!is_eos) {
+            QW_CUDA(cudaMemcpyAsync(w.out + (size_t)b * max_new, &first[b], 4, cudaMemcpyHostToDevice, st));
+            bc.n_out[b] = 1;
+        }
+        all &= is_eos;
+    }
+    bc.done = (all || max_new <= 1) ? 1 : 0;
+    QW_CUDA(cudaMemcpyAsync(w.bctl, &bc, sizeof(bc), cudaMemcpyHostToDevice, st));
+    QW_CUDA(cudaStreamSynchronize(st));  // the host copies above read stack memory
+    QW_CUDA(cudaEventRecord(e1, st));
+    if (max_new > 1 && !bc.done) {
+        // sub-batches of at most mk_batch_rows sequences (shared memory holds every
+        // row's staged activations), one launch each per step, sizes balanced
+        const int cap = mk_batch_rows(m);
+        if (cap < 1) throw Error(QW_ERR_UNSUPPORTED, "this model does not fit the batched decode step");
+        const int nch = (nseq + cap - 1) / cap;
+        cudaGraph_t g;
+        cudaGraphExec_t ge = nullptr;
+        QW_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        bool ok = true;
+        try {
+            for (int ci = 0, b0 = 0; ci < nch; ++ci) {
+                const int nc = nseq / nch + (ci < nseq % nch ? 1 : 0);
+                MkBatch mb{caches + b0, nc, w.bctl, b0, nseq, ci == nch - 1};
+                ok = ok && mk_forward(m, caches[b0], w.next_tok + b0, nc, 2, false, w.argmax, st, nullptr, w.next_tok,
+                                      w.out, nullptr, &mb);
+                b0 += nc;
+            }
+        } catch (...) {
+            cudaStreamEndCapture(st, &g);
+            throw;
+        }
+        QW_CUDA(cudaStreamEndCapture(st, &g));
+        if (!ok) {
+            cudaGraphDestroy(g);
+            throw Error(QW_ERR_UNSUPPORTED, "this model / batch does not fit the batched decode step");
+        }
+        QW_CUDA(cudaGraphInstantiate(&ge, g, 0));
+        cudaGraphDestroy(g);
+        for (int i = 1; i < max_new; ++i) QW_CUDA(cudaGraphLaunch(ge, st));
+        QW_CUDA(cudaEventRecord(e2, st));
+        QW_CUDA(cudaStreamSynchronize(st));
+        cudaGraphExecDestroy(ge);
+    } else {
+        QW_CUDA(cudaEventRecord(e2, st));
+        QW_CUDA(cudaStreamSynchronize(st));
+    }
+    QW_CUDA(cudaMemcpy(&bc, w.bctl, sizeof(bc), cudaMemcpyDeviceToHost));
+    float pf = 0, dc = 0;
+    cudaEventElapsedTime(&pf, e0, e1);
+    cudaEventElapsedTime(&dc, e1, e2);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaEventDestroy(e2);
+    outs.assign(nseq, {});
+    std::vector<int> h((size_t)nseq * max_new);
+    QW_CUDA(cudaMemcpy(h.data(), w.out, h.size() * 4, cudaMemcpyDeviceToHost));
+    int total = 0;
+    for (int b = 0; b < nseq; ++b) {
+        outs[b].assign(h.begin() + (size_t)b * max_new, h.begin() + (size_t)b * max_new + bc.n_out[b]);
+        total += bc.n_out[b] + (bc.stopped[b] ? 1 : 0);
+        QW_CUDA(cudaMemcpy(&caches[b]->seq_len, caches[b]->d_seq_len, sizeof(int), cudaMemcpyDeviceToHost));
+    }
+    if (stats) {
+        int np = 0;
+        for (int b = 0; b < nseq; ++b) np += (int)prompts[b].size();
+        stats->prompt_tokens = np;
+        stats->completion_tokens = total;
+        stats->finish_reason = 0;
+        stats->prefill_ms = pf;
+        stats->decode_ms = dc;
+    }
+}
+
 }  // namespace qw
 
 namespace qw {

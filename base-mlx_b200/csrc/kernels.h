@@ -115,6 +115,18 @@ struct StepCtl {
     int n_eos;
     int eos[8];
 };
+// Batched greedy decode control block (device): the step count, each
+// sequence's output count and whether it stopped at EOS; `done` once every
+// sequence stopped or the token budget is spent (later replays do nothing).
+struct BatchCtl {
+    int produced;  // tokens picked per sequence so far (the prefill's included)
+    int max_new;
+    int done;
+    int n_eos;
+    int eos[8];
+    int n_out[8];
+    int stopped[8];
+};
 // Temperature / top-p sampling parameters (SamplingParams fields that
 // engine.rs:195-263 pick_next reads).  seed drives a counter-based draw:
 // u = top 24 bits of splitmix64(seed ^ splitmix64(counter)) / 2^24, counter =

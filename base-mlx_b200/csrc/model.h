@@ -75,6 +75,7 @@ struct Workspace {
     int* out = nullptr;          // generated tokens
     int out_cap = 0;
     StepCtl* ctl = nullptr;
+    BatchCtl* bctl = nullptr;
     float* probs = nullptr;      // sampling: softmax probabilities [vocab]
     SampleCfg* scfg = nullptr;   // sampling parameters of the running generation
     void* sctrl = nullptr;       // sampling control block (zeroed at allocation)
@@ -160,9 +161,23 @@ void mk_prepare(qw_model* m);
 void mk_free(qw_model* m);
 // QW_MK_PROFILE diagnostics: copy the persistent kernel's stamp buffer; bytes copied (0 when absent)
 size_t mk_prof_read(const qw_model* m, void* dst, size_t bytes);
+// A batched step: nseq independent sequences, one new token each (row b of
+// the ids / logits / argmax is sequence b, with cache caches[b]).
+struct MkBatch {
+    qw_cache* const* caches;
+    int nseq;
+    BatchCtl* bctl;  // device loop bookkeeping, or null
+    int b0 = 0;       // first sequence of this launch within the whole batch
+    int btotal = 0;   // sequences in the whole batch (0: nseq)
+    bool finalize = true;  // this launch completes the step
+};
+// Largest number of sequences one batched step carries on this model (shared
+// memory holds every row's staged activations), 0 without the persistent kernel.
+int mk_batch_rows(qw_model* m);
 // false when the step does not fit the persistent kernel (the caller runs the kernel chain)
 bool mk_forward(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_mode, bool store_logits,
-                int* d_argmax, cudaStream_t st, StepCtl* ctl, int* next_tok, int* out, const int* gate);
+                int* d_argmax, cudaStream_t st, StepCtl* ctl, int* next_tok, int* out, const int* gate,
+                const MkBatch* batch = nullptr);
 
 // forward.cu
 // logits_mode: 0 = none, 1 = last row, 2 = all rows
@@ -170,6 +185,10 @@ void forward_dev(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_m
                  int* d_argmax, cudaStream_t st, StepCtl* ctl, int* next_tok, int* out, const int* gate = nullptr);
 void generate_greedy_dev(qw_model* m, qw_cache* c, int n_prompt, int max_new, const std::vector<int>& eos,
                          qw_gen_stats* stats, cudaStream_t st);
+// nseq prompts decoded together (one persistent step per token for all of them)
+void generate_greedy_batch_dev(qw_model* m, qw_cache* const* caches, int nseq, const std::vector<std::vector<int>>& prompts,
+                               int max_new, const std::vector<int>& eos, std::vector<std::vector<int>>& outs,
+                               qw_gen_stats* stats, cudaStream_t st);
 void generate_sampled_dev(qw_model* m, qw_cache* c, int n_prompt, int max_new, const std::vector<int>& eos,
                           const SampleCfg& cfg, qw_gen_stats* stats, cudaStream_t st);
 

@@ -127,6 +127,9 @@ SIGNATURES = {
     "qw_forward_trace": [P, P, U32P, I, U16P, U16P, U16P, U16P, U32P],
     "qw_debug_decode_stamps": [P, P, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)],
     "qw_generate_greedy": [P, U32P, I, I, U32P, I, U32P, ctypes.POINTER(I), ctypes.POINTER(GenStats)],
+    "qw_generate_greedy_batch": [P, ctypes.POINTER(P), I, U32P, ctypes.POINTER(I), I, U32P, I, U32P,
+                                 ctypes.POINTER(I), ctypes.POINTER(GenStats)],
+    "qw_forward_batch": [P, ctypes.POINTER(P), I, U32P, U16P, U32P],
     "qw_generate_sampled": [P, U32P, I, I, ctypes.c_float, ctypes.c_float, ctypes.c_uint64, I, U32P, I, U32P,
                             ctypes.POINTER(I), ctypes.POINTER(GenStats)],
     "qw_sample_topp": [P, I, ctypes.c_float, ctypes.c_float, ctypes.c_uint64, ctypes.c_uint64, P, P, P],
@@ -312,6 +315,48 @@ class Qwen3:
         check(lib().qw_forward_trace(self.h, cache.h, ids_p, n, res.ctypes.data_as(U16P), mid.ctypes.data_as(U16P),
                                      att.ctypes.data_as(U16P), logits.ctypes.data_as(U16P), am.ctypes.data_as(U32P)))
         return bf16_to_f32(res), bf16_to_f32(mid), bf16_to_f32(att), bf16_to_f32(logits), int(am[0])
+
+    def forward_batch(self, tokens, caches, want_logits: bool = True):
+        """One batched decode step: tokens[b] at caches[b]'s next position.
+        Returns (logits [nseq, vocab] float32 or None, argmax [nseq])."""
+        ids, ids_p = _u32(tokens)
+        n = len(ids)
+        hs = (P * n)(*[c.h for c in caches])
+        logits = np.empty((n, self.vocab_local), np.uint16) if want_logits else None
+        am = np.empty(n, np.uint32)
+        check(lib().qw_forward_batch(self.h, hs, n, ids_p, logits.ctypes.data_as(U16P) if want_logits else None,
+                                     am.ctypes.data_as(U32P)))
+        return (bf16_to_f32(logits) if want_logits else None), am
+
+    def generate_greedy_batch(self, prompts, max_new: int, caches=None, eos=None):
+        """Greedy decode of several prompts at once (one cache each; created
+        with room for prompt + max_new when not given).  Returns (list of
+        token lists, GenStats)."""
+        n = len(prompts)
+        own = caches is None
+        if own:
+            caches = [self.new_cache(len(p) + max(max_new, 1) + 1) for p in prompts]
+        flat = np.concatenate([np.asarray(p, np.uint32) for p in prompts])
+        fp = flat.ctypes.data_as(U32P)
+        lens = (I * n)(*[len(p) for p in prompts])
+        mn = max(max_new, 1)
+        out = np.empty((n, mn), np.uint32)
+        n_out = (I * n)()
+        st = GenStats()
+        if eos is not None:
+            e, ep = _u32(eos)
+            ne = len(e)
+        else:
+            ep, ne = None, 0
+        hs = (P * n)(*[c.h for c in caches])
+        try:
+            check(lib().qw_generate_greedy_batch(self.h, hs, n, fp, lens, max_new, ep, ne, out.ctypes.data_as(U32P),
+                                                 n_out, ctypes.byref(st)))
+        finally:
+            if own:
+                for c in caches:
+                    c.close()
+        return [[int(t) for t in out[b, :n_out[b]]] for b in range(n)], st
 
     def generate_greedy(self, prompt, max_new: int, eos=None) -> GenerationResult:
         p, pp = _u32(prompt)

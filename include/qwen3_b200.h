@@ -181,6 +181,28 @@ QW_API int qw_generate_greedy(qw_model* m, const uint32_t* prompt_host, int n_pr
                               const uint32_t* eos, int n_eos, uint32_t* out_host, int* n_out,
                               qw_gen_stats* stats);
 
+/* Batched greedy generation (benchmark config 5 at batch 8; the reference
+ * serves one request at a time, model.rs:21-108, so this has no single
+ * reference counterpart: it is generate_text's greedy loop, engine.rs:149-201,
+ * for nseq independent requests at once).  nseq (1..8) prompts, concatenated
+ * in prompts_host with lengths n_prompt[nseq], each decoded in its own cache
+ * caches[nseq] (distinct, of this model; reset to the prompt first).  Every
+ * decode step carries all nseq sequences through the weights once; each
+ * sequence's tokens equal its batch-1 greedy run.  out_host is [nseq][max_new]
+ * (row stride max_new), n_out[b] = ids written for sequence b (a terminating
+ * EOS is not written); stats: prompt / completion tokens summed over the
+ * batch, prefill_ms of all prompts, decode_ms of the batched loop. */
+QW_API int qw_generate_greedy_batch(qw_model* m, qw_cache* const* caches, int nseq, const uint32_t* prompts_host,
+                                    const int* n_prompt, int max_new, const uint32_t* eos, int n_eos,
+                                    uint32_t* out_host, int* n_out, qw_gen_stats* stats);
+
+/* One batched decode step: token ids_host[b] of sequence b at caches[b]'s next
+ * position (nseq 1..8, distinct caches); logits_out_host [nseq][vocab] bf16
+ * (may be NULL) and argmax_out_host [nseq] (may be NULL).  Each cache grows
+ * by one position. */
+QW_API int qw_forward_batch(qw_model* m, qw_cache* const* caches, int nseq, const uint32_t* ids_host,
+                            uint16_t* logits_out_host, uint32_t* argmax_out_host);
+
 /* Greedy speculative decoding: k drafted tokens per iteration, one (k+1)-row
  * target verify, on-device accept and rollback.  k = 3 reproduces the
  * reference loop (SPEC_K = 4).  With forced_seq != NULL and force_p > 0 each
