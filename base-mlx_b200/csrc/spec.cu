@@ -10,9 +10,14 @@
 //   bonus is fed to the draft.
 //
 // B200 structure: the per-iteration work is three captured CUDA graphs
-// (draft: draft forward of the leader, then k x [pick + draft forward];
-// verify: target forward of k+1 rows; accept: the accept kernel) replayed back
-// to back.
+// (draft: one 2-row draft forward of [token before the leader, leader], then
+// k picks with a 1-row draft forward between consecutive picks; verify: target
+// forward of k+1 rows; accept: the accept kernel) replayed back to back.  The
+// k-th drafted token is never run through the draft here: its KV row, needed
+// only when all k are accepted, is the first row of the next iteration's
+// 2-row forward, which otherwise rewrites the last kept position with the
+// same token (a row's results do not depend on the row count, so the rewrite
+// is bit-identical).  k draft forwards per iteration instead of k + 1.
 // The accept kernel compares, emits, updates the statistics and rewinds both
 // device-side cache lengths, so the host never waits on a token: it only
 // polls a mapped "done" flag two iterations behind the GPU.
@@ -51,9 +56,10 @@ QW_DEV bool in_list(const int* l, int n, int t) {
     return r;
 }
 
-// After the prefill: leader = target argmax of the last prompt row.
-__global__ void spec_init_kernel(SpecCtl* c, const int* t_argmax, int* verify_in, int* draft_in, int* out,
-                                 volatile int* host_flag) {
+// After the prefill: leader = target argmax of the last prompt row; the
+// draft's first input pair is (last prompt token, leader) at positions plen-1, plen.
+__global__ void spec_init_kernel(SpecCtl* c, const int* t_argmax, int* verify_in, int* draft_in2,
+                                 const int* prompt, int* d_seq, int* out, volatile int* host_flag) {
     pdl_wait();
     pdl_launch_dependents();
     if (threadIdx.x != 0) return;
@@ -67,7 +73,9 @@ __global__ void spec_init_kernel(SpecCtl* c, const int* t_argmax, int* verify_in
         if (c->emitted >= c->max_new) c->done = 1;
     }
     verify_in[0] = leader;
-    *draft_in = leader;
+    draft_in2[0] = prompt[c->plen - 1];
+    draft_in2[1] = leader;
+    *d_seq = c->plen - 1;
     c->slot = 0;
     c->n_eff = c->k;
     host_flag[0] = c->done;
@@ -97,7 +105,7 @@ __global__ void spec_pick_kernel(SpecCtl* c, const int* d_argmax, const int* for
 }
 
 // speculative.rs:153-239: accept, emit, roll back both caches, set up the next leader.
-__global__ void spec_accept_kernel(SpecCtl* c, const int* preds, int* verify_in, int* draft_in, int* out,
+__global__ void spec_accept_kernel(SpecCtl* c, const int* preds, int* verify_in, int* draft_in2, int* out,
                                    int* t_seq, int* d_seq, volatile int* host_flag) {
     pdl_wait();
     pdl_launch_dependents();
@@ -131,11 +139,14 @@ __global__ void spec_accept_kernel(SpecCtl* c, const int* preds, int* verify_in,
             c->done = 1;
         } else {
             out[c->emitted++] = bonus;
-            const int keep = c->plen + c->emitted - 1;
+            const int keep = c->plen + c->emitted - 1;  // the bonus's position
             *t_seq = keep;
-            *d_seq = keep;
+            // the draft restarts one position earlier: its next 2-row forward
+            // (re)computes the last kept token and runs the bonus
+            *d_seq = keep - 1;
+            draft_in2[0] = verify_in[n_acc];  // d_{n_acc}, or the old leader when none was accepted
+            draft_in2[1] = bonus;
             verify_in[0] = bonus;
-            *draft_in = bonus;
             c->slot = 0;
             c->n_eff = c->k;
             if (c->emitted >= c->max_new) c->done = 1;
@@ -235,7 +246,8 @@ void spec_generate_dev(qw_model* t, qw_model* d, const SpecRequest& r, std::vect
     Workspace& tw = t->ws;
     Workspace& dw = d->ws;
     int* verify_in = tw.ids;
-    int* draft_in = dw.next_tok;
+    int* draft_in2 = dw.next_tok;     // [2]: the 2-row draft input of an iteration
+    int* draft_in = dw.next_tok + 2;  // the 1-row draft input after each pick
     int* flag = S->host_flag;
     const int* gate = &S->ctl->done;
 
@@ -248,18 +260,19 @@ void spec_generate_dev(qw_model* t, qw_model* d, const SpecRequest& r, std::vect
                 *g = nullptr;
             }
         S->gD = capture(st, [&] {
-            forward_dev(d, dc, draft_in, 1, 1, false, dw.argmax, st, nullptr, nullptr, nullptr, gate);
+            forward_dev(d, dc, draft_in2, 2, 1, false, dw.argmax, st, nullptr, nullptr, nullptr, gate);
             for (int j = 0; j < r.k; ++j) {
                 QW_CUDA(launch1(spec_pick_kernel, st, S->ctl, (const int*)dw.argmax, (const int*)S->forced, verify_in,
                                 draft_in));
-                forward_dev(d, dc, draft_in, 1, 1, false, dw.argmax, st, nullptr, nullptr, nullptr, gate);
+                if (j + 1 < r.k)
+                    forward_dev(d, dc, draft_in, 1, 1, false, dw.argmax, st, nullptr, nullptr, nullptr, gate);
             }
         });
         S->gV = capture(st, [&] {
             forward_dev(t, tc, verify_in, r.k + 1, 2, false, tw.argmax, st, nullptr, nullptr, nullptr, gate);
         });
         S->gA = capture(st, [&] {
-            QW_CUDA(launch1(spec_accept_kernel, st, S->ctl, (const int*)tw.argmax, verify_in, draft_in, tw.out,
+            QW_CUDA(launch1(spec_accept_kernel, st, S->ctl, (const int*)tw.argmax, verify_in, draft_in2, tw.out,
                             tc->d_seq_len, dc->d_seq_len, (volatile int*)flag));
         });
         S->draft = d;
@@ -305,8 +318,8 @@ void spec_generate_dev(qw_model* t, qw_model* d, const SpecRequest& r, std::vect
     QW_CUDA(cudaEventRecord(S->ev[0], st));
     forward_dev(t, tc, tw.ids, r.n_prompt, 1, false, tw.argmax, st, nullptr, nullptr, nullptr, nullptr);
     forward_dev(d, dc, dw.ids, r.n_prompt, 0, false, dw.argmax, st, nullptr, nullptr, nullptr, nullptr);
-    QW_CUDA(launch1(spec_init_kernel, st, S->ctl, (const int*)tw.argmax, verify_in, draft_in, tw.out,
-                    (volatile int*)flag));
+    QW_CUDA(launch1(spec_init_kernel, st, S->ctl, (const int*)tw.argmax, verify_in, draft_in2, (const int*)dw.ids,
+                    dc->d_seq_len, tw.out, (volatile int*)flag));
     QW_CUDA(cudaEventRecord(S->ev[1], st));
 
     int launched = 0;
