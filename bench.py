@@ -53,8 +53,8 @@ sys.path.insert(0, os.path.join(ROOT, "base-mlx_b200"))
 
 PROMPT_LEN, DECODE_TOKENS, KV_PREALLOC, SEED = 512, 300, 4096, 1234
 # DRAM bytes read per launch / algorithmic bytes of decode_step_kernel, from an ncu capture
-# (profiles/decode_step_kernel_traffic.md)
-TRAFFIC_RATIO = 1.0010
+# of the Qwen3-4B layer shapes (4 layers + lm_head; profiles/decode_step_kernel_4b_l4_full.md)
+TRAFFIC_RATIO = 1.0043
 
 # Workload shapes (config.json contents of the random-init models)
 CFG_0_6B = dict(
@@ -453,8 +453,9 @@ def run_ours(args):
         step_gbs = (w_bytes + kv_bytes) / step_s / 1e9
         roof = {"bound": "hbm", "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(step_gbs / peak, 4), "traffic": int(TRAFFIC_RATIO * (w_bytes + kv_bytes)),
-                "traffic_source": "ncu dram__bytes_read+write on the Qwen3-0.6B step, read/algorithmic ratio "
-                                  "1.0010 applied to these algorithmic bytes (profiles/decode_step_kernel_traffic.md)",
+                "traffic_source": "ncu dram__bytes_read on the Qwen3-4B layer shapes (4 layers + lm_head, one "
+                                  "launch): read/algorithmic 1.0043, applied to these algorithmic bytes "
+                                  "(profiles/decode_step_kernel_4b_l4_full.md)",
                 "kernel": "decode_step_kernel (persistent decode step: all 36 layers + lm_head in one launch)",
                 "bytes_per_launch": int(w_bytes + kv_bytes), "launches_timed": int(dec_tokens),
                 "bytes_note": "quantized weights (0.5625 B/param) + bf16 K/V read at the mean KV length 662",
@@ -610,13 +611,16 @@ def profile_sampled(n: int, model: str) -> None:
     print(f"profile_sampled: {model} prefill {plen} + {len(r.tokens)} sampled tokens")
 
 
-def profile_decode(n: int, model: str) -> None:
+def profile_decode(n: int, model: str, layers: int = 0) -> None:
     """Prefill and n decode steps, one qw_forward each (the ncu workloads): the
     bench model (Qwen3-4B, 512-token prompt) or, for captures that must stay
-    small, Qwen3-0.6B with a 128-token prompt."""
+    small, Qwen3-0.6B with a 128-token prompt; layers > 0 keeps only that many
+    decoder layers (the 4B layer shapes at a few hundred MB on the device)."""
     import torch
     import qwen3_b200 as q
     cfg = dict(CFG_4B if model == "4b" else CFG_0_6B)
+    if layers > 0:
+        cfg["num_hidden_layers"] = layers
     plen = PROMPT_LEN if model == "4b" else 128
     m = q.Qwen3.init_random(cfg, SEED, norm_mode="ones", device=0)
     c = m.new_cache(KV_PREALLOC)
@@ -624,7 +628,8 @@ def profile_decode(n: int, model: str) -> None:
     for _ in range(n):
         _, tok = m.forward([tok], c, want_logits=False)
     torch.cuda.synchronize()
-    print(f"profile_decode: {model} prefill {plen} + {n} decode steps, last token {tok}")
+    print(f"profile_decode: {model} ({cfg['num_hidden_layers']} layers) prefill {plen} + {n} decode steps, "
+          f"last token {tok}")
 
 
 def run_tp_decode(args):
@@ -750,6 +755,8 @@ def main():
                     help="profiling workload for ncu: weight init, the prefill and N greedy decode steps through "
                          "qw_forward; prints no bench line")
     ap.add_argument("--profile-model", choices=["4b", "0.6b"], default="4b")
+    ap.add_argument("--profile-layers", type=int, default=0, metavar="L",
+                    help="with --profile-decode: keep only L decoder layers")
     ap.add_argument("--profile-sampled", type=int, default=0, metavar="N",
                     help="profiling workload for ncu: a sampled generation of N tokens; prints no bench line")
     ap.add_argument("--profile-qmm", default="", metavar="M,K,N",
@@ -767,7 +774,7 @@ def main():
     elif args.profile_sampled > 0:
         profile_sampled(args.profile_sampled, args.profile_model)
     elif args.profile_decode > 0:
-        profile_decode(args.profile_decode, args.profile_model)
+        profile_decode(args.profile_decode, args.profile_model, args.profile_layers)
     elif args.impl == "reference":
         run_reference(args)
     else:
