@@ -174,6 +174,9 @@ QW_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// Generic-proxy accesses of shared memory (a consumed ring slot) ordered before
+// the bulk copy (async proxy) that refills it.
+QW_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 // Bounded wait: gives up after ~2^22 polls (each try_wait already suspends
 // for a while), so a lost transfer becomes an error flag instead of a hang.
 QW_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {

@@ -257,9 +257,6 @@ QW_DEV bool mbar_test(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// The shared-memory reads of a ring slot (generic proxy) are ordered before the
-// bulk copy (async proxy) that refills it.
-QW_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Advance to the next non-empty range of warp w, from phase c.pi on.
 QW_DEV void issue_enter(IssueCur& c, const PhaseInfo* tab, int np, int w) {

@@ -588,6 +588,186 @@ __global__ void __launch_bounds__(128) qgemm_kernel(const QmmArgs a) {
         }
 }
 
+// ===========================================================================
+// Streaming decode GEMV for the standalone op (M <= 8, one output segment,
+// plain bf16 store, no RMSNorm prologue): persistent CTAs, one per SM, walk
+// the 16-row tiles tile = blockIdx.x, blockIdx.x + gridDim.x, ...  Each tile's
+// weight rows, scales and biases (MLX layout, rows contiguous) arrive by
+// 16-byte asynchronous copies spread over all threads (tracked per slot by an
+// mbarrier every thread arrives on) into a ring of `ns` tile slots, so a CTA keeps ns tiles in flight while it computes;
+// weights do not depend on the previous kernel, so the first ns tiles are
+// issued before the programmatic-launch wait.  Activations are staged once per
+// CTA (fragment order, as in qgemv_kernel).  Warp w takes the tile's groups
+// w, w + 16, ...; the 16 warps' partial sums meet in shared memory in warp
+// order (double-buffered: one CTA barrier per tile).
+// ===========================================================================
+constexpr int GS_NW = 16;
+constexpr int GS_NS_MAX = 8;
+
+struct GsLayout {
+    unsigned rs, srs, off_s, off_b, stage, off_x, off_xsum, off_red, off_bar, total;
+};
+
+__host__ __device__ inline GsLayout gs_layout(int KG, int M, int ns) {
+    GsLayout L;
+    const int kw = KG * 8;                                // weight words per row
+    L.rs = (unsigned)(kw + ((8 - (kw % 32)) + 32) % 32) * 4u;  // row stride = 32 B mod 128 B: conflict-free fragments
+    L.srs = (unsigned)((KG * 2 + 15) / 16) * 16u;         // one scale (bias) row
+    L.off_s = 16u * L.rs;
+    L.off_b = L.off_s + 16u * L.srs;
+    L.stage = L.off_b + 16u * L.srs;
+    L.off_x = (unsigned)ns * L.stage;
+    L.off_xsum = L.off_x + (unsigned)KG * M * XS_BLOCK_WORDS * 4u;
+    L.off_red = L.off_xsum + (unsigned)KG * 16u * 4u;
+    L.off_bar = L.off_red + 2u * GS_NW * 128u * 4u;
+    L.total = L.off_bar + GS_NS_MAX * 8u;
+    return L;
+}
+
+__global__ void __launch_bounds__(GS_NW * 32, 1) qgemv_stream_kernel(const __grid_constant__ QmmArgs a, int ns,
+                                                                      int ntiles) {
+    constexpr int NT = GS_NW * 32;
+    extern __shared__ __align__(128) unsigned char smraw[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int M = a.M, K = a.K, KW = K / 8, KG = K / 64;
+    const GsLayout L = gs_layout(KG, M, ns);
+    const QSeg& sg = a.seg[0];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smraw + L.off_bar);
+    uint32_t* xs = reinterpret_cast<uint32_t*>(smraw + L.off_x);
+    float* xsum = reinterpret_cast<float*>(smraw + L.off_xsum);  // [KG][even, odd][8 columns]
+    float* red = reinterpret_cast<float*>(smraw + L.off_red);    // [2][GS_NW][4][32]
+
+    // every thread: its 16-byte chunks of tile `tile` (consecutive threads take
+    // consecutive chunks of a row) into ring slot `slot`, then one arrival on
+    // the slot's barrier once they have landed (the barrier expects NT)
+    auto issue = [&](int tile, int slot) {
+        const int row0 = tile * 16;
+        const int nr = min(16, sg.n - row0);
+        unsigned char* base = smraw + (size_t)slot * L.stage;
+        const int cw = KW / 4, cs = KG / 8;  // 16-byte chunks per weight row, per scale (bias) row
+        const int per_row = cw + 2 * cs;
+        for (int c = threadIdx.x; c < nr * per_row; c += NT) {
+            const int r = c / per_row, j = c - r * per_row;
+            const size_t row = (size_t)row0 + r;
+            if (j < cw)
+                cp_async16(base + r * L.rs + j * 16, sg.w + row * KW + j * 4);
+            else if (j < cw + cs)
+                cp_async16(base + L.off_s + r * L.srs + (j - cw) * 16, sg.s + row * KG + (j - cw) * 8);
+            else
+                cp_async16(base + L.off_b + r * L.srs + (j - cw - cs) * 16, sg.b + row * KG + (j - cw - cs) * 8);
+        }
+        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&full[slot])) : "memory");
+    };
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < ns; ++i) mbar_init(&full[i], NT);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    for (int i = 0; i < ns; ++i) {
+        const int tile = blockIdx.x + i * gridDim.x;
+        if (tile < ntiles) issue(tile, i);
+    }
+
+    pdl_launch_dependents();
+    pdl_wait();
+
+    {
+        // activations and even / odd group sums (uniform trip count: every lane
+        // takes part in the quad shuffles)
+        const int units = KG * M * 4;
+        for (int u0 = 0; u0 < units; u0 += NT) {
+            const int u = u0 + threadIdx.x;
+            float se = 0.f, so = 0.f;
+            int gl = 0, m = 0, tt = 0;
+            if (u < units) {
+                gl = u / (M * 4);
+                const int rem = u - gl * M * 4;
+                m = rem >> 2;
+                tt = rem & 3;
+                stage16_f16(a.x + (size_t)m * a.ldx + gl * 64 + 16 * tt, nullptr, 1.f,
+                            xs + (size_t)(gl * M + m) * XS_BLOCK_WORDS + tt * 8, se, so);
+            }
+            se += __shfl_xor_sync(0xffffffffu, se, 1);
+            se += __shfl_xor_sync(0xffffffffu, se, 2);
+            so += __shfl_xor_sync(0xffffffffu, so, 1);
+            so += __shfl_xor_sync(0xffffffffu, so, 2);
+            if (u < units && tt == 0) {
+                xsum[gl * 16 + m] = se;
+                xsum[gl * 16 + 8 + m] = so;
+            }
+        }
+    }
+    __syncthreads();
+
+    const uint32_t* xb = xs + g * XS_BLOCK_WORDS + t * 8;
+    const int xstride = M * XS_BLOCK_WORDS;
+    const bool has_col = g < M;
+    const int rsw = (int)(L.rs / 4), srs2 = (int)(L.srs / 2);
+    const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int i = 0;; ++i) {
+        const int tile = blockIdx.x + i * gridDim.x;
+        if (tile >= ntiles) break;
+        const int slot = i % ns;
+        const bool landed = mbar_wait_bounded(&full[slot], (uint32_t)((i / ns) & 1));
+        if (!__syncthreads_and(landed)) {
+            if (threadIdx.x == 0 && a.err) atomicOr(a.err, QW_DERR_TIMEOUT);
+            break;
+        }
+        const uint32_t* W = reinterpret_cast<const uint32_t*>(smraw + (size_t)slot * L.stage);
+        const uint16_t* Ssm = reinterpret_cast<const uint16_t*>(smraw + (size_t)slot * L.stage + L.off_s);
+        const uint16_t* Bsm = reinterpret_cast<const uint16_t*>(smraw + (size_t)slot * L.stage + L.off_b);
+        float acc[4] = {0.f, 0.f, 0.f, 0.f}, bacc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int gl = warp; gl < KG; gl += GS_NW) {
+            uint4 be = make_uint4(0u, 0u, 0u, 0u), bo = be;
+            if (has_col) {
+                const uint4* p = reinterpret_cast<const uint4*>(xb + gl * xstride);
+                be = p[0];
+                bo = p[1];
+            }
+            const float2 xe = *reinterpret_cast<const float2*>(xsum + gl * 16 + 2 * t);
+            const float2 xo = *reinterpret_cast<const float2*>(xsum + gl * 16 + 8 + 2 * t);
+            const float xt0 = xe.x + xo.x, xt1 = xe.y + xo.y;
+            const uint2 wa = *reinterpret_cast<const uint2*>(W + g * rsw + gl * 8 + 2 * t);
+            const uint2 wb = *reinterpret_cast<const uint2*>(W + (g + 8) * rsw + gl * 8 + 2 * t);
+            const uint32_t wa8x = wa.x >> 8, wb8x = wb.x >> 8, wa8y = wa.y >> 8, wb8y = wb.y >> 8;
+            float ce[4], co[4];
+            mma_f16(ce, nib_even(wa.x), nib_even(wb.x), nib_even(wa8x), nib_even(wb8x), be.x, be.y, zero4);
+            mma_f16(co, nib_odd(wa.x), nib_odd(wb.x), nib_odd(wa8x), nib_odd(wb8x), bo.x, bo.y, zero4);
+            mma_f16(ce, nib_even(wa.y), nib_even(wb.y), nib_even(wa8y), nib_even(wb8y), be.z, be.w, ce);
+            mma_f16(co, nib_odd(wa.y), nib_odd(wb.y), nib_odd(wa8y), nib_odd(wb8y), bo.z, bo.w, co);
+            const float s0 = u16_to_f(Ssm[g * srs2 + gl]) * QW_NIB_SCALE;
+            const float s1 = u16_to_f(Ssm[(g + 8) * srs2 + gl]) * QW_NIB_SCALE;
+            const float b0 = u16_to_f(Bsm[g * srs2 + gl]), b1 = u16_to_f(Bsm[(g + 8) * srs2 + gl]);
+            acc[0] = fmaf(s0, fmaf(co[0], 0.0625f, ce[0]), acc[0]);
+            acc[1] = fmaf(s0, fmaf(co[1], 0.0625f, ce[1]), acc[1]);
+            acc[2] = fmaf(s1, fmaf(co[2], 0.0625f, ce[2]), acc[2]);
+            acc[3] = fmaf(s1, fmaf(co[3], 0.0625f, ce[3]), acc[3]);
+            bacc[0] = fmaf(b0, xt0, bacc[0]);
+            bacc[1] = fmaf(b0, xt1, bacc[1]);
+            bacc[2] = fmaf(b1, xt0, bacc[2]);
+            bacc[3] = fmaf(b1, xt1, bacc[3]);
+        }
+        float* rb = red + (size_t)(i & 1) * GS_NW * 128;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) rb[warp * 128 + e * 32 + lane] = acc[e] + bacc[e];
+        __syncthreads();
+        // the slot is free (every warp has read it): refill it with tile i + ns
+        const int next = tile + ns * (int)gridDim.x;
+        if (next < ntiles) issue(next, slot);
+        // outputs (row r, column m) of the tile: the 16 warps' sums in warp order
+        if ((int)threadIdx.x < 16 * M) {
+            const int r = threadIdx.x / M, m = threadIdx.x - r * M;
+            const int ln = 4 * (r & 7) + (m >> 1), e = 2 * (r >> 3) + (m & 1);
+            float sum = 0.f;
+#pragma unroll
+            for (int w = 0; w < GS_NW; ++w) sum += rb[w * 128 + e * 32 + ln];
+            const int row = tile * 16 + r;
+            if (row < sg.n) reinterpret_cast<bf16*>(sg.y)[(size_t)m * sg.ldy + row] = f2bf(sum);
+        }
+    }
+}
+
 template <typename Kern>
 cudaError_t launch_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
                       const QmmArgs& a) {
@@ -616,6 +796,44 @@ cudaError_t launch_qgemv_t(const QmmArgs& a, int nrb, size_t smem, cudaStream_t 
     return launch_ex(qgemv_kernel<RT, NW, false>, dim3(nrb), dim3(NW * 32), smem, st, pdl, a);
 }
 
+// The streaming GEMV when it applies (one plain-store segment, no norm, rows
+// longer than 4096 inputs -- where one CTA per tile leaves too few CTAs per SM;
+// measured on the Qwen3-4B shapes it is slower than qgemv_kernel for K <= 4096
+// -- 16-byte aligned rows and at least two tile slots in shared memory);
+// cudaErrorNotSupported otherwise.
+cudaError_t launch_qgemv_stream(const QmmArgs& a, cudaStream_t st, bool pdl, int num_sms) {
+    if (a.nseg != 1 || a.epi != EPI_STORE || a.norm_w || a.M < 1 || a.M > 8 || a.K % 512 != 0 || a.K <= 4096 ||
+        num_sms < 1)
+        return cudaErrorNotSupported;
+    const QSeg& sg = a.seg[0];
+    if (sg.n < 1 || ((uintptr_t)sg.w | (uintptr_t)sg.s | (uintptr_t)sg.b) % 16 != 0) return cudaErrorNotSupported;
+    const int KG = a.K / 64;
+    int dev = 0, dev_smem = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&dev_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return e;
+    const GsLayout L1 = gs_layout(KG, a.M, 1);
+    const long long fixed = (long long)L1.total - L1.stage;
+    const int ns = (int)std::min<long long>(GS_NS_MAX, (dev_smem - fixed) / (long long)L1.stage);
+    if (ns < 2) return cudaErrorNotSupported;
+    const GsLayout L = gs_layout(KG, a.M, ns);
+    e = ensure_max_dyn_smem(qgemv_stream_kernel, (int)L.total);
+    if (e != cudaSuccess) return e;
+    const int ntiles = (sg.n + 15) / 16;
+    const int grid = std::min(ntiles, num_sms);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(GS_NW * 32);
+    cfg.dynamicSmemBytes = L.total;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, qgemv_stream_kernel, a, ns, ntiles);
+}
+
 int qgemv_row_blocks(const QmmArgs& a) {
     if (a.epi == EPI_SWIGLU) return (a.seg[0].n + 15) / 16;
     int nrb = 0;
@@ -641,9 +859,12 @@ int qgemv_max_k(int M) {
 }
 
 cudaError_t launch_qgemv(QmmArgs a, cudaStream_t st, bool pdl, int num_sms) {
-    (void)num_sms;
     if (a.M < 1 || a.M > 8 || a.K <= 0 || a.K % 64 != 0 || a.nseg < 1 || a.nseg > 3)
         return cudaErrorInvalidValue;
+    {
+        const cudaError_t es = launch_qgemv_stream(a, st, pdl, num_sms);
+        if (es != cudaErrorNotSupported) return es;
+    }
     const int RT = a.epi == EPI_SWIGLU ? 2 : 1;
     int nrb = 0;
     if (RT == 2) {
