@@ -553,6 +553,43 @@ int qw_spec_generate(qw_model* target, qw_model* draft, const uint32_t* prompt, 
     });
 }
 
+int qw_spec_generate_sampled(qw_model* target, qw_model* draft, const uint32_t* prompt, int n_prompt, int max_new,
+                             int k, float temperature, float top_p, uint64_t seed, const uint32_t* eos, int n_eos,
+                             uint32_t* out, int* n_out, qw_spec_stats* stats) {
+    if (!(temperature > 0.f))  // greedy: the exact greedy loop
+        return qw_spec_generate(target, draft, prompt, n_prompt, max_new, k, 0.f, seed, nullptr, 0, eos, n_eos, out,
+                                n_out, stats);
+    return guard([&] {
+        need(target && draft && prompt && out && n_out, "target/draft/prompt/out");
+        need(n_prompt >= 1, "empty prompt");
+        need(top_p == top_p && temperature == temperature, "NaN parameter");
+        if (qw_check_compatible(target, draft) != QW_OK) throw qw::Error(QW_ERR_MODEL_LOAD, g_err);
+        check_ids(target, prompt, n_prompt);
+        QW_CUDA(cudaSetDevice(target->device));
+        std::vector<int> p(prompt, prompt + n_prompt);
+        qw::SpecRequest r;
+        r.prompt = p.data();
+        r.n_prompt = n_prompt;
+        r.max_new = max_new;
+        r.k = k;
+        r.force_p = 0.f;
+        r.seed = seed;
+        r.forced = nullptr;
+        r.n_forced = 0;
+        r.eos_target = eos_list(target, eos, n_eos);
+        r.eos_draft = eos_list(draft, eos, n_eos);
+        r.temperature = temperature;
+        r.top_p = top_p;
+        std::vector<int> toks;
+        qw_spec_stats s;
+        std::memset(&s, 0, sizeof(s));
+        qw::spec_generate_dev(target, draft, r, toks, &s);
+        for (size_t i = 0; i < toks.size(); ++i) out[i] = (uint32_t)toks[i];
+        *n_out = (int)toks.size();
+        if (stats) *stats = s;
+    });
+}
+
 // The multi-row qw_quantized_matmul keeps one fp16 activation buffer per
 // (device, stream), grown on demand and kept until exit: calls on one stream
 // are ordered, so they can share it, and no call pays an allocation.

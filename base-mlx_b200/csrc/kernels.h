@@ -152,6 +152,23 @@ struct SampleArgs {
     int* token_out;              // standalone: the picked token
     void* ctrl;                  // QW_SAMPLE_CTRL_BYTES control block, zero before its first use
     int* err;                    // device error flags (timeouts), may be null
+    // speculative sampling: the draw's counter = *ctr_iter * 64 + ctr_base when
+    // ctr_iter is set; desc_out receives the nucleus of `probs` (which then
+    // holds the row's softmax); no_draw skips the draw (token_out untouched)
+    const int* ctr_iter;
+    int ctr_base;
+    struct SpDesc* desc_out;
+    int no_draw;
+    const int* gate;  // nonzero: the launch does nothing (a finished loop's replays)
+};
+// The top-p nucleus of a probability row p (softmax of logits / t): x is in it
+// iff found == 0, or p[x] > value, or p[x] == value and x <= tie_idx (value =
+// the float with bits `key`); P(x) = p[x] / renorm inside it, 0 outside.
+struct SpDesc {
+    uint32_t key;
+    int tie_idx;
+    float renorm;
+    int found;
 };
 // softmax(logits / t), nucleus of cumulative mass >= top_p in descending-
 // probability order (ties by index), categorical draw inside it: one

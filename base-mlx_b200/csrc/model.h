@@ -201,6 +201,11 @@ struct SpecRequest {
     const int* forced;  // host, may be null
     int n_forced;
     std::vector<int> eos_target, eos_draft;
+    // temperature > 0: speculative sampling (draft tokens drawn from the draft's
+    // top-p distribution, accepted with probability min(1, P_target / P_draft),
+    // residual draw on rejection); force_p is ignored then
+    float temperature = 0.f;
+    float top_p = 1.f;
 };
 void spec_state_free(void* p);
 void spec_generate_dev(qw_model* target, qw_model* draft, const SpecRequest& r, std::vector<int>& out,

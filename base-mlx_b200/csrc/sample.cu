@@ -413,6 +413,7 @@ __global__ void __launch_bounds__(SG_NT, 1) sample_kernel(const SampleArgs a) {
     SpGlobal* g = reinterpret_cast<SpGlobal*>(a.ctrl);
     StepCtl* ctl = a.ctl;
     if (ctl && *reinterpret_cast<volatile int*>(&ctl->done)) return;  // same value in every CTA
+    if (a.gate && *reinterpret_cast<const volatile int*>(a.gate)) return;
     const SampleCfg cfg = a.cfg_dev ? *a.cfg_dev : a.cfg;
     const int V = a.V;
     const bf16* lg = a.logits;
@@ -485,8 +486,32 @@ __global__ void __launch_bounds__(SG_NT, 1) sample_kernel(const SampleArgs a) {
         const int np = s.n_need;
         const u64 renorm = nfound ? s.above + (u64)np * to_fx((double)__uint_as_float(kp)) : ptotal;
         __syncthreads();
+        if (a.desc_out) {
+            // the nucleus as (value, last included index among the ties, mass)
+            int tie = V - 1;
+            if (nfound) {
+                nth_equal(p, V, kp, np, s, g, target, a.err);
+                tie = __ldcg(&g->token);
+            }
+            if (blockIdx.x == 0 && tid == 0) {
+                a.desc_out->key = kp;
+                a.desc_out->tie_idx = tie;
+                a.desc_out->renorm = (float)((double)renorm / SP_FX);
+                a.desc_out->found = nfound ? 1 : 0;
+            }
+            __syncthreads();
+        }
+        if (a.no_draw) {
+            if (tid == 0 && atomicAdd(&g->exit, 1u) == gridDim.x - 1) {
+                g->bar = 0u;
+                g->exit = 0u;
+            }
+            return;
+        }
         // categorical draw (engine.rs:241-262)
-        const unsigned long long ctr = ctl ? (cfg.same_draw ? 0ull : (unsigned long long)ctl->produced) : a.counter;
+        const unsigned long long ctr =
+            a.ctr_iter ? (unsigned long long)(*a.ctr_iter) * 64ull + (unsigned long long)a.ctr_base
+                       : (ctl ? (cfg.same_draw ? 0ull : (unsigned long long)ctl->produced) : a.counter);
         const float r = __fmul_rn(sample_u(cfg.seed, ctr), (float)((double)renorm / SP_FX));
         wselect(p, V, to_fx((double)r), s, g, target, pass, a.err);
         uint32_t kr = s.key;

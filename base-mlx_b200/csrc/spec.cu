@@ -156,11 +156,194 @@ __global__ void spec_accept_kernel(SpecCtl* c, const int* preds, int* verify_in,
     host_flag[1] = c->emitted;
 }
 
+// ---- speculative sampling (temperature > 0) -----------------------------------
+// The reference falls back to plain sampled decoding for temperature > 0
+// (speculative.rs:65-69; rejection sampling is the missing piece it names).
+// This is the speculative-sampling rule over the sampled pick's distributions
+// (engine.rs:203-263: softmax of logits / t, top-p nucleus): the drafted token
+// d_i ~ Q_i (the draft's pick) is accepted with probability min(1, P_i(d_i) /
+// Q_i(d_i)), i.e. when u * Q < P with u = draw(iteration, 16 + i); at the
+// first rejection the emitted token is drawn from max(0, P_i - Q_i), after k
+// acceptances from P_k (draw(iteration, 32)), so every emitted token follows
+// the target's distribution.  Those draws walk the row in index order with
+// exact 2^-60 fixed-point masses (the sums do not depend on the order of the
+// partial sums).
+constexpr int SS_NT = 1024;
+
+QW_DEV uint32_t draw24(unsigned long long seed, unsigned long long counter) {
+    return (uint32_t)(splitmix64(seed ^ splitmix64(counter)) >> 40);
+}
+// P(x) of a nucleus-truncated, renormalised row
+QW_DEV float nucleus_p(const float* p, const SpDesc& d, int x) {
+    const float v = p[x];
+    const float kv = __uint_as_float(d.key);
+    const bool in = !d.found || v > kv || (v == kv && x <= d.tie_idx);
+    return in ? __fdiv_rn(v, d.renorm) : 0.f;
+}
+QW_DEV unsigned long long fx60(float v) {
+    return v <= 0.f ? 0ull : __double2ull_rn((double)v * 1152921504606846976.0);
+}
+
+// Accept / residual draw / emit / roll back (one CTA).  pt: the target's k + 1
+// softmax rows and nuclei (rows of the verify), pd / dd: the draft's k rows.
+__global__ void __launch_bounds__(SS_NT, 1) spec_sampled_accept_kernel(SpecCtl* c, const float* pt, const SpDesc* dt,
+                                                                        const float* pd, const SpDesc* dd, int V,
+                                                                        int* verify_in, int* draft_in2, int* out,
+                                                                        int* t_seq, int* d_seq,
+                                                                        volatile int* host_flag) {
+    __shared__ int s_nacc, s_mode, s_tok;
+    __shared__ unsigned long long s_scan[SS_NT / 32];
+    __shared__ unsigned long long s_R;
+    pdl_wait();
+    pdl_launch_dependents();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (c->done) {  // the same value in every thread
+        if (tid == 0) {
+            host_flag[0] = c->done;
+            host_flag[1] = c->emitted;
+        }
+        return;
+    }
+    const unsigned long long it64 = (unsigned long long)c->iters * 64ull;
+    if (tid == 0) {
+        const int n = c->n_eff;
+        int n_acc = 0;
+        while (n_acc < n) {
+            const int d = verify_in[1 + n_acc];
+            const float P = nucleus_p(pt + (size_t)n_acc * V, dt[n_acc], d);
+            const float Q = nucleus_p(pd + (size_t)n_acc * V, dd[n_acc], d);
+            const float u = (float)draw24(c->seed, it64 + 16ull + (unsigned long long)n_acc) * (1.0f / 16777216.0f);
+            if (__fmul_rn(u, Q) < P)
+                ++n_acc;
+            else
+                break;
+        }
+        s_nacc = n_acc;
+        s_mode = n_acc < n ? 0 : 1;  // 0: residual of row n_acc, 1: the target's row n_acc
+        s_tok = -1;
+    }
+    __syncthreads();
+    const int row = s_nacc;
+    const uint32_t U = draw24(c->seed, it64 + 32ull);
+    const int chunk = (V + SS_NT - 1) / SS_NT;
+    const int x0 = min(V, tid * chunk), x1 = min(V, x0 + chunk);
+    const float* P = pt + (size_t)row * V;
+    const SpDesc dP = dt[row];
+    for (int attempt = 0; attempt < 2; ++attempt) {
+        const int mode = s_mode;
+        const bool resid = mode == 0;
+        const float* Q = pd + (size_t)(resid ? row : 0) * V;
+        const SpDesc dQ = dd[resid ? row : 0];
+        auto w = [&](int x) -> unsigned long long {
+            const float pv = nucleus_p(P, dP, x);
+            return resid ? fx60(fmaxf(__fsub_rn(pv, nucleus_p(Q, dQ, x)), 0.f)) : fx60(pv);
+        };
+        unsigned long long sum = 0ull;
+        for (int x = x0; x < x1; ++x) sum += w(x);
+        unsigned long long inc = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned long long y = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += y;
+        }
+        if (lane == 31) s_scan[warp] = inc;
+        __syncthreads();
+        if (warp == 0) {
+            unsigned long long v = s_scan[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned long long y = __shfl_up_sync(0xffffffffu, v, o);
+                if (lane >= o) v += y;
+            }
+            s_scan[lane] = v;
+            if (lane == 31) s_R = v;
+        }
+        __syncthreads();
+        const unsigned long long R = s_R;
+        if (R == 0ull) {
+            // no residual mass (the rows agree to rounding): draw from the target row
+            __syncthreads();
+            if (tid == 0) s_mode = 1;
+            __syncthreads();
+            if (!resid) break;
+            continue;
+        }
+        const unsigned long long tgt = (R >> 24) * U + (((R & 0xFFFFFFull) * U) >> 24);  // floor(R U / 2^24) < R
+        const unsigned long long excl = (warp > 0 ? s_scan[warp - 1] : 0ull) + inc - sum;
+        if (sum > 0ull && excl <= tgt && tgt < excl + sum) {
+            unsigned long long acc = excl;
+            for (int x = x0; x < x1; ++x) {
+                acc += w(x);
+                if (acc > tgt) {
+                    s_tok = x;
+                    break;
+                }
+            }
+        }
+        __syncthreads();
+        break;
+    }
+    if (tid != 0) return;
+    const int n = c->n_eff, n_acc = s_nacc;
+    const int bonus = s_tok < 0 ? 0 : s_tok;
+    c->proposed += n;
+    c->iters += 1;
+    c->accepted += n_acc;
+    bool stop = false;
+    for (int i = 0; i < n_acc && !stop; ++i) {
+        const int t = verify_in[1 + i];
+        if (c->emitted >= c->max_new) {
+            stop = true;
+        } else if (in_list(c->eos_t, c->n_eos_t, t)) {
+            c->finish = 1;
+            stop = true;
+        } else {
+            out[c->emitted++] = t;
+        }
+    }
+    if (!stop && c->emitted >= c->max_new) stop = true;
+    if (!stop && in_list(c->eos_t, c->n_eos_t, bonus)) {
+        c->finish = 1;
+        stop = true;
+    }
+    if (stop) {
+        c->done = 1;
+    } else {
+        out[c->emitted++] = bonus;
+        const int keep = c->plen + c->emitted - 1;
+        *t_seq = keep;
+        *d_seq = keep - 1;
+        draft_in2[0] = verify_in[n_acc];
+        draft_in2[1] = bonus;
+        verify_in[0] = bonus;
+        c->slot = 0;
+        c->n_eff = c->k;
+        if (c->emitted >= c->max_new) c->done = 1;
+    }
+    host_flag[0] = c->done;
+    host_flag[1] = c->emitted;
+}
+
 template <typename K, typename... Args>
 cudaError_t launch1(K kernel, cudaStream_t st, Args... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(1);
     cfg.blockDim = dim3(32);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+// launch1 with a whole-CTA block (the speculative-sampling accept kernel)
+template <typename K, typename... Args>
+cudaError_t launch_cta(K kernel, int threads, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(threads);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -180,10 +363,22 @@ struct SpecState {
     int forced_cap = 0;
     int* host_flag = nullptr;  // mapped pinned [done, emitted]
     std::vector<cudaEvent_t> ev;
+    // speculative sampling: the draft's k and the target's k + 1 softmax rows,
+    // their nuclei (draft first), the draft pick's token; the captured parameters
+    bool sampled = false;
+    float temperature = 0.f, top_p = 1.f;
+    uint64_t seed = 0;
+    float* probs = nullptr;
+    SpDesc* desc = nullptr;
+    int* stok = nullptr;
+    size_t probs_cap = 0;
     ~SpecState() {
         for (auto g : {gD, gV, gA})
             if (g) cudaGraphExecDestroy(g);
         if (ctl) cudaFree(ctl);
+        if (probs) cudaFree(probs);
+        if (desc) cudaFree(desc);
+        if (stok) cudaFree(stok);
         if (forced) cudaFree(forced);
         if (host_flag) cudaFreeHost(host_flag);
         for (auto e : ev) cudaEventDestroy(e);
@@ -251,30 +446,86 @@ void spec_generate_dev(qw_model* t, qw_model* d, const SpecRequest& r, std::vect
     int* flag = S->host_flag;
     const int* gate = &S->ctl->done;
 
+    const bool sampled = r.temperature > 0.f;
+    const int V = t->vocab_l;
+    if (sampled) {
+        if (t->vocab_l != t->cfg.vocab || d->vocab_l != V)
+            throw Error(QW_ERR_UNSUPPORTED, "speculative sampling needs the whole vocabulary on one rank for target and draft");
+        ensure_workspace(d, r.n_prompt, 8);
+        const size_t need_p = (size_t)(2 * r.k + 1) * V;
+        if (S->probs_cap < need_p) {
+            if (S->probs) cudaFree(S->probs);
+            if (S->desc) cudaFree(S->desc);
+            S->probs = nullptr;
+            S->desc = nullptr;
+            QW_CUDA(cudaMalloc(&S->probs, need_p * sizeof(float)));
+            QW_CUDA(cudaMalloc(&S->desc, (size_t)(2 * 8 + 1) * sizeof(SpDesc)));
+            S->probs_cap = need_p;
+        }
+        if (!S->stok) QW_CUDA(cudaMalloc(&S->stok, 64));
+    }
     const bool stale = S->draft != d || S->k != r.k || S->tgen != tw.generation || S->dgen != dw.generation ||
-                       S->tc != tc || S->dc != dc || !S->gD;
+                       S->tc != tc || S->dc != dc || !S->gD || S->sampled != sampled ||
+                       (sampled && (S->temperature != r.temperature || S->top_p != r.top_p || S->seed != r.seed));
     if (stale) {
         for (cudaGraphExec_t* g : {&S->gD, &S->gV, &S->gA})
             if (*g) {
                 cudaGraphExecDestroy(*g);
                 *g = nullptr;
             }
+        float* probs_d = S->probs;                      // [k][V]
+        float* probs_t = S->probs + (size_t)r.k * V;  // [k + 1][V]
+        SpDesc* desc_d = S->desc;
+        SpDesc* desc_t = S->desc + 8;
+        // one row's softmax and nucleus (and, for the draft, the pick) on the shared control block
+        auto sample_row = [&](const bf16* logits, float* probs, SpDesc* desc, int ctr_base, bool draw) {
+            SampleArgs sa;
+            std::memset(&sa, 0, sizeof(sa));
+            sa.logits = logits;
+            sa.V = V;
+            sa.cfg.temperature = r.temperature;
+            sa.cfg.top_p = r.top_p;
+            sa.cfg.seed = r.seed;
+            sa.probs = probs;
+            sa.token_out = S->stok;
+            sa.ctrl = dw.sctrl;
+            sa.err = t->d_err;
+            sa.ctr_iter = &S->ctl->iters;
+            sa.ctr_base = ctr_base;
+            sa.desc_out = desc;
+            sa.no_draw = draw ? 0 : 1;
+            sa.gate = gate;
+            QW_CUDA(launch_sample(sa, st));
+        };
         S->gD = capture(st, [&] {
-            forward_dev(d, dc, draft_in2, 2, 1, false, dw.argmax, st, nullptr, nullptr, nullptr, gate);
+            forward_dev(d, dc, draft_in2, 2, 1, sampled, dw.argmax, st, nullptr, nullptr, nullptr, gate);
             for (int j = 0; j < r.k; ++j) {
-                QW_CUDA(launch1(spec_pick_kernel, st, S->ctl, (const int*)dw.argmax, (const int*)S->forced, verify_in,
-                                draft_in));
+                if (sampled) sample_row(dw.logits, probs_d + (size_t)j * V, desc_d + j, j, true);
+                QW_CUDA(launch1(spec_pick_kernel, st, S->ctl, sampled ? (const int*)S->stok : (const int*)dw.argmax,
+                                (const int*)S->forced, verify_in, draft_in));
                 if (j + 1 < r.k)
-                    forward_dev(d, dc, draft_in, 1, 1, false, dw.argmax, st, nullptr, nullptr, nullptr, gate);
+                    forward_dev(d, dc, draft_in, 1, 1, sampled, dw.argmax, st, nullptr, nullptr, nullptr, gate);
             }
         });
         S->gV = capture(st, [&] {
-            forward_dev(t, tc, verify_in, r.k + 1, 2, false, tw.argmax, st, nullptr, nullptr, nullptr, gate);
+            forward_dev(t, tc, verify_in, r.k + 1, 2, sampled, tw.argmax, st, nullptr, nullptr, nullptr, gate);
+            if (sampled)
+                for (int j = 0; j <= r.k; ++j)
+                    sample_row(tw.logits + (size_t)j * V, probs_t + (size_t)j * V, desc_t + j, 0, false);
         });
         S->gA = capture(st, [&] {
-            QW_CUDA(launch1(spec_accept_kernel, st, S->ctl, (const int*)tw.argmax, verify_in, draft_in2, tw.out,
-                            tc->d_seq_len, dc->d_seq_len, (volatile int*)flag));
+            if (sampled)
+                QW_CUDA(launch_cta(spec_sampled_accept_kernel, SS_NT, st, S->ctl, (const float*)probs_t,
+                                   (const SpDesc*)desc_t, (const float*)probs_d, (const SpDesc*)desc_d, V, verify_in,
+                                   draft_in2, tw.out, tc->d_seq_len, dc->d_seq_len, (volatile int*)flag));
+            else
+                QW_CUDA(launch1(spec_accept_kernel, st, S->ctl, (const int*)tw.argmax, verify_in, draft_in2, tw.out,
+                                tc->d_seq_len, dc->d_seq_len, (volatile int*)flag));
         });
+        S->sampled = sampled;
+        S->temperature = r.temperature;
+        S->top_p = r.top_p;
+        S->seed = r.seed;
         S->draft = d;
         S->k = r.k;
         S->tgen = tw.generation;
@@ -288,7 +539,7 @@ void spec_generate_dev(qw_model* t, qw_model* d, const SpecRequest& r, std::vect
     h.max_new = max_new;
     h.k = r.k;
     h.plen = r.n_prompt;
-    h.force_p = r.force_p;
+    h.force_p = sampled ? 0.f : r.force_p;
     h.seed = r.seed;
     h.n_forced = r.forced ? r.n_forced : 0;
     h.n_eos_t = (int)std::min<size_t>(r.eos_target.size(), 8);
@@ -316,10 +567,31 @@ void spec_generate_dev(qw_model* t, qw_model* d, const SpecRequest& r, std::vect
     }
     // prefill: target (last-row logits -> leader), draft (no logits needed)
     QW_CUDA(cudaEventRecord(S->ev[0], st));
-    forward_dev(t, tc, tw.ids, r.n_prompt, 1, false, tw.argmax, st, nullptr, nullptr, nullptr, nullptr);
-    forward_dev(d, dc, dw.ids, r.n_prompt, 0, false, dw.argmax, st, nullptr, nullptr, nullptr, nullptr);
-    QW_CUDA(launch1(spec_init_kernel, st, S->ctl, (const int*)tw.argmax, verify_in, draft_in2, (const int*)dw.ids,
-                    dc->d_seq_len, tw.out, (volatile int*)flag));
+    forward_dev(t, tc, tw.ids, r.n_prompt, 1, sampled, tw.argmax, st, nullptr, nullptr, nullptr, nullptr);
+    // the draft prefills all but the last prompt token: the first iteration's 2-row
+    // draft step runs that token (as every later iteration's 2-row step reruns the
+    // last kept token), so each draft KV row after the prompt's first n - 1 comes
+    // from the decode step's arithmetic
+    if (r.n_prompt > 1)
+        forward_dev(d, dc, dw.ids, r.n_prompt - 1, 0, false, dw.argmax, st, nullptr, nullptr, nullptr, nullptr);
+    if (sampled) {
+        // the first token is drawn from the target's distribution after the prompt (draw counter 2^40)
+        SampleArgs sa;
+        std::memset(&sa, 0, sizeof(sa));
+        sa.logits = tw.logits;
+        sa.V = V;
+        sa.cfg.temperature = r.temperature;
+        sa.cfg.top_p = r.top_p;
+        sa.cfg.seed = r.seed;
+        sa.probs = S->probs;
+        sa.token_out = S->stok;
+        sa.ctrl = dw.sctrl;
+        sa.err = t->d_err;
+        sa.counter = 1ull << 40;
+        QW_CUDA(launch_sample(sa, st));
+    }
+    QW_CUDA(launch1(spec_init_kernel, st, S->ctl, sampled ? (const int*)S->stok : (const int*)tw.argmax, verify_in,
+                    draft_in2, (const int*)dw.ids, dc->d_seq_len, tw.out, (volatile int*)flag));
     QW_CUDA(cudaEventRecord(S->ev[1], st));
 
     int launched = 0;

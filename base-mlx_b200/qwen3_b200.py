@@ -135,6 +135,8 @@ SIGNATURES = {
     "qw_sample_topp": [P, I, ctypes.c_float, ctypes.c_float, ctypes.c_uint64, ctypes.c_uint64, P, P, P],
     "qw_spec_generate": [P, P, U32P, I, I, I, ctypes.c_float, ctypes.c_uint64, U32P, I, U32P, I, U32P,
                          ctypes.POINTER(I), ctypes.POINTER(SpecStats)],
+    "qw_spec_generate_sampled": [P, P, U32P, I, I, I, ctypes.c_float, ctypes.c_float, ctypes.c_uint64, U32P, I,
+                                 U32P, ctypes.POINTER(I), ctypes.POINTER(SpecStats)],
     "qw_quantized_matmul": [P, P, P, P, P, I, I, I, I, I, P],
     "qw_quantized_matmul_argmax_static": [P, P, P, P, P, P, I, I, I, I, I, P],
 }
@@ -456,6 +458,28 @@ def speculative_generate(target: Qwen3, draft: Qwen3, prompt, max_new: int, k: i
         ep, ne = None, 0
     check(lib().qw_spec_generate(target.h, draft.h, pp, len(p), max_new, k, float(force_p), seed & ((1 << 64) - 1),
                                  fp, nf, ep, ne, out.ctypes.data_as(U32P), ctypes.byref(n), ctypes.byref(st)))
+    res = GenerationResult([int(t) for t in out[:n.value]], len(p), st.completion_tokens,
+                           "stop" if st.finish_reason == 1 else "length", st.prefill_ms, st.total_ms)
+    return res, st
+
+
+def speculative_generate_sampled(target: Qwen3, draft: Qwen3, prompt, max_new: int, k: int = 3,
+                                 temperature: float = 0.7, top_p: float = 0.95, seed: int = 0, eos=None):
+    """Speculative sampling (rejection rule over the sampled pick's distributions;
+    the reference falls back to plain sampling here, speculative.rs:65-69).
+    Returns (GenerationResult, SpecStats)."""
+    p, pp = _u32(prompt)
+    out = np.empty(max(max_new, 1) + 1, np.uint32)
+    n = ctypes.c_int()
+    st = SpecStats()
+    if eos is not None:
+        e, ep = _u32(eos)
+        ne = len(e)
+    else:
+        ep, ne = None, 0
+    check(lib().qw_spec_generate_sampled(target.h, draft.h, pp, len(p), max_new, k, float(temperature), float(top_p),
+                                         seed & ((1 << 64) - 1), ep, ne, out.ctypes.data_as(U32P), ctypes.byref(n),
+                                         ctypes.byref(st)))
     res = GenerationResult([int(t) for t in out[:n.value]], len(p), st.completion_tokens,
                            "stop" if st.finish_reason == 1 else "length", st.prefill_ms, st.total_ms)
     return res, st

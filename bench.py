@@ -525,7 +525,8 @@ def run_ours(args):
 
 
 def spec_measure(q, target, prompt, cfg4):
-    """Config 4: 4B target + 0.6B draft, k=4, forced acceptance p in {0, 0.5, 0.8, 1}."""
+    """Config 4: 4B target + 0.6B draft, k=4, forced acceptance p in {0, 0.5, 0.8, 1}; and speculative
+    sampling (temperature 0.7, top-p 0.95) against plain sampled decode."""
     draft = q.Qwen3.init_random(dict(CFG_0_6B), SEED + 1, norm_mode="ones", device=0)
     plain = target.generate_greedy(prompt, DECODE_TOKENS)
     out = {"k": 4, "plain_decode_tok_s": round((plain.completion_tokens - 1) / (plain.decode_ms / 1e3), 2)}
@@ -540,6 +541,21 @@ def spec_measure(q, target, prompt, cfg4):
                         "draft_ms_mean": round(st.draft_ms_mean, 3), "verify_ms_mean": round(st.verify_ms_mean, 3),
                         "accept_ms_mean": round(st.accept_ms_mean, 3)}
         out[f"p{p}"]["speedup_vs_plain"] = round(out[f"p{p}"]["tok_s"] / out["plain_decode_tok_s"], 3)
+    # speculative sampling (temperature 0.7, top-p 0.95) against plain sampled decode
+    ps = target.generate_sampled(prompt, DECODE_TOKENS, temperature=0.7, top_p=0.95, seed=SEED, eos=[1 << 30])
+    plain_s = (ps.completion_tokens - 1) / (ps.decode_ms / 1e3)
+    q.speculative_generate_sampled(target, draft, prompt, DECODE_TOKENS, k=4, temperature=0.7, top_p=0.95, seed=7,
+                                   eos=[1 << 30])
+    res, st = q.speculative_generate_sampled(target, draft, prompt, DECODE_TOKENS, k=4, temperature=0.7, top_p=0.95,
+                                             seed=7, eos=[1 << 30])
+    dec_ms = st.total_ms - st.prefill_ms
+    tok_s = (res.completion_tokens - 1) / (dec_ms / 1e3)
+    out["sampled_t0.7_p0.95"] = {"tok_s": round(tok_s, 2), "plain_sampled_tok_s": round(plain_s, 2),
+                                 "speedup_vs_plain_sampled": round(tok_s / plain_s, 3), "iters": st.iters,
+                                 "accepted": st.accepted, "proposed": st.proposed,
+                                 "draft_ms_mean": round(st.draft_ms_mean, 3),
+                                 "verify_ms_mean": round(st.verify_ms_mean, 3),
+                                 "accept_ms_mean": round(st.accept_ms_mean, 3)}
     draft.close()
     return out
 

@@ -181,6 +181,24 @@ QW_API int qw_generate_greedy(qw_model* m, const uint32_t* prompt_host, int n_pr
                               const uint32_t* eos, int n_eos, uint32_t* out_host, int* n_out,
                               qw_gen_stats* stats);
 
+/* Speculative sampling (temperature > 0): the reference falls back to plain
+ * sampled decoding there (speculative.rs:65-69); this runs the rejection rule
+ * on the device over the sampled pick's distributions (engine.rs:203-263:
+ * softmax of logits / temperature, top-p nucleus).  The first token and each
+ * of the k drafted tokens per iteration are drawn like qw_generate_sampled;
+ * drafted token i is accepted with probability min(1, P_target / P_draft) of
+ * that token; at the first rejection the emitted token is drawn from
+ * max(0, P_target - P_draft), after k acceptances from the target's next row,
+ * so every token follows the target's distribution.  Draws come from the
+ * counter-based generator seeded by `seed` (iteration t, slot i: draft pick
+ * 64t + i, acceptance 64t + 16 + i, residual / bonus 64t + 32; first token
+ * 2^40).  temperature <= 0 runs qw_spec_generate's greedy loop.  Target and
+ * draft must hold the whole vocabulary (no vocabulary-parallel lm_head). */
+QW_API int qw_spec_generate_sampled(qw_model* target, qw_model* draft, const uint32_t* prompt_host, int n_prompt,
+                                    int max_new, int k, float temperature, float top_p, uint64_t seed,
+                                    const uint32_t* eos, int n_eos, uint32_t* out_host, int* n_out,
+                                    qw_spec_stats* stats);
+
 /* Batched greedy generation (benchmark config 5 at batch 8; the reference
  * serves one request at a time, model.rs:21-108, so this has no single
  * reference counterpart: it is generate_text's greedy loop, engine.rs:149-201,
