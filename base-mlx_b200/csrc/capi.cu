@@ -175,6 +175,20 @@ int qw_model_tp_attach(qw_model* m, const void* uid, int rank, int size) {
     });
 }
 
+int qw_tp_exchange_handle(qw_model* m, void* out, size_t bytes) {
+    return guard([&] {
+        need(m && out, "model/out");
+        qw::tp_push_handle(m, out, bytes);
+    });
+}
+
+int qw_tp_exchange_open(qw_model* m, const void* handles, size_t bytes) {
+    return guard([&] {
+        need(m && handles, "model/handles");
+        qw::tp_push_open(m, handles, bytes);
+    });
+}
+
 // speculative.rs:40-54
 int qw_check_compatible(const qw_model* t, const qw_model* d) {
     return guard([&] {

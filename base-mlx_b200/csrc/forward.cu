@@ -73,6 +73,29 @@ void qmm(qw_model* m, QmmArgs a, cudaStream_t st) {
         QW_CUDA(launch_qgemm(a, st, m->num_sms));
 }
 
+// o_proj / down_proj and, under tensor parallelism, the sum of the ranks'
+// partials into the residual stream: over peer memory for decode rows (the
+// GEMV pushes its partial rows to every rank, one small kernel sums them), else
+// an NCCL all-reduce and a residual add.
+void tp_reduce_gemv(qw_model* m, QmmArgs& a, int S, cudaStream_t st) {
+    Workspace& w = m->ws;
+    if (m->tp_size > 1 && S <= TP_PUSH_ROWS && tp_push_ready(m)) {
+        a.epi = EPI_F32_PUSH;
+        if (a.M <= 8 && qgemv_fits(a)) {
+            tp_push_args(m, a.push);
+            QW_CUDA(launch_qgemv(a, st, true, m->num_sms));
+            QW_CUDA(launch_tp_push_reduce(m, w.x, S, st));
+            return;
+        }
+        a.epi = EPI_F32;
+    }
+    qmm(m, a, st);
+    if (m->tp_size > 1) {
+        tp_allreduce_sum_f32(m, w.f32, (size_t)S * m->cfg.hidden, st);
+        QW_CUDA(launch_resid_add_f32(w.x, w.f32, S * m->cfg.hidden, st));
+    }
+}
+
 }  // namespace
 
 void forward_dev(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_mode, bool store_logits,
@@ -148,11 +171,7 @@ void forward_dev(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_m
             a.seg[0] = seg_of(L.o, tp ? (void*)w.f32 : (void*)w.x, H);
             a.nseg = 1;
             a.epi = tp ? EPI_F32 : EPI_RESID;
-            qmm(m, a, st);
-            if (tp) {
-                tp_allreduce_sum_f32(m, w.f32, (size_t)S * H, st);
-                QW_CUDA(launch_resid_add_f32(w.x, w.f32, S * H, st));
-            }
+            tp_reduce_gemv(m, a, S, st);
         }
         if (m->trace)
             QW_CUDA(cudaMemcpyAsync(m->trace_mid + (size_t)l * S * H, w.x, (size_t)S * H * 2,
@@ -176,11 +195,7 @@ void forward_dev(qw_model* m, qw_cache* c, const int* d_ids, int S, int logits_m
             a.seg[0] = seg_of(L.down, tp ? (void*)w.f32 : (void*)w.x, H);
             a.nseg = 1;
             a.epi = tp ? EPI_F32 : EPI_RESID;
-            qmm(m, a, st);
-            if (tp) {
-                tp_allreduce_sum_f32(m, w.f32, (size_t)S * H, st);
-                QW_CUDA(launch_resid_add_f32(w.x, w.f32, S * H, st));
-            }
+            tp_reduce_gemv(m, a, S, st);
         }
         if (m->trace)
             QW_CUDA(cudaMemcpyAsync(m->trace + (size_t)(l + 1) * S * H, w.x, (size_t)S * H * 2,

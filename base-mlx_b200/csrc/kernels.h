@@ -14,6 +14,7 @@ enum Epi : int {
     EPI_SWIGLU = 2,  // y = bf16(bf16(g*bf16(sigmoid(g))) * u), g/u = bf16(gate/up acc)
     EPI_LOGITS = 3,  // bf16 logits (optional store) + fused argmax per row
     EPI_F32 = 4,     // y_f32 = acc (tensor-parallel partial sums)
+    EPI_F32_PUSH = 5,  // tensor parallel, decode: acc stored into every rank's receive slot (TpPush)
 };
 
 // One quantized linear segment [n rows x K] (MLX layout).
@@ -25,6 +26,23 @@ struct QSeg {
     int n;
     int ldy;
     int rb0;            // first row block of this segment in the launch grid
+};
+
+// Tensor-parallel reduction over peer memory (decode rows <= TP_PUSH_ROWS): a
+// GEMV with EPI_F32_PUSH writes its fp32 partial of output (row m, feature f)
+// into every rank q's exchange block, recv[q][((e & 1) * n + self) *
+// TP_PUSH_ROWS + m][f] (e = *epoch + 1, the reduction's epoch); each CTA then
+// arrives on a local counter (acquire-release, GPU scope) and the last one
+// stores e into every rank's flag for this source rank with a system-scope
+// release (the arrivals chain every CTA's stores before it).
+constexpr int TP_PUSH_MAX = 8;   // ranks
+constexpr int TP_PUSH_ROWS = 8;  // rows per reduction
+struct TpPush {
+    float* recv[TP_PUSH_MAX];     // each rank's receive region (this rank's own at [self])
+    unsigned* flag[TP_PUSH_MAX];  // each rank's flag for this source rank
+    const unsigned* epoch;        // this rank's completed reductions
+    unsigned* ctr;                // CTA arrivals of the GEMV (zero between launches)
+    int n, self, H;
 };
 
 struct QmmArgs {
@@ -43,6 +61,7 @@ struct QmmArgs {
     int store_logits;
     int amax_row_offset;               // global index of row 0 (vocab-parallel shards)
     int* err;
+    TpPush push;                       // EPI_F32_PUSH
 };
 
 // Decode / verify path: M <= 8.

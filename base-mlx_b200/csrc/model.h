@@ -84,6 +84,7 @@ struct Workspace {
 };
 
 struct TpComm;  // tensor-parallel communicator (NCCL), defined in tp.cu
+struct TpPeer;  // peer-memory exchange block for the decode reductions, defined in tp.cu
 struct MkState;  // persistent decode kernel: packed weights + sync words, defined in decode_mk.cu
 
 }  // namespace qw
@@ -110,6 +111,7 @@ struct qw_model {
     std::map<std::string, qw::TensorRef> tensors;
     qw::Workspace ws;
     qw::TpComm* tp = nullptr;
+    qw::TpPeer* tpp = nullptr;
     std::vector<qw_cache*> caches;  // live caches (freed with the model)
     qw_cache* gen_cache = nullptr;  // cache used by the generate entry points
     void* spec_state = nullptr;     // speculative-decoding graphs (spec.cu)
@@ -217,5 +219,12 @@ void tp_attach(qw_model* m, const void* unique_id, int rank, int size);
 void tp_allreduce_sum_f32(qw_model* m, float* buf, size_t count, cudaStream_t st);
 void tp_allreduce_max_u64(qw_model* m, unsigned long long* buf, size_t count, cudaStream_t st);
 void tp_destroy(qw_model* m);
+// peer-memory reductions (decode): this rank's IPC handle, the ranks' handles
+// opened, whether the push path is on, GEMV arguments, the reducing kernel
+void tp_push_handle(qw_model* m, void* out, size_t bytes);
+void tp_push_open(qw_model* m, const void* handles, size_t bytes);
+bool tp_push_ready(const qw_model* m);
+void tp_push_args(qw_model* m, TpPush& a);
+cudaError_t launch_tp_push_reduce(qw_model* m, bf16* x, int S, cudaStream_t st);
 
 }  // namespace qw

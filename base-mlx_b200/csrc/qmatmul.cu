@@ -450,6 +450,21 @@ __global__ void __launch_bounds__(NW * 32) qgemv_kernel(const QmmArgs a) {
         else
             store_out(a, si, a.epi, row, 0, col, v[0][e], 0.f);
     }
+    if (a.epi == EPI_F32_PUSH) {
+        // arrival (acquire-release): the last CTA's system-scope release then
+        // carries every CTA's peer stores to the ranks' flags
+        __syncwarp();
+        if (lane == 0) {
+            unsigned old;
+            asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.push.ctr) : "memory");
+            if (old == gridDim.x - 1) {
+                const unsigned ep = *a.push.epoch + 1u;
+                for (int q = 0; q < a.push.n; ++q)
+                    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.push.flag[q]), "r"(ep) : "memory");
+                *a.push.ctr = 0u;
+            }
+        }
+    }
 }
 
 // ===========================================================================

@@ -20,6 +20,12 @@ QW_DEV void store_out(const QmmArgs& a, int si, int epi, int row, int feat, int 
     const size_t idx = (size_t)col * sg.ldy + row;
     if (epi == EPI_F32) {
         reinterpret_cast<float*>(sg.y)[idx] = v0;
+    } else if (epi == EPI_F32_PUSH) {
+        // this rank's partial into every rank's receive slot (peer stores over NVLink)
+        const TpPush& p = a.push;
+        const unsigned e = *p.epoch + 1u;
+        const size_t off = ((size_t)((e & 1u) * p.n + p.self) * TP_PUSH_ROWS + col) * p.H + row;
+        for (int q = 0; q < p.n; ++q) p.recv[q][off] = v0;
     } else if (epi == EPI_RESID) {
         bf16* y = reinterpret_cast<bf16*>(sg.y);
         y[idx] = f2bf(__fadd_rn(bf2f(y[idx]), bfr(v0)));

@@ -10,6 +10,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <cstdlib>
 #include <cstring>
 
 #include "model.h"
@@ -88,7 +89,170 @@ void tp_allreduce_max_u64(qw_model* m, unsigned long long* buf, size_t count, cu
     check_nccl(m->tp, m->tp->allreduce(buf, buf, count, ncclUint64, ncclMax, m->tp->comm, st), "ncclAllReduce(max)");
 }
 
+// ---- reductions over peer memory (decode) ------------------------------------
+// The o_proj / down_proj reduction of a decode or verify step without a library
+// collective: the GEMV's epilogue stores its fp32 partial rows straight into
+// every rank's exchange block (EPI_F32_PUSH, plain stores over NVLink through
+// CUDA IPC mappings) and its last CTA raises the reduction's epoch flag on every
+// rank; tp_push_reduce_kernel then waits (bounded) until every rank's flag
+// reached the epoch, sums the partials in rank order -- every rank computes the
+// same sum -- and adds them to the residual stream.  Receive slots alternate by
+// epoch parity: a rank writes epoch e only after its own reduction e - 1
+// completed, which needed every rank's epoch e - 1 data, pushed after that
+// rank had finished reading epoch e - 2 from the same slot.
+struct TpPeer {
+    void* block = nullptr;  // this rank's exchange block
+    size_t bytes = 0, off_flags = 0, off_epoch = 0;
+    void* peer[TP_PUSH_MAX] = {};  // every rank's block as mapped here (own block at [rank])
+    bool opened[TP_PUSH_MAX] = {};
+    bool ready = false;
+};
+
+static void tp_peer_layout(const qw_model* m, size_t& recv_bytes, size_t& off_flags, size_t& off_epoch,
+                           size_t& total) {
+    recv_bytes = (size_t)2 * m->tp_size * TP_PUSH_ROWS * m->cfg.hidden * sizeof(float);
+    off_flags = (recv_bytes + 255) & ~(size_t)255;
+    off_epoch = off_flags + 256;
+    total = off_epoch + 256;
+}
+
+void tp_push_handle(qw_model* m, void* out, size_t bytes) {
+    if (m->tp_size < 2 || m->tp_size > TP_PUSH_MAX) throw Error(QW_ERR_UNSUPPORTED, "peer reductions need 2..8 ranks");
+    if (bytes < sizeof(cudaIpcMemHandle_t)) throw Error(QW_ERR_INVALID_ARG, "handle buffer smaller than 64 bytes");
+    QW_CUDA(cudaSetDevice(m->device));
+    if (!m->tpp) m->tpp = new TpPeer();
+    TpPeer* p = m->tpp;
+    if (!p->block) {
+        size_t recv;
+        tp_peer_layout(m, recv, p->off_flags, p->off_epoch, p->bytes);
+        QW_CUDA(cudaMalloc(&p->block, p->bytes));
+        QW_CUDA(cudaMemset(p->block, 0, p->bytes));
+        QW_CUDA(cudaDeviceSynchronize());
+    }
+    cudaIpcMemHandle_t h;
+    QW_CUDA(cudaIpcGetMemHandle(&h, p->block));
+    std::memcpy(out, &h, sizeof(h));
+}
+
+void tp_push_open(qw_model* m, const void* handles, size_t bytes) {
+    TpPeer* p = m->tpp;
+    if (!p || !p->block) throw Error(QW_ERR_INVALID_ARG, "call qw_tp_exchange_handle first");
+    const int n = m->tp_size;
+    if (bytes < (size_t)n * sizeof(cudaIpcMemHandle_t)) throw Error(QW_ERR_INVALID_ARG, "one 64-byte handle per rank");
+    QW_CUDA(cudaSetDevice(m->device));
+    for (int q = 0; q < n; ++q) {
+        if (q == m->tp_rank) {
+            p->peer[q] = p->block;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, (const char*)handles + (size_t)q * sizeof(h), sizeof(h));
+        void* ptr = nullptr;
+        QW_CUDA(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+        p->peer[q] = ptr;
+        p->opened[q] = true;
+    }
+    // measured on Qwen3-32B decode: 86.4 vs 89.7 tok/s (NCCL) at 2 GPUs, 113.9 vs
+    // 116.1 at 4 -- NCCL stays the default; QW_TP_PUSH=1 selects the peer path
+    const char* e = std::getenv("QW_TP_PUSH");
+    p->ready = e && std::atoi(e) == 1;
+}
+
+bool tp_push_ready(const qw_model* m) { return m->tpp && m->tpp->ready; }
+
+void tp_push_args(qw_model* m, TpPush& a) {
+    TpPeer* p = m->tpp;
+    std::memset(&a, 0, sizeof(a));
+    a.n = m->tp_size;
+    a.self = m->tp_rank;
+    a.H = m->cfg.hidden;
+    for (int q = 0; q < a.n; ++q) {
+        a.recv[q] = reinterpret_cast<float*>(p->peer[q]);
+        a.flag[q] = reinterpret_cast<unsigned*>((char*)p->peer[q] + p->off_flags) + a.self;
+    }
+    a.epoch = reinterpret_cast<const unsigned*>((char*)p->block + p->off_epoch);
+    a.ctr = reinterpret_cast<unsigned*>((char*)p->block + p->off_epoch) + 32;  // its own 128-byte line
+}
+
+namespace {
+
+QW_DEV unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// x[m][f] = bf16(x + bf16(sum over ranks q, in rank order, of partial_q[m][f]))
+// once every rank's flag reached this reduction's epoch.
+__global__ void __launch_bounds__(512) tp_push_reduce_kernel(bf16* x, const float* recv, const unsigned* flags,
+                                                             unsigned* epoch, int n, int S, int H, int* err) {
+    pdl_wait();
+    const unsigned e = *epoch + 1u;
+    {
+        unsigned long long t0;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+        while (true) {
+            bool mine = true;
+            if (threadIdx.x < n) mine = (int)(ld_acquire_sys(flags + threadIdx.x) - e) >= 0;
+            if (__syncthreads_and(mine)) break;
+            // thread 0 keeps the clock; its decision reaches every thread
+            bool late = false;
+            if (threadIdx.x == 0) {
+                unsigned long long t;
+                asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+                late = t - t0 > 2000000000ull;
+                if (late && err) atomicOr(err, QW_DERR_TIMEOUT);
+            }
+            if (__syncthreads_or(late)) break;
+        }
+    }
+    __syncthreads();
+    const float* base = recv + (size_t)(e & 1u) * n * TP_PUSH_ROWS * H;
+    for (int i = threadIdx.x; i < S * H; i += blockDim.x) {
+        const int mrow = i / H, f = i - mrow * H;
+        float sum = 0.f;
+        for (int q = 0; q < n; ++q) sum += __ldcg(base + ((size_t)q * TP_PUSH_ROWS + mrow) * H + f);
+        x[(size_t)mrow * H + f] = f2bf(__fadd_rn(bf2f(x[(size_t)mrow * H + f]), bfr(sum)));
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+    if (threadIdx.x == 0) *epoch = e;
+}
+
+}  // namespace
+
+cudaError_t launch_tp_push_reduce(qw_model* m, bf16* x, int S, cudaStream_t st) {
+    TpPeer* p = m->tpp;
+    if (S < 1 || S > TP_PUSH_ROWS) return cudaErrorInvalidValue;
+    const int H = m->cfg.hidden;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(512);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, tp_push_reduce_kernel, x, (const float*)p->block,
+                              (const unsigned*)((char*)p->block + p->off_flags),
+                              (unsigned*)((char*)p->block + p->off_epoch), m->tp_size, S, H, m->d_err);
+}
+
+static void tp_peer_free(qw_model* m) {
+    TpPeer* p = m->tpp;
+    if (!p) return;
+    cudaSetDevice(m->device);
+    cudaDeviceSynchronize();
+    for (int q = 0; q < TP_PUSH_MAX; ++q)
+        if (p->opened[q]) cudaIpcCloseMemHandle(p->peer[q]);
+    if (p->block) cudaFree(p->block);
+    delete p;
+    m->tpp = nullptr;
+}
+
 void tp_destroy(qw_model* m) {
+    tp_peer_free(m);
     if (!m->tp) return;
     if (m->tp->comm) m->tp->destroy(m->tp->comm);
     delete m->tp;

@@ -114,6 +114,8 @@ SIGNATURES = {
     "qw_model_export_tensor": [P, ctypes.c_char_p, P, ctypes.c_size_t],
     "qw_model_stream": [P, ctypes.POINTER(P)],
     "qw_model_tp_attach": [P, P, I, I],
+    "qw_tp_exchange_handle": [P, P, ctypes.c_size_t],
+    "qw_tp_exchange_open": [P, P, ctypes.c_size_t],
     "qw_tp_unique_id": [P, ctypes.c_size_t],
     "qw_check_compatible": [P, P],
     "qw_cache_new": [P, I, ctypes.POINTER(P)],
@@ -429,10 +431,24 @@ def tp_share_unique_id(rank: int, group=None, make_id=None) -> bytes:
     return bytes(uid)
 
 
-def tp_init(model: "Qwen3", rank: int, size: int, group=None) -> None:
+def tp_init(model: "Qwen3", rank: int, size: int, group=None, peer_reduce: bool = True) -> None:
     """Attach the NCCL communicator of a tensor-parallel group of `size` ranks
-    (one process per GPU, model loaded with tp_rank=rank, tp_size=size)."""
+    (one process per GPU, model loaded with tp_rank=rank, tp_size=size); with
+    peer_reduce, also map every rank's exchange block (CUDA IPC handles shared
+    over the host group) so that decode-step reductions run over peer memory."""
+    import torch.distributed as dist
     model.tp_attach(tp_share_unique_id(rank, group), rank, size)
+    if not peer_reduce:
+        return
+    buf = ctypes.create_string_buffer(64)
+    check(lib().qw_tp_exchange_handle(model.h, buf, 64))
+    handles = [None] * size
+    dist.all_gather_object(handles, bytes(buf.raw), group=group)
+    joined = b"".join(handles)
+    if len(joined) != 64 * size:
+        raise Inference(-1, "tensor-parallel exchange handles are malformed")
+    jb = ctypes.create_string_buffer(joined, len(joined))
+    check(lib().qw_tp_exchange_open(model.h, jb, len(joined)))
 
 
 def check_compatible(target: Qwen3, draft: Qwen3) -> None:

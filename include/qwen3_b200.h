@@ -122,6 +122,21 @@ QW_API int qw_tp_unique_id(void* out, size_t bytes);
  * model loaded with tp_size > 1.  Must be called on every rank before forward. */
 QW_API int qw_model_tp_attach(qw_model* m, const void* nccl_unique_id, int rank, int size);
 
+/* Tensor parallelism without a library collective on the decode path: each
+ * rank allocates an exchange block and returns its CUDA IPC handle (64 bytes)
+ * with qw_tp_exchange_handle; after the ranks have shared their handles over
+ * the host (rank order, size x 64 bytes), qw_tp_exchange_open maps every
+ * peer's block.  With QW_TP_PUSH=1 set at open time the o_proj / down_proj
+ * reductions of steps of up to 8 rows then run over peer memory: the GEMV
+ * stores its fp32 partial rows into
+ * every rank's block and raises an epoch flag there, one small kernel per rank
+ * waits for the flags (bounded), sums the partials in rank order and adds them
+ * to the residual (NCCL keeps the prefill reductions and the lm_head argmax).
+ * Measured slightly slower than NCCL on Qwen3-32B decode at 2 and 4 GPUs, so
+ * NCCL is the default.  No reference counterpart. */
+QW_API int qw_tp_exchange_handle(qw_model* m, void* handle_out, size_t bytes);
+QW_API int qw_tp_exchange_open(qw_model* m, const void* handles, size_t bytes);
+
 QW_API int qw_check_compatible(const qw_model* target, const qw_model* draft);
 
 /* ---- KV cache --------------------------------------------------------- */

@@ -102,6 +102,18 @@ CASES = {
 @pytest.mark.skipif(_ngpu() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("case", sorted(CASES))
 def test_tp2_matches_single_gpu(case, tmp_path):
+    _tp2_case(case, tmp_path)
+
+
+@pytest.mark.skipif(_ngpu() < 2, reason="needs two GPUs")
+def test_tp2_peer_memory_reductions_match_single_gpu(tmp_path, monkeypatch):
+    """The decode reductions over peer memory (QW_TP_PUSH=1: the GEMV pushes its
+    partial rows to every rank, one kernel per rank sums them) instead of NCCL."""
+    monkeypatch.setenv("QW_TP_PUSH", "1")
+    _tp2_case("0.6b_4layers", tmp_path)
+
+
+def _tp2_case(case, tmp_path):
     cfg, plen, tol = CASES[case]
     port = _free_port()
     ctx = mp.get_context("spawn")
