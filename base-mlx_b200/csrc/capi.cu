@@ -664,7 +664,12 @@ int qw_quantized_matmul(const void* x, const void* w, const void* scales, const 
         a.epi = qw::EPI_STORE;
         cudaStream_t st = (cudaStream_t)stream;
         if (M <= 8 && qw::qgemv_fits(a)) {
-            QW_CUDA(qw::launch_qgemv(a, st, false, sms));
+            // programmatic launch: the GEMV's blocks start while the previous
+            // kernel drains and prefetch their weights into L2; every read of
+            // x, w, scales and biases into the SMs and every write of y follows
+            // the wait on that kernel
+            a.weights_after_wait = 1;
+            QW_CUDA(qw::launch_qgemv(a, st, true, sms));
         } else if (qw::qgemm_tc_supported(a) && !legacy_prefill_gemm()) {
             // fp16 copy of x for the tensor-core kernel
             const size_t bytes = qw::qgemm_tc_scratch_bytes(M, K);
@@ -724,8 +729,9 @@ extern "C" int qw_quantized_matmul_argmax_static(const void* x, const void* w, c
             throw qw::Error(QW_ERR_INVALID_ARG, "qw_quantized_matmul_argmax_static: M * ceil(N/16) = " +
                                                     std::to_string(slots) + " exceeds the static scratch of " +
                                                     std::to_string(QW_STATIC_AMAX_SLOTS) + " slots");
-        int dev = 0;
+        int dev = 0, sms = 0;
         QW_CUDA(cudaGetDevice(&dev));
+        QW_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
         unsigned long long* scratch = static_amax(dev);
         qw::QmmArgs a;
         std::memset(&a, 0, sizeof(a));
@@ -749,7 +755,8 @@ extern "C" int qw_quantized_matmul_argmax_static(const void* x, const void* w, c
                                                     " does not fit the GEMV's shared-memory staging (220 KB); "
                                                     "largest K: " + std::to_string(qw::qgemv_max_k(M)));
         cudaStream_t st = (cudaStream_t)stream;
-        QW_CUDA(qw::launch_qgemv(a, st, false, 0));
+        a.weights_after_wait = 1;  // programmatic launch with L2 hints only before the wait
+        QW_CUDA(qw::launch_qgemv(a, st, true, sms));
         QW_CUDA(qw::launch_amax_finalize(scratch, qw::qgemv_row_blocks(a), M, argmax_dev, nullptr, st));
     });
 }

@@ -191,6 +191,20 @@ QW_DEV void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 QW_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+// L2 prefetch hint for the 16-byte-aligned interior of [p, p + bytes) in
+// pieces of at most 32 KB.  A hint only: reads issued after it still see
+// every write that reaches L2 before them, so it may run ahead of the
+// programmatic-launch wait even for data the previous kernel writes.
+QW_DEV void prefetch_l2_range(const void* p, size_t bytes) {
+    uintptr_t b = ((uintptr_t)p + 15) & ~(uintptr_t)15;
+    const uintptr_t e = ((uintptr_t)p + bytes) & ~(uintptr_t)15;
+    while (b < e) {
+        const uint32_t n = (uint32_t)((e - b) < 32768 ? (e - b) : 32768);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(b), "r"(n) : "memory");
+        b += n;
+    }
+}
 template <int N>
 QW_DEV void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");

@@ -62,6 +62,11 @@ struct QmmArgs {
     int amax_row_offset;               // global index of row 0 (vocab-parallel shards)
     int* err;
     TpPush push;                       // EPI_F32_PUSH
+    // 0: the weights are static (model weights), so the GEMV copies them into
+    // shared memory before the programmatic-launch wait.  1: the previous
+    // kernel on the stream may have written them (the standalone op), so only
+    // L2 prefetch hints run before the wait and the copies after it.
+    int weights_after_wait;
 };
 
 // Decode / verify path: M <= 8.

@@ -46,6 +46,7 @@
 #include "kernels.h"
 #include "qmm_epi.cuh"
 #include "smem_attr.h"
+#include "tma_map.h"
 
 namespace qw {
 namespace {
@@ -116,15 +117,6 @@ QW_DEV bool tc_wait(uint64_t* bar, uint32_t parity) {
 
 QW_DEV void tc_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-// 2-D TMA tensor load into this CTA's own shared memory only, from this GPU's
-// own memory; completion counted on `bar` in bytes.
-QW_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
-        : "memory");
 }
 QW_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 QW_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -398,44 +390,15 @@ cudaError_t launch_pdl(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStre
     return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
-// cuTensorMapEncodeTiled, resolved through the runtime (no link-time libcuda).
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return (EncodeTiledFn) nullptr;
-        return reinterpret_cast<EncodeTiledFn>(p);
-    }();
-    return fn;
-}
-
-// 2-D map over a row-major [rows, cols] tensor with a (box_cols x box_rows) box.
-bool make_map(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* base, long long cols, long long rows,
-              int box_cols, int box_rows, CUtensorMapSwizzle sw) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return false;
-    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)cols * esize};
-    const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
-    const cuuint32_t estr[2] = {1, 1};
-    return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
-              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-// Weight-side maps depend only on (pointer, rows, K): cached across calls.
+// Weight-side maps depend only on (weight, scale and bias pointers, rows, K):
+// cached across calls.
 struct SegMaps {
     CUtensorMap w, s, b;
 };
 bool seg_maps(const QSeg& sg, int K, SegMaps& out) {
     static std::mutex mu;
-    static std::map<std::tuple<const void*, int, int>, SegMaps> cache;
-    const auto key = std::make_tuple((const void*)sg.w, sg.n, K);
+    static std::map<std::tuple<const void*, const void*, const void*, int, int>, SegMaps> cache;
+    const auto key = std::make_tuple((const void*)sg.w, (const void*)sg.s, (const void*)sg.b, sg.n, K);
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find(key);
     if (it != cache.end()) {

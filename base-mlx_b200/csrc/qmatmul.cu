@@ -22,12 +22,16 @@
 // so the activations are permuted the same way (permute16) when they are
 // staged into shared memory.
 #include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include <cuda_fp16.h>
 
 #include "kernels.h"
 #include "qmm_epi.cuh"
 #include "smem_attr.h"
+#include "tma_map.h"
 
 namespace qw {
 namespace {
@@ -206,9 +210,26 @@ __global__ void __launch_bounds__(NW * 32) qgemv_kernel(const QmmArgs a) {
         tl[0] = Tile{sg.w, sg.s, sg.b, lrb * 16, sg.n};
     }
 
-    // Weights are static: put the whole slab in flight before waiting on the
-    // previous kernel (programmatic dependent launch).  Rows past n are left
-    // unloaded; their results are never stored.
+    // Static weights: the whole slab goes in flight before the wait on the
+    // previous kernel (programmatic dependent launch).  Weights the previous
+    // kernel may write (a.weights_after_wait): L2 prefetch hints before the
+    // wait, the copies after it.  Rows past n are left unloaded; their results
+    // are never stored.
+    const bool after_wait = a.weights_after_wait != 0;
+    if (after_wait) {
+        if ((int)threadIdx.x < RT) {
+            const Tile& tt = tl[threadIdx.x];
+            const int nr = min(16, tt.nrows - tt.row0);
+            if (nr > 0) {
+                prefetch_l2_range(tt.w + (size_t)tt.row0 * KW, (size_t)nr * KW * 4);
+                prefetch_l2_range(tt.s + (size_t)tt.row0 * KG, (size_t)nr * KG * 2);
+                prefetch_l2_range(tt.b + (size_t)tt.row0 * KG, (size_t)nr * KG * 2);
+            }
+        }
+        // trigger only after the wait: one programmatic launch ahead at most
+        pdl_wait();
+        pdl_launch_dependents();
+    }
     if (KG % 8 == 0) {
         // every stage has 8 groups = 16 chunks of 16 bytes per row: fixed
         // per-thread (row, chunk) slots, advanced by 64 words per stage
@@ -268,9 +289,10 @@ __global__ void __launch_bounds__(NW * 32) qgemv_kernel(const QmmArgs a) {
             Bsm[r * L.ngp + gl] = bv;
         }
     }
-
-    pdl_launch_dependents();
-    pdl_wait();
+    if (!after_wait) {
+        pdl_launch_dependents();
+        pdl_wait();
+    }
 
     if (a.norm_w) {
         // sum of squares of every activation row in one pass
@@ -610,8 +632,8 @@ __global__ void __launch_bounds__(128) qgemm_kernel(const QmmArgs a) {
 // weight rows, scales and biases (MLX layout, rows contiguous) arrive by
 // 16-byte asynchronous copies spread over all threads (tracked per slot by an
 // mbarrier every thread arrives on) into a ring of `ns` tile slots, so a CTA keeps ns tiles in flight while it computes;
-// weights do not depend on the previous kernel, so the first ns tiles are
-// issued before the programmatic-launch wait.  Activations are staged once per
+// static weights: the first ns tiles are issued before the programmatic-launch
+// wait (with a.weights_after_wait only their L2 prefetch hints are).  Activations are staged once per
 // CTA (fragment order, as in qgemv_kernel).  Warp w takes the tile's groups
 // w, w + 16, ...; the 16 warps' partial sums meet in shared memory in warp
 // order (double-buffered: one CTA barrier per tile).
@@ -679,13 +701,29 @@ __global__ void __launch_bounds__(GS_NW * 32, 1) qgemv_stream_kernel(const __gri
         fence_mbar_init();
     }
     __syncthreads();
-    for (int i = 0; i < ns; ++i) {
-        const int tile = blockIdx.x + i * gridDim.x;
-        if (tile < ntiles) issue(tile, i);
+    auto issue_first = [&]() {
+        for (int i = 0; i < ns; ++i) {
+            const int tile = blockIdx.x + i * gridDim.x;
+            if (tile < ntiles) issue(tile, i);
+        }
+    };
+    if (a.weights_after_wait) {
+        // weights the previous kernel may write: L2 hints only before the wait
+        const int tile = blockIdx.x + (int)threadIdx.x * gridDim.x;
+        if ((int)threadIdx.x < ns && tile < ntiles) {
+            const int row0 = tile * 16, nr = min(16, sg.n - row0);
+            prefetch_l2_range(sg.w + (size_t)row0 * KW, (size_t)nr * KW * 4);
+            prefetch_l2_range(sg.s + (size_t)row0 * KG, (size_t)nr * KG * 2);
+            prefetch_l2_range(sg.b + (size_t)row0 * KG, (size_t)nr * KG * 2);
+        }
+        pdl_wait();
+        pdl_launch_dependents();
+        issue_first();
+    } else {
+        issue_first();
+        pdl_launch_dependents();
+        pdl_wait();
     }
-
-    pdl_launch_dependents();
-    pdl_wait();
 
     {
         // activations and even / odd group sums (uniform trip count: every lane
@@ -783,6 +821,292 @@ __global__ void __launch_bounds__(GS_NW * 32, 1) qgemv_stream_kernel(const __gri
     }
 }
 
+// ===========================================================================
+// Warp-ring decode GEMV for the standalone op (M <= 8, one output segment,
+// plain bf16 store or the lm_head's logits with per-tile argmax keys, no
+// RMSNorm prologue, K a multiple of 512): persistent CTAs of WR_NW warps, one
+// per SM.  CTA c takes the 16-row tiles [c*T/C, (c+1)*T/C); the CTA's
+// granules -- one granule is a stage of 8 groups (512 inputs) of one tile,
+// tile-major -- are split into WR_NW equal contiguous ranges, one per warp.
+// A warp streams its range through its own ring of `ns` slots, one TMA box
+// per operand: the 16 rows' weight words as two 128-byte-wide boxes with the
+// 128-byte swizzle, then 16 x 8 scales and 16 x 8 biases; lane 0 issues the
+// four loads, one mbarrier per slot counts the bytes.  Tile row pi(i) =
+// (i & 8) | (i & 3) << 1 | (i >> 2) & 1 feeds mma row i, which with the
+// swizzle makes every fragment load conflict-free.  A tile the warp covers
+// whole is stored straight from its accumulators; a tile split between warps
+// leaves one partial per warp in shared memory, summed in warp order by its
+// first warp after one CTA barrier.  Against qgemv_kernel this removes the
+// per-tile activation staging, copy issue, CTA barriers and cross-warp
+// reduction, which bound that kernel's issue rate on wide outputs.
+// ===========================================================================
+constexpr int WR_NW = 16;
+constexpr int WR_NS_MAX = 4;
+constexpr int WR_SLOT = 5120;  // two 2 KB weight boxes, 256 B scales, 256 B biases, pad to 1 KB
+
+struct WrMaps {
+    CUtensorMap w, s, b;
+};
+
+struct WrLayout {
+    unsigned off_xsum, off_bar, off_part, off_slots, total;
+};
+
+// offsets from the dynamic shared memory base rounded up to 1 KB; total
+// includes that rounding slack
+__host__ __device__ inline WrLayout wr_layout(int KG, int M, int ns) {
+    WrLayout L;
+    L.off_xsum = (unsigned)KG * M * XS_BLOCK_WORDS * 4u;
+    L.off_bar = L.off_xsum + (unsigned)KG * 16u * 4u;
+    L.off_part = L.off_bar + WR_NW * WR_NS_MAX * 8u;
+    L.off_slots = (L.off_part + WR_NW * 2u * 512u + 1023u) & ~1023u;
+    L.total = L.off_slots + (unsigned)(WR_NW * ns * WR_SLOT) + 1024u;
+    return L;
+}
+
+QW_DEV int wr_row(int i) { return (i & 8) | ((i & 3) << 1) | ((i >> 2) & 1); }
+
+// Outputs of one 16-row tile from a warp's fragment sums v (lane g, t: mma
+// rows g and g + 8 = tile rows wr_row(g), wr_row(g) + 8; columns 2t, 2t + 1):
+// bf16 stores, or for EPI_LOGITS the bf16-rounded logits (stored if asked)
+// and the tile's per-column maximum key.  Called by all 32 lanes.
+QW_DEV void wr_store_tile(const QmmArgs& a, int tile, const float (&v)[4], int lane) {
+    const QSeg& sg = a.seg[0];
+    const int g = lane >> 2, t = lane & 3;
+    const int rbase = tile * 16 + wr_row(g);
+    if (a.epi == EPI_LOGITS) {
+        unsigned long long best[2] = {0ull, 0ull};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int row = rbase + 8 * (e >> 1);
+            const int col = 2 * t + (e & 1);
+            if (row < sg.n && col < a.M) {
+                const float l = bfr(v[e]);
+                if (a.store_logits) reinterpret_cast<bf16*>(sg.y)[(size_t)col * sg.ldy + row] = f2bf(l);
+                best[e & 1] = umax64(best[e & 1], amax_key(l, (uint32_t)(row + a.amax_row_offset)));
+            }
+        }
+#pragma unroll
+        for (int cp = 0; cp < 2; ++cp)
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) best[cp] = umax64(best[cp], __shfl_xor_sync(0xffffffffu, best[cp], o));
+        if (g == 0) {
+#pragma unroll
+            for (int cp = 0; cp < 2; ++cp)
+                if (2 * t + cp < a.M) a.amax_partial[(size_t)tile * a.M + 2 * t + cp] = best[cp];
+        }
+        return;
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const int row = rbase + 8 * (e >> 1);
+        const int col = 2 * t + (e & 1);
+        if (row < sg.n && col < a.M) reinterpret_cast<bf16*>(sg.y)[(size_t)col * sg.ldy + row] = f2bf(v[e]);
+    }
+}
+
+__global__ void __launch_bounds__(WR_NW * 32, 1) qgemv_wr_kernel(const __grid_constant__ QmmArgs a,
+                                                                  const __grid_constant__ WrMaps maps, int ns,
+                                                                  int ntiles) {
+    constexpr int NT = WR_NW * 32;
+    extern __shared__ __align__(1024) unsigned char wr_smem_raw[];
+    unsigned char* smraw = reinterpret_cast<unsigned char*>(((uintptr_t)wr_smem_raw + 1023) & ~(uintptr_t)1023);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int M = a.M, KG = a.K / 64, S = KG / 8;
+    const WrLayout L = wr_layout(KG, M, ns);
+    uint32_t* xs = reinterpret_cast<uint32_t*>(smraw);
+    float* xsum = reinterpret_cast<float*>(smraw + L.off_xsum);  // [KG][even, odd][8 columns]
+    uint64_t* bar0 = reinterpret_cast<uint64_t*>(smraw + L.off_bar);
+    uint64_t* bars = bar0 + warp * WR_NS_MAX;
+    float* part = reinterpret_cast<float*>(smraw + L.off_part);  // [warp][first, last][4][32]
+    unsigned char* ring = smraw + L.off_slots + (size_t)warp * ns * WR_SLOT;
+
+    // the CTA's tiles [t0, t1) and this warp's granules [gb, ge) of them
+    const int t0 = (int)((long long)blockIdx.x * ntiles / gridDim.x);
+    const int t1 = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
+    const int gc = (t1 - t0) * S;
+    const int gb = (int)((long long)warp * gc / WR_NW), ge = (int)((long long)(warp + 1) * gc / WR_NW);
+
+    // granule j (CTA-local) into slot (j - gb) % ns: lane 0 only
+    auto issue = [&](int j) {
+        const int tl = j / S, s = j - tl * S;
+        const int row0 = (t0 + tl) * 16, k = (j - gb) % ns;
+        unsigned char* slot = ring + (size_t)k * WR_SLOT;
+        mbar_arrive_expect_tx(&bars[k], 4096u + 512u);
+        tma_load_2d(slot, &maps.w, s * 64, row0, &bars[k]);
+        tma_load_2d(slot + 2048, &maps.w, s * 64 + 32, row0, &bars[k]);
+        tma_load_2d(slot + 4096, &maps.s, s * 8, row0, &bars[k]);
+        tma_load_2d(slot + 4352, &maps.b, s * 8, row0, &bars[k]);
+    };
+    if ((int)threadIdx.x < WR_NW * WR_NS_MAX) {
+        mbar_init(&bar0[threadIdx.x], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    const int npre = min(ns, ge - gb);
+    if (a.weights_after_wait) {
+        // weights the previous kernel may write: L2 hints only before the wait
+        if (lane == 0) {
+            for (int i = 0; i < npre; ++i) {
+                const int j = gb + i, tl = j / S, s = j - tl * S, row0 = (t0 + tl) * 16;
+                tma_prefetch_2d(&maps.w, s * 64, row0);
+                tma_prefetch_2d(&maps.w, s * 64 + 32, row0);
+                tma_prefetch_2d(&maps.s, s * 8, row0);
+                tma_prefetch_2d(&maps.b, s * 8, row0);
+            }
+        }
+        pdl_wait();
+        pdl_launch_dependents();
+        if (lane == 0)
+            for (int i = 0; i < npre; ++i) issue(gb + i);
+    } else {
+        if (lane == 0)
+            for (int i = 0; i < npre; ++i) issue(gb + i);
+        pdl_launch_dependents();
+        pdl_wait();
+    }
+
+    {
+        // activations and even / odd group sums (uniform trip count: every lane
+        // takes part in the quad shuffles)
+        const int units = KG * M * 4;
+        for (int u0 = 0; u0 < units; u0 += NT) {
+            const int u = u0 + threadIdx.x;
+            float se = 0.f, so = 0.f;
+            int gl = 0, m = 0, tt = 0;
+            if (u < units) {
+                gl = u / (M * 4);
+                const int rem = u - gl * M * 4;
+                m = rem >> 2;
+                tt = rem & 3;
+                stage16_f16(a.x + (size_t)m * a.ldx + gl * 64 + 16 * tt, nullptr, 1.f,
+                            xs + (size_t)(gl * M + m) * XS_BLOCK_WORDS + tt * 8, se, so);
+            }
+            se += __shfl_xor_sync(0xffffffffu, se, 1);
+            se += __shfl_xor_sync(0xffffffffu, se, 2);
+            so += __shfl_xor_sync(0xffffffffu, so, 1);
+            so += __shfl_xor_sync(0xffffffffu, so, 2);
+            if (u < units && tt == 0) {
+                xsum[gl * 16 + m] = se;
+                xsum[gl * 16 + 8 + m] = so;
+            }
+        }
+    }
+    __syncthreads();
+
+    const uint32_t* xb = xs + g * XS_BLOCK_WORDS + t * 8;
+    const int xstride = M * XS_BLOCK_WORDS;
+    const bool has_col = g < M;
+    const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+    // this lane's weight words in a slot: tile row r = wr_row(g) (and r + 8,
+    // 1 KB further), words 2t, 2t + 1 of group q at 16-byte chunk
+    // (2 (q & 3) + t / 2) ^ (r & 7) of the row in box q / 4
+    const int r = wr_row(g);
+    uint32_t woff[4];
+#pragma unroll
+    for (int qq = 0; qq < 4; ++qq) woff[qq] = (uint32_t)(r * 128 + (((2 * qq + (t >> 1)) ^ (r & 7)) << 4) + ((t & 1) << 3));
+    const int first_tile = gb / S;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f}, bacc[4] = {0.f, 0.f, 0.f, 0.f};
+    int j = gb;
+    for (; j < ge; ++j) {
+        const int k = (j - gb) % ns;
+        const bool landed = mbar_wait_bounded(&bars[k], (uint32_t)(((j - gb) / ns) & 1));
+        if (!__all_sync(0xffffffffu, landed)) {
+            if (lane == 0 && a.err) atomicOr(a.err, QW_DERR_TIMEOUT);
+            break;
+        }
+        const int tl = j / S, s = j - tl * S;
+        const unsigned char* sp = ring + (size_t)k * WR_SLOT;
+        const uint16_t* Ssm = reinterpret_cast<const uint16_t*>(sp + 4096);
+        const uint16_t* Bsm = Ssm + 128;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const int gl = s * 8 + q;
+            uint4 be = make_uint4(0u, 0u, 0u, 0u), bo = be;
+            if (has_col) {
+                const uint4* p = reinterpret_cast<const uint4*>(xb + gl * xstride);
+                be = p[0];
+                bo = p[1];
+            }
+            const float2 xe = *reinterpret_cast<const float2*>(xsum + gl * 16 + 2 * t);
+            const float2 xo = *reinterpret_cast<const float2*>(xsum + gl * 16 + 8 + 2 * t);
+            const float xt0 = xe.x + xo.x, xt1 = xe.y + xo.y;
+            const unsigned char* wbox = sp + (q >> 2) * 2048 + woff[q & 3];
+            const uint2 wa = *reinterpret_cast<const uint2*>(wbox);
+            const uint2 wb = *reinterpret_cast<const uint2*>(wbox + 1024);
+            const uint32_t wa8x = wa.x >> 8, wb8x = wb.x >> 8, wa8y = wa.y >> 8, wb8y = wb.y >> 8;
+            float ce[4], co[4];
+            mma_f16(ce, nib_even(wa.x), nib_even(wb.x), nib_even(wa8x), nib_even(wb8x), be.x, be.y, zero4);
+            mma_f16(co, nib_odd(wa.x), nib_odd(wb.x), nib_odd(wa8x), nib_odd(wb8x), bo.x, bo.y, zero4);
+            mma_f16(ce, nib_even(wa.y), nib_even(wb.y), nib_even(wa8y), nib_even(wb8y), be.z, be.w, ce);
+            mma_f16(co, nib_odd(wa.y), nib_odd(wb.y), nib_odd(wa8y), nib_odd(wb8y), bo.z, bo.w, co);
+            // 2^24 undoes the subnormal encoding of the nibbles (exact: a power of two)
+            const float s0 = u16_to_f(Ssm[r * 8 + q]) * QW_NIB_SCALE;
+            const float s1 = u16_to_f(Ssm[(r + 8) * 8 + q]) * QW_NIB_SCALE;
+            const float b0 = u16_to_f(Bsm[r * 8 + q]), b1 = u16_to_f(Bsm[(r + 8) * 8 + q]);
+            acc[0] = fmaf(s0, fmaf(co[0], 0.0625f, ce[0]), acc[0]);
+            acc[1] = fmaf(s0, fmaf(co[1], 0.0625f, ce[1]), acc[1]);
+            acc[2] = fmaf(s1, fmaf(co[2], 0.0625f, ce[2]), acc[2]);
+            acc[3] = fmaf(s1, fmaf(co[3], 0.0625f, ce[3]), acc[3]);
+            bacc[0] = fmaf(b0, xt0, bacc[0]);
+            bacc[1] = fmaf(b0, xt1, bacc[1]);
+            bacc[2] = fmaf(b1, xt0, bacc[2]);
+            bacc[3] = fmaf(b1, xt1, bacc[3]);
+        }
+        // every lane has read the slot: refill it with the granule ns ahead
+        __syncwarp();
+        if (lane == 0 && j + ns < ge) {
+            fence_proxy_async_smem();
+            issue(j + ns);
+        }
+        if (s == S - 1 || j == ge - 1) {
+            float v[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                v[e] = acc[e] + bacc[e];
+                acc[e] = bacc[e] = 0.f;
+            }
+            if (tl * S >= gb && (tl + 1) * S <= ge) {
+                wr_store_tile(a, t0 + tl, v, lane);
+            } else {
+                float* pp = part + (size_t)(warp * 2 + (tl == first_tile ? 0 : 1)) * 128;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) pp[e * 32 + lane] = v[e];
+            }
+        }
+    }
+    if (j < ge) {
+        // timed out: let the loads still in flight into this warp's ring land
+        // (bounded) before the CTA can exit
+        for (int jj = j + 1; jj < min(ge, j + ns); ++jj)
+            (void)mbar_wait_bounded(&bars[(jj - gb) % ns], (uint32_t)(((jj - gb) / ns) & 1));
+    }
+    __syncthreads();
+    // tiles split between warps: the first covering warp (whose range ends
+    // inside the tile) sums the partials in warp order
+    if (ge > gb) {
+        const int tl = (ge - 1) / S;
+        if (!((tl + 1) * S <= ge) && gb <= tl * S) {
+            float v[4];
+            const float* pp = part + (size_t)(warp * 2 + (tl == first_tile ? 0 : 1)) * 128;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) v[e] = pp[e * 32 + lane];
+            // later warps whose ranges start inside the tile hold it as their first tile
+            for (int u = warp + 1; u < WR_NW; ++u) {
+                const int ub = (int)((long long)u * gc / WR_NW), ue = (int)((long long)(u + 1) * gc / WR_NW);
+                if (ub >= (tl + 1) * S) break;
+                if (ue > ub) {
+                    const float* up = part + (size_t)(u * 2) * 128;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) v[e] += up[e * 32 + lane];
+                }
+            }
+            wr_store_tile(a, t0 + tl, v, lane);
+        }
+    }
+}
+
 template <typename Kern>
 cudaError_t launch_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
                       const QmmArgs& a) {
@@ -849,6 +1173,71 @@ cudaError_t launch_qgemv_stream(const QmmArgs& a, cudaStream_t st, bool pdl, int
     return cudaLaunchKernelEx(&cfg, qgemv_stream_kernel, a, ns, ntiles);
 }
 
+// Tensor maps of one segment for the warp-ring GEMV (weights: 32-word x
+// 16-row boxes, 128-byte swizzle; scales, biases: 8 x 16 boxes), cached by
+// (weight, scale and bias pointers, rows, K).
+static bool wr_maps(const QSeg& sg, int K, WrMaps& out) {
+    static std::mutex mu;
+    static std::map<std::tuple<const void*, const void*, const void*, int, int>, WrMaps> cache;
+    const auto key = std::make_tuple((const void*)sg.w, (const void*)sg.s, (const void*)sg.b, sg.n, K);
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        out = it->second;
+        return true;
+    }
+    WrMaps m;
+    const int KW = K / 8, KG = K / 64;
+    if (!make_map(&m.w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, sg.w, KW, sg.n, 32, 16, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&m.s, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, sg.s, KG, sg.n, 8, 16, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map(&m.b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, sg.b, KG, sg.n, 8, 16, CU_TENSOR_MAP_SWIZZLE_NONE))
+        return false;
+    if (cache.size() > 4096) cache.clear();
+    cache.emplace(key, m);
+    out = m;
+    return true;
+}
+
+// The warp-ring GEMV when it applies (one segment, plain store or logits, no
+// norm, K a multiple of 512, 16-byte aligned operands, at least
+// WR_MIN_TILES_PER_SM tiles per SM, two ring slots per warp in shared
+// memory); cudaErrorNotSupported otherwise.
+constexpr int WR_MIN_TILES_PER_SM = 1;
+
+cudaError_t launch_qgemv_wr(const QmmArgs& a, cudaStream_t st, bool pdl, int num_sms) {
+    if (a.nseg != 1 || (a.epi != EPI_STORE && a.epi != EPI_LOGITS) || a.norm_w || a.M < 1 || a.M > 8 ||
+        a.K % 512 != 0 || num_sms < 1 || !encode_fn())
+        return cudaErrorNotSupported;
+    const QSeg& sg = a.seg[0];
+    if (sg.n < 1 || ((uintptr_t)sg.w | (uintptr_t)sg.s | (uintptr_t)sg.b) % 16 != 0) return cudaErrorNotSupported;
+    const int ntiles = (sg.n + 15) / 16;
+    if (ntiles < WR_MIN_TILES_PER_SM * num_sms) return cudaErrorNotSupported;
+    const int KG = a.K / 64;
+    int dev = 0, dev_smem = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&dev_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return e;
+    const long long fixed = (long long)wr_layout(KG, a.M, 0).total;
+    const int ns = (int)std::min<long long>(WR_NS_MAX, (dev_smem - fixed) / (long long)(WR_NW * WR_SLOT));
+    if (ns < 2) return cudaErrorNotSupported;
+    WrMaps maps;
+    if (!wr_maps(sg, a.K, maps)) return cudaErrorNotSupported;
+    const WrLayout L = wr_layout(KG, a.M, ns);
+    e = ensure_max_dyn_smem(qgemv_wr_kernel, (int)L.total);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(std::min(ntiles, num_sms));
+    cfg.blockDim = dim3(WR_NW * 32);
+    cfg.dynamicSmemBytes = L.total;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, qgemv_wr_kernel, a, maps, ns, ntiles);
+}
+
 int qgemv_row_blocks(const QmmArgs& a) {
     if (a.epi == EPI_SWIGLU) return (a.seg[0].n + 15) / 16;
     int nrb = 0;
@@ -877,8 +1266,12 @@ cudaError_t launch_qgemv(QmmArgs a, cudaStream_t st, bool pdl, int num_sms) {
     if (a.M < 1 || a.M > 8 || a.K <= 0 || a.K % 64 != 0 || a.nseg < 1 || a.nseg > 3)
         return cudaErrorInvalidValue;
     {
+        // long rows (K > 4096, few tiles per SM): the streaming GEMV; wide
+        // outputs: the warp-ring GEMV (measured faster on the Qwen3-4B shapes)
         const cudaError_t es = launch_qgemv_stream(a, st, pdl, num_sms);
         if (es != cudaErrorNotSupported) return es;
+        const cudaError_t ew = launch_qgemv_wr(a, st, pdl, num_sms);
+        if (ew != cudaErrorNotSupported) return ew;
     }
     const int RT = a.epi == EPI_SWIGLU ? 2 : 1;
     int nrb = 0;

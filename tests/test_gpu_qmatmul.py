@@ -56,7 +56,11 @@ def test_qmatmul_4b_shapes(M, K, N):
 
 
 @pytest.mark.parametrize("M,K,N", [(1, 64, 16), (3, 192, 40), (8, 320, 96), (9, 128, 48), (33, 256, 200),
-                                   (2048, 2560, 1024)])
+                                   (2048, 2560, 1024),
+                                   # warp-ring GEMV (>= one 16-row tile per SM, K a multiple of 512): ragged
+                                   # last tile, one-granule tiles with most warps idle, tiles split over many
+                                   # warps, eight columns
+                                   (3, 1024, 4741), (1, 512, 2400), (2, 4096, 2371), (8, 1536, 2376)])
 def test_qmatmul_edges(M, K, N):
     x, w, s, b = _case(M, K, N, seed=7 + M + K + N)
     ref = nm.bf16_round(x @ nm.dequantize(w, s, b).T)
@@ -86,3 +90,34 @@ def test_qmatmul_long_rows_32b_down_proj(M):
     x, w, s, b = _case(M, 25600, 160, seed=61 + M)
     ref = nm.bf16_round(x @ nm.dequantize(w, s, b).T)
     _check(_run_gpu(x, w, s, b), ref)
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 2560, 6144), (5, 9728, 2560), (1, 2560, 151936)])
+def test_qmatmul_inputs_written_by_previous_kernel(M, K, N):
+    """The standalone op starts while the previous kernel drains (programmatic
+    launch); weights, scales, biases and x written by that kernel must still be
+    the ones it reads.  Each call's operands are produced by a device copy
+    launched directly before it on the same stream, into buffers that held
+    other values, and consecutive calls write the same output."""
+    import torch
+    import qwen3_b200 as q
+    dev = torch.device("cuda:0")
+    cases = [_case(M, K, N, seed=400 + i) for i in range(3)]
+    srcs = [tuple(torch.from_numpy(a.view(dt)).to(dev) for a, dt in
+                  zip((nm.f32_to_bf16_bits(x), w, s, b), (np.int16, np.int32, np.int16, np.int16)))
+            for (x, w, s, b) in cases]
+    bufs = [torch.empty_like(t) for t in srcs[0]]
+    yt = torch.zeros((M, N), dtype=torch.int16, device=dev)
+    outs = []
+    stream = torch.cuda.current_stream()
+    for i in range(3):
+        # the weight words last: the kernel directly before the matmul writes them
+        for j in (0, 2, 3, 1):
+            bufs[j].copy_(srcs[i][j], non_blocking=True)
+        q.quantized_matmul(bufs[0].data_ptr(), bufs[1].data_ptr(), bufs[2].data_ptr(), bufs[3].data_ptr(),
+                           yt.data_ptr(), M, N, K, stream=stream.cuda_stream)
+        outs.append(yt.clone())
+    torch.cuda.synchronize()
+    for (x, w, s, b), yo in zip(cases, outs):
+        ref = nm.bf16_round(x @ nm.dequantize(w, s, b).T)
+        _check(nm.bf16_bits_to_f32(yo.cpu().numpy().view(np.uint16)), ref)
