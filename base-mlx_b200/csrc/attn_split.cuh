@@ -116,8 +116,10 @@ QW_DEV void split_body(const AttnArgs& a, SplitSmem<RMAX>& sm, const int kvh, co
         *reinterpret_cast<uint32_t*>(&sm.qs[r][2 * lane]) = pack_bf16x2(o[0], o[1]);
         *reinterpret_cast<uint32_t*>(&sm.qs[r][HALF + 2 * lane]) = pack_bf16x2(o[2], o[3]);
     }
-    // new positions inside this split: k_norm + RoPE, cache write, tile row
-    for (int p = max(off, j0) + warp; p < j1; p += NT / 32) {
+    // new positions inside this split: k_norm + RoPE, cache write, tile row;
+    // taken by the warps from the top down, so that with R + S <= 16 they run
+    // beside the query rows instead of after them
+    for (int p = max(off, j0) + (NT / 32 - 1 - warp); p < j1; p += NT / 32) {
         const int i = p - off;
         float o[4];
         norm_rope_row(a.k + (size_t)i * a.ldk + kvh * D, sm.kn, a.eps, sm.cs[i], sm.sn[i], lane, o);
