@@ -274,7 +274,11 @@ QW_API int qw_sample_topp(const void* logits, int vocab, float temperature, floa
 
 /* y[M,N] (bf16) = x[M,K] (bf16) . dequant(W)^T with W uint32 [N,K/8],
  * scales/biases bf16 [N,K/64]; device pointers; stream may be NULL (default
- * stream).  Only group_size 64 and bits 4 are supported. */
+ * stream).  Only group_size 64 and bits 4 are supported.  At M <= 8 the kernel
+ * is launched so that it may start while the previous kernel on the stream
+ * drains; it then only prefetches into L2 until that kernel has completed, so
+ * operands that kernel writes are read correctly.  The weights' tensor-map
+ * descriptors are cached per (w, scales, biases, N, K). */
 QW_API int qw_quantized_matmul(const void* x, const void* w, const void* scales, const void* biases,
                                void* y, int M, int N, int K, int group_size, int bits, void* stream);
 
