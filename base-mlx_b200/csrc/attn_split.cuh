@@ -7,7 +7,9 @@
 // not depend on the sequence length or on the number of rows in the launch (a
 // (k+1)-row verify equals k+1 single-row decodes bit for bit).  The item
 // serves the G = Hq / Hkv query heads of its kv head for the S new rows
-// (R = G S rows).  Its cached keys / values arrive by two bulk copies (the
+// (R = G S rows), or, when the grid has room for more items, a subset of
+// them: each row's arithmetic is the same either way, fewer rows per item
+// only shorten the item.  Its cached keys / values arrive by two bulk copies (the
 // rows are contiguous in the [kv head][position][128] cache), issued while
 // the CTA still waits for the other CTAs' q|k|v; the new positions' k / v
 // are normalised, rotated and written to the cache by the item that owns
@@ -86,15 +88,23 @@ QW_DEV void split_preload(const AttnArgs& a, SplitSmem<RMAX>& sm, int kvh, int s
     }
 }
 
-// One (kv head, split) item with NT threads (NT = 512).  `preloaded`: the
-// cached rows were issued by split_preload (else this issues them).
-template <int RMAX, int NT, typename Sync>
+// One (kv head, split) item with NT threads (NT = 512).  With SUB it serves
+// the query heads qh0_ .. qh0_ + nqh_ - 1 of the kv head's G (fewer than G when
+// the grid has room for more items: every row's arithmetic is the same either
+// way), its rows being the kv head's rows qh0 S .. (qh0 + nqh) S - 1 and its
+// merge counter counters[kvh G + qh0]; without SUB all G (qh0 = 0, merge
+// counter counters[kvh]), and the code is the plain per-kv-head item.
+// `preloaded`: the cached rows were issued by split_preload (else this issues
+// them).
+template <int RMAX, int NT, bool SUB, typename Sync>
 QW_DEV void split_body(const AttnArgs& a, SplitSmem<RMAX>& sm, const int kvh, const int split, const int nsplit,
-                       const int off, const int tid, Sync sync, bool preloaded) {
+                       const int off, const int qh0_, const int nqh_, const int tid, Sync sync, bool preloaded) {
     static_assert(NT == 512, "thread mapping assumes 512 threads");
     constexpr int RQ = (RMAX + 3) / 4;  // rows per row quarter
     const int lane = tid & 31, warp = tid >> 5;
-    const int S = a.S, G = a.Hq / a.Hkv, R = G * S;
+    const int S = a.S, G = a.Hq / a.Hkv;
+    const int qh0 = SUB ? qh0_ : 0, nqh = SUB ? nqh_ : G;
+    const int R = nqh * S;
     const int T = off + S;
     const int j0 = split * SPLIT_KEYS;
     const int j1 = min(j0 + SPLIT_KEYS, T);
@@ -109,7 +119,7 @@ QW_DEV void split_body(const AttnArgs& a, SplitSmem<RMAX>& sm, const int kvh, co
     // queries of the G heads: q_norm + RoPE (warp per row)
     for (int r = warp; r < R; r += NT / 32) {
         const int gi = r / S, i = r - gi * S;
-        const int h = kvh * G + gi, pos = off + i;
+        const int h = kvh * G + qh0 + gi, pos = off + i;
         float o[4];
         (void)pos;
         norm_rope_row(a.q + (size_t)i * a.ldq + h * D, sm.qn, a.eps, sm.cs[i], sm.sn[i], lane, o);
@@ -124,13 +134,16 @@ QW_DEV void split_body(const AttnArgs& a, SplitSmem<RMAX>& sm, const int kvh, co
         float o[4];
         norm_rope_row(a.k + (size_t)i * a.ldk + kvh * D, sm.kn, a.eps, sm.cs[i], sm.sn[i], lane, o);
         const uint32_t k01 = pack_bf16x2(o[0], o[1]), k23 = pack_bf16x2(o[2], o[3]);
+        // the cache rows: written once, by the item of the kv head's first query heads
         bf16* kd = a.kcache + ((size_t)kvh * a.max_pos + p) * D;
-        *reinterpret_cast<uint32_t*>(kd + 2 * lane) = k01;
-        *reinterpret_cast<uint32_t*>(kd + HALF + 2 * lane) = k23;
+        if (qh0 == 0) {
+            *reinterpret_cast<uint32_t*>(kd + 2 * lane) = k01;
+            *reinterpret_cast<uint32_t*>(kd + HALF + 2 * lane) = k23;
+        }
         *reinterpret_cast<uint32_t*>(&sm.kt[p - j0][2 * lane]) = k01;
         *reinterpret_cast<uint32_t*>(&sm.kt[p - j0][HALF + 2 * lane]) = k23;
         const uint2 vv = __ldcg(reinterpret_cast<const uint2*>(a.v + (size_t)i * a.ldv + kvh * D + 4 * lane));
-        *reinterpret_cast<uint2*>(a.vcache + ((size_t)kvh * a.max_pos + p) * D + 4 * lane) = vv;
+        if (qh0 == 0) *reinterpret_cast<uint2*>(a.vcache + ((size_t)kvh * a.max_pos + p) * D + 4 * lane) = vv;
         *reinterpret_cast<uint2*>(&sm.vt[p - j0][4 * lane]) = vv;
     }
     ATTN_STAMP(1);
@@ -219,7 +232,7 @@ QW_DEV void split_body(const AttnArgs& a, SplitSmem<RMAX>& sm, const int kvh, co
     // P.V: thread = (dimension pair dp, key eighth ke): keys 16 ke .. 16 ke + 15 in
     // order for rows in groups of 8; the eight key-eighth sums of a (row, dim) meet
     // in shared memory (the K tile's space) in key order.
-    const size_t pbase = ((size_t)kvh * nsplit + split) * RMAX;
+    const size_t pbase = ((size_t)kvh * nsplit + split) * RMAX + (size_t)qh0 * S;
     {
         const int nk = j1 - j0;
         const int dp = (warp & 1) * 32 + lane, ke = warp >> 1;
@@ -276,7 +289,8 @@ QW_DEV void split_body(const AttnArgs& a, SplitSmem<RMAX>& sm, const int kvh, co
     }
     sync();
     ATTN_STAMP(4);
-    if (tid == 0) sm.last = (atom_add_acq_rel(&a.counters[kvh], 1u) == (unsigned)(nsplit - 1));
+    unsigned* const counter = &a.counters[SUB ? kvh * G + qh0 : kvh];
+    if (tid == 0) sm.last = (atom_add_acq_rel(counter, 1u) == (unsigned)(nsplit - 1));
     sync();
     ATTN_STAMP(7);
     if (!sm.last) return;
@@ -288,7 +302,7 @@ QW_DEV void split_body(const AttnArgs& a, SplitSmem<RMAX>& sm, const int kvh, co
     constexpr int PMAX = 8;
     const int d = tid & (D - 1), rq = tid >> 7;
     auto fetch = [&](int s2, int r, float& m_, float& l_, float& o_) {
-        const float* pp = &a.part[(((size_t)kvh * nsplit + s2) * RMAX + r) * (D + 2)];
+        const float* pp = &a.part[(((size_t)kvh * nsplit + s2) * RMAX + qh0 * S + r) * (D + 2)];
         m_ = __ldcg(pp + D);
         l_ = __ldcg(pp + D + 1);
         o_ = __ldcg(pp + d);
@@ -306,7 +320,8 @@ QW_DEV void split_body(const AttnArgs& a, SplitSmem<RMAX>& sm, const int kvh, co
         float M = -INFINITY;
 #pragma unroll
         for (int u = 0; u < PMAX; ++u) M = fmaxf(M, m0[u]);
-        for (int s2 = PMAX; s2 < nsplit; ++s2) M = fmaxf(M, __ldcg(&a.part[(((size_t)kvh * nsplit + s2) * RMAX + r) * (D + 2) + D]));
+        for (int s2 = PMAX; s2 < nsplit; ++s2)
+            M = fmaxf(M, __ldcg(&a.part[(((size_t)kvh * nsplit + s2) * RMAX + qh0 * S + r) * (D + 2) + D]));
         float O = 0.f, L = 0.f;
 #pragma unroll
         for (int u = 0; u < PMAX; ++u) {
@@ -324,9 +339,9 @@ QW_DEV void split_body(const AttnArgs& a, SplitSmem<RMAX>& sm, const int kvh, co
             O = fmaf(wgt != 0.f ? o_ : 0.f, wgt, O);
         }
         const int gi = r / S, i = r - gi * S;
-        a.out[(size_t)i * a.ldo + (kvh * G + gi) * D + d] = f2bf(O / L);
+        a.out[(size_t)i * a.ldo + (kvh * G + qh0 + gi) * D + d] = f2bf(O / L);
     }
-    if (tid == 0) a.counters[kvh] = 0u;
+    if (tid == 0) *counter = 0u;
 }
 
 }  // namespace attn

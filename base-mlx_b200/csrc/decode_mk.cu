@@ -845,16 +845,36 @@ QW_DEV void gemv_epilogue(const MkArgs& a, const PhaseInfo& P, int Mx, const flo
 }
 
 // ---- attention items ---------------------------------------------------------
-// Items of one launch: (kv head, split) of the sequence, or, in a batched step,
-// (sequence, kv head, split) in sequence order.
-QW_DEV int attn_items(const MkArgs& a, const MkMisc& mm) {
-    return a.nseq > 0 ? mm.ibase[a.nseq] : a.aa.Hkv * attn::split_count(mm.seq + a.M);
+// Items of one launch: (kv head, query-head group, split) of the sequence, or,
+// in a batched step, (sequence, kv head, split) in sequence order with all G
+// query heads per item.  A multi-row (verify) launch gives its items the fewest
+// query heads (a divisor of G) for which every item still has a CTA of its
+// own: fewer rows per item shorten the attention phase, whose slowest item
+// every CTA waits for (5-row verify on Qwen3-4B: 3.00 -> 2.80 ms).  A one-row
+// step keeps all G per item: more, smaller items measured slower there
+// (Qwen3-4B 497 -> 486 tok/s, Qwen3-0.6B 1027 -> 967 tok/s).
+template <bool SUB>
+QW_DEV int attn_heads_per_item(const MkArgs& a, int nsp) {
+    const int G = a.aa.Hq / a.aa.Hkv;
+    if (SUB && a.M >= 2)
+        for (int h = 1; h < G; ++h)
+            if (G % h == 0 && a.aa.Hkv * (G / h) * nsp <= (int)gridDim.x) return h;
+    return G;
 }
-// Item `it` of layer l: its kv head, split, split count, first new position and
-// the attention arguments of its sequence.
+template <bool SUB>
+QW_DEV int attn_items(const MkArgs& a, const MkMisc& mm) {
+    if (a.nseq > 0) return mm.ibase[a.nseq];
+    const int nsp = attn::split_count(mm.seq + a.M);
+    if (!SUB) return a.aa.Hkv * nsp;
+    return a.aa.Hkv * (a.aa.Hq / a.aa.Hkv / attn_heads_per_item<SUB>(a, nsp)) * nsp;
+}
+// Item `it` of layer l: its kv head, split, split count, first new position,
+// query heads [qh0, qh0 + nqh) of the kv head, and the attention arguments of
+// its sequence.
 struct AttnItem {
-    int kvh, split, nsp, off;
+    int kvh, split, nsp, off, qh0, nqh;
 };
+template <bool SUB>
 QW_DEV AttnItem attn_item(const MkArgs& a, const MkMisc& mm, int l, int it, const bf16* qn, const bf16* kn,
                           AttnArgs& aa) {
     aa = a.aa;
@@ -866,8 +886,20 @@ QW_DEV AttnItem attn_item(const MkArgs& a, const MkMisc& mm, int l, int it, cons
         r.nsp = attn::split_count(mm.seq + a.M);
         aa.kcache = a.kc0 + (size_t)l * a.kv_layer_elems;
         aa.vcache = a.vc0 + (size_t)l * a.kv_layer_elems;
-        r.kvh = it / r.nsp;
-        r.split = it - r.kvh * r.nsp;
+        if (!SUB) {
+            r.kvh = it / r.nsp;
+            r.split = it - r.kvh * r.nsp;
+            r.qh0 = 0;
+            r.nqh = a.aa.Hq / a.aa.Hkv;
+            return r;
+        }
+        r.nqh = attn_heads_per_item<SUB>(a, r.nsp);
+        const int per_kvh = (a.aa.Hq / a.aa.Hkv / r.nqh) * r.nsp;
+        r.kvh = it / per_kvh;
+        const int rem = it - r.kvh * per_kvh;
+        const int qg = rem / r.nsp;
+        r.split = rem - qg * r.nsp;
+        r.qh0 = qg * r.nqh;
         return r;
     }
     int b = 0;
@@ -877,6 +909,8 @@ QW_DEV AttnItem attn_item(const MkArgs& a, const MkMisc& mm, int l, int it, cons
     r.nsp = attn::split_count(r.off + 1);
     r.kvh = j / r.nsp;
     r.split = j - r.kvh * r.nsp;
+    r.qh0 = 0;
+    r.nqh = a.aa.Hq / a.aa.Hkv;
     const MkSeq& sq = a.seqs[b];
     aa.q = a.q + (size_t)b * a.QD;
     aa.k = a.k + (size_t)b * a.KD;
@@ -887,13 +921,16 @@ QW_DEV AttnItem attn_item(const MkArgs& a, const MkMisc& mm, int l, int it, cons
     aa.kcache = sq.kc0 + (size_t)l * sq.kv_layer_elems;
     aa.vcache = sq.vc0 + (size_t)l * sq.kv_layer_elems;
     aa.part = a.aa.part + (size_t)b * a.part_seq_stride;
-    aa.counters = a.aa.counters + (size_t)b * a.aa.Hkv;
+    aa.counters = a.aa.counters + (size_t)b * a.aa.Hq;
     return r;
 }
 
 // ---- the kernel ------------------------------------------------------------
 template <int RMAX, int R>
 __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const __grid_constant__ MkArgs a) {
+    // attention items with fewer query heads only in the multi-row (verify)
+    // instantiations: the one-row kernel keeps the plain per-kv-head items
+    constexpr bool RMAX_SUB = RMAX > 8;
     extern __shared__ __align__(128) unsigned char sm[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     MkMisc& mm = *reinterpret_cast<MkMisc*>(sm + a.off_misc);
@@ -1006,9 +1043,9 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const __grid_cons
             csync();
             {
                 // this CTA's first attention item: issue its cached K/V rows now
-                if ((int)blockIdx.x < attn_items(a, mm)) {
+                if ((int)blockIdx.x < attn_items<RMAX_SUB>(a, mm)) {
                     AttnArgs aa;
-                    const AttnItem ai = attn_item(a, mm, l, blockIdx.x, q_norm, k_norm, aa);
+                    const AttnItem ai = attn_item<RMAX_SUB>(a, mm, l, blockIdx.x, q_norm, k_norm, aa);
                     attn::split_preload<RMAX>(aa, *reinterpret_cast<attn::SplitSmem<RMAX>*>(uni), ai.kvh, ai.split,
                                               ai.off, tid);
                 }
@@ -1024,14 +1061,14 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const __grid_cons
             MK_STAMP(5 * l + 1, 0);
             {
                 attn::SplitSmem<RMAX>& asm_ = *reinterpret_cast<attn::SplitSmem<RMAX>*>(uni);
-                const int items = attn_items(a, mm);
+                const int items = attn_items<RMAX_SUB>(a, mm);
                 for (int it = blockIdx.x; it < items; it += C) {
                     AttnArgs aa;
-                    const AttnItem ai = attn_item(a, mm, l, it, q_norm, k_norm, aa);
+                    const AttnItem ai = attn_item<RMAX_SUB>(a, mm, l, it, q_norm, k_norm, aa);
                     aa.prof = a.prof ? a.prof + ((size_t)blockIdx.x * MK_PROF_PHASES + 5 * l + 1) * MK_PROF_SLOTS
                                      : nullptr;
-                    attn::split_body<RMAX, MK_NT>(aa, asm_, ai.kvh, ai.split, ai.nsp, ai.off, tid, CSync{},
-                                                  it == (int)blockIdx.x);
+                    attn::split_body<RMAX, MK_NT, RMAX_SUB>(aa, asm_, ai.kvh, ai.split, ai.nsp, ai.off, ai.qh0,
+                                                            ai.nqh, tid, CSync{}, it == (int)blockIdx.x);
                     csync();
                 }
             }
@@ -1197,7 +1234,7 @@ __global__ void __launch_bounds__(MK_NT, 1) decode_step_kernel(const __grid_cons
             }
         }
         if (aborted)
-            for (int h = 0; h < a.aa.Hkv * (a.nseq > 0 ? a.nseq : 1); ++h) a.aa.counters[h] = 0u;
+            for (int h = 0; h < a.aa.Hq * (a.nseq > 0 ? a.nseq : 1); ++h) a.aa.counters[h] = 0u;
         a.sync[0] = 0u;
         a.sync[1] = 0u;
         a.sync[2] = 0u;  // visible to the next launch at kernel completion

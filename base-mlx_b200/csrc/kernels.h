@@ -103,7 +103,7 @@ struct AttnArgs {
     int S, Hq, Hkv;                                // local heads
     float scale;
     float* part;          // [Hkv, nsplit, R, 130]
-    unsigned* counters;   // [Hkv]
+    unsigned* counters;   // merge counters: [Hq] (split attention: kvh * G + first query head of the item; the kernel-chain attention uses [Hkv])
     bf16* out; int ldo;   // [S, Hq*128]
     int nsplit;
     int* err;

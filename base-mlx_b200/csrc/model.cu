@@ -395,7 +395,8 @@ void ensure_workspace(qw_model* m, int rows, int logits_rows) {
     w.amax_keys = (unsigned long long*)alloc((size_t)logits_rows * 8);
     const int nsplit_max = std::max(1, 2 * m->num_sms);
     w.attn_part = (float*)alloc((size_t)m->hkv_l * nsplit_max * 64 * 130 * 4);
-    w.attn_counters = (unsigned*)alloc((size_t)8 * std::max(m->hkv_l, 8) * 4);  // [sequence][kv head]
+    // [sequence][query head]: one merge counter per (kv head, first query head of an item)
+    w.attn_counters = (unsigned*)alloc((size_t)8 * std::max(m->hq_l, 8) * 4);
     w.next_tok = (int*)alloc(64);
     w.out_cap = std::max(w.out_cap, 65536);
     w.out = (int*)alloc((size_t)w.out_cap * 4);
@@ -405,7 +406,7 @@ void ensure_workspace(qw_model* m, int rows, int logits_rows) {
     w.scfg = (SampleCfg*)alloc(sizeof(SampleCfg));
     w.sctrl = alloc(QW_SAMPLE_CTRL_BYTES);
     QW_CUDA(cudaMemset(w.sctrl, 0, QW_SAMPLE_CTRL_BYTES));
-    QW_CUDA(cudaMemset(w.attn_counters, 0, (size_t)8 * std::max(m->hkv_l, 8) * 4));
+    QW_CUDA(cudaMemset(w.attn_counters, 0, (size_t)8 * std::max(m->hq_l, 8) * 4));
     QW_CUDA(cudaMemset(w.next_tok, 0, 64));
     w.cap_rows = rows;
     w.cap_logits = logits_rows;
