@@ -663,14 +663,21 @@ int qw_quantized_matmul(const void* x, const void* w, const void* scales, const 
         a.nseg = 1;
         a.epi = qw::EPI_STORE;
         cudaStream_t st = (cudaStream_t)stream;
-        if (M <= 8 && qw::qgemv_fits(a)) {
+        if (M <= 8) {
             // programmatic launch: the GEMV's blocks start while the previous
             // kernel drains and prefetch their weights into L2; every read of
             // x, w, scales and biases into the SMs and every write of y follows
-            // the wait on that kernel
+            // the wait on that kernel.  cudaErrorNotSupported: no GEMV form
+            // fits this row length in shared memory, the tiled GEMM takes it.
             a.weights_after_wait = 1;
-            QW_CUDA(qw::launch_qgemv(a, st, true, sms));
-        } else if (qw::qgemm_tc_supported(a) && !legacy_prefill_gemm()) {
+            const cudaError_t e = qw::launch_qgemv(a, st, true, sms);
+            if (e != cudaErrorNotSupported) {
+                QW_CUDA(e);
+                return;
+            }
+            a.weights_after_wait = 0;
+        }
+        if (qw::qgemm_tc_supported(a) && !legacy_prefill_gemm()) {
             // fp16 copy of x for the tensor-core kernel
             const size_t bytes = qw::qgemm_tc_scratch_bytes(M, K);
             QW_CUDA(qw::launch_qgemm_tc(a, qmm_scratch(dev, st, bytes), bytes, st));

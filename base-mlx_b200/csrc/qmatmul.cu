@@ -824,10 +824,11 @@ __global__ void __launch_bounds__(GS_NW * 32, 1) qgemv_stream_kernel(const __gri
 // ===========================================================================
 // Warp-ring decode GEMV for the standalone op (M <= 8, one output segment,
 // plain bf16 store or the lm_head's logits with per-tile argmax keys, no
-// RMSNorm prologue, K a multiple of 512): persistent CTAs of WR_NW warps, one
-// per SM.  CTA c takes the 16-row tiles [c*T/C, (c+1)*T/C); the CTA's
-// granules -- one granule is a stage of 8 groups (512 inputs) of one tile,
-// tile-major -- are split into WR_NW equal contiguous ranges, one per warp.
+// RMSNorm prologue, K a multiple of 512): persistent CTAs of NW warps (16, or
+// 8 / 4 when the staged activations leave no room for 16 rings), one per SM.
+// CTA c takes the 16-row tiles [c*T/C, (c+1)*T/C); the CTA's granules -- one
+// granule is a stage of 8 groups (512 inputs) of one tile, tile-major -- are
+// split into NW equal contiguous ranges, one per warp.
 // A warp streams its range through its own ring of `ns` slots, one TMA box
 // per operand: the 16 rows' weight words as two 128-byte-wide boxes with the
 // 128-byte swizzle, then 16 x 8 scales and 16 x 8 biases; lane 0 issues the
@@ -840,7 +841,6 @@ __global__ void __launch_bounds__(GS_NW * 32, 1) qgemv_stream_kernel(const __gri
 // per-tile activation staging, copy issue, CTA barriers and cross-warp
 // reduction, which bound that kernel's issue rate on wide outputs.
 // ===========================================================================
-constexpr int WR_NW = 16;
 constexpr int WR_NS_MAX = 4;
 constexpr int WR_SLOT = 5120;  // two 2 KB weight boxes, 256 B scales, 256 B biases, pad to 1 KB
 
@@ -854,13 +854,13 @@ struct WrLayout {
 
 // offsets from the dynamic shared memory base rounded up to 1 KB; total
 // includes that rounding slack
-__host__ __device__ inline WrLayout wr_layout(int KG, int M, int ns) {
+__host__ __device__ inline WrLayout wr_layout(int KG, int M, int ns, int nw) {
     WrLayout L;
     L.off_xsum = (unsigned)KG * M * XS_BLOCK_WORDS * 4u;
     L.off_bar = L.off_xsum + (unsigned)KG * 16u * 4u;
-    L.off_part = L.off_bar + WR_NW * WR_NS_MAX * 8u;
-    L.off_slots = (L.off_part + WR_NW * 2u * 512u + 1023u) & ~1023u;
-    L.total = L.off_slots + (unsigned)(WR_NW * ns * WR_SLOT) + 1024u;
+    L.off_part = L.off_bar + (unsigned)nw * WR_NS_MAX * 8u;
+    L.off_slots = (L.off_part + (unsigned)nw * 2u * 512u + 1023u) & ~1023u;
+    L.total = L.off_slots + (unsigned)(nw * ns * WR_SLOT) + 1024u;
     return L;
 }
 
@@ -905,16 +905,17 @@ QW_DEV void wr_store_tile(const QmmArgs& a, int tile, const float (&v)[4], int l
     }
 }
 
-__global__ void __launch_bounds__(WR_NW * 32, 1) qgemv_wr_kernel(const __grid_constant__ QmmArgs a,
-                                                                  const __grid_constant__ WrMaps maps, int ns,
-                                                                  int ntiles) {
-    constexpr int NT = WR_NW * 32;
+template <int NW>
+__global__ void __launch_bounds__(NW * 32, 1) qgemv_wr_kernel(const __grid_constant__ QmmArgs a,
+                                                               const __grid_constant__ WrMaps maps, int ns,
+                                                               int ntiles) {
+    constexpr int NT = NW * 32;
     extern __shared__ __align__(1024) unsigned char wr_smem_raw[];
     unsigned char* smraw = reinterpret_cast<unsigned char*>(((uintptr_t)wr_smem_raw + 1023) & ~(uintptr_t)1023);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int M = a.M, KG = a.K / 64, S = KG / 8;
-    const WrLayout L = wr_layout(KG, M, ns);
+    const WrLayout L = wr_layout(KG, M, ns, NW);
     uint32_t* xs = reinterpret_cast<uint32_t*>(smraw);
     float* xsum = reinterpret_cast<float*>(smraw + L.off_xsum);  // [KG][even, odd][8 columns]
     uint64_t* bar0 = reinterpret_cast<uint64_t*>(smraw + L.off_bar);
@@ -926,7 +927,7 @@ __global__ void __launch_bounds__(WR_NW * 32, 1) qgemv_wr_kernel(const __grid_co
     const int t0 = (int)((long long)blockIdx.x * ntiles / gridDim.x);
     const int t1 = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
     const int gc = (t1 - t0) * S;
-    const int gb = (int)((long long)warp * gc / WR_NW), ge = (int)((long long)(warp + 1) * gc / WR_NW);
+    const int gb = (int)((long long)warp * gc / NW), ge = (int)((long long)(warp + 1) * gc / NW);
 
     // granule j (CTA-local) into slot (j - gb) % ns: lane 0 only
     auto issue = [&](int j) {
@@ -939,7 +940,7 @@ __global__ void __launch_bounds__(WR_NW * 32, 1) qgemv_wr_kernel(const __grid_co
         tma_load_2d(slot + 4096, &maps.s, s * 8, row0, &bars[k]);
         tma_load_2d(slot + 4352, &maps.b, s * 8, row0, &bars[k]);
     };
-    if ((int)threadIdx.x < WR_NW * WR_NS_MAX) {
+    if ((int)threadIdx.x < NW * WR_NS_MAX) {
         mbar_init(&bar0[threadIdx.x], 1);
         fence_mbar_init();
     }
@@ -1093,8 +1094,8 @@ __global__ void __launch_bounds__(WR_NW * 32, 1) qgemv_wr_kernel(const __grid_co
 #pragma unroll
             for (int e = 0; e < 4; ++e) v[e] = pp[e * 32 + lane];
             // later warps whose ranges start inside the tile hold it as their first tile
-            for (int u = warp + 1; u < WR_NW; ++u) {
-                const int ub = (int)((long long)u * gc / WR_NW), ue = (int)((long long)(u + 1) * gc / WR_NW);
+            for (int u = warp + 1; u < NW; ++u) {
+                const int ub = (int)((long long)u * gc / NW), ue = (int)((long long)(u + 1) * gc / NW);
                 if (ub >= (tl + 1) * S) break;
                 if (ue > ub) {
                     const float* up = part + (size_t)(u * 2) * 128;
@@ -1217,17 +1218,24 @@ cudaError_t launch_qgemv_wr(const QmmArgs& a, cudaStream_t st, bool pdl, int num
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&dev_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     if (e != cudaSuccess) return e;
-    const long long fixed = (long long)wr_layout(KG, a.M, 0).total;
-    const int ns = (int)std::min<long long>(WR_NS_MAX, (dev_smem - fixed) / (long long)(WR_NW * WR_SLOT));
-    if (ns < 2) return cudaErrorNotSupported;
+    // 16 warps with two ring slots each when they fit beside the staged
+    // activations, else 8, else 4
+    int nw = 16, ns = 0;
+    for (; nw >= 4; nw /= 2) {
+        const long long fixed = (long long)wr_layout(KG, a.M, 0, nw).total;
+        ns = (int)std::min<long long>(WR_NS_MAX, (dev_smem - fixed) / (long long)(nw * WR_SLOT));
+        if (ns >= 2) break;
+    }
+    if (nw < 4) return cudaErrorNotSupported;
     WrMaps maps;
     if (!wr_maps(sg, a.K, maps)) return cudaErrorNotSupported;
-    const WrLayout L = wr_layout(KG, a.M, ns);
-    e = ensure_max_dyn_smem(qgemv_wr_kernel, (int)L.total);
+    const WrLayout L = wr_layout(KG, a.M, ns, nw);
+    auto kern = nw == 16 ? qgemv_wr_kernel<16> : nw == 8 ? qgemv_wr_kernel<8> : qgemv_wr_kernel<4>;
+    e = ensure_max_dyn_smem(kern, (int)L.total);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(std::min(ntiles, num_sms));
-    cfg.blockDim = dim3(WR_NW * 32);
+    cfg.blockDim = dim3(nw * 32);
     cfg.dynamicSmemBytes = L.total;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -1235,7 +1243,7 @@ cudaError_t launch_qgemv_wr(const QmmArgs& a, cudaStream_t st, bool pdl, int num
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, qgemv_wr_kernel, a, maps, ns, ntiles);
+    return cudaLaunchKernelEx(&cfg, kern, a, maps, ns, ntiles);
 }
 
 int qgemv_row_blocks(const QmmArgs& a) {
@@ -1292,7 +1300,7 @@ cudaError_t launch_qgemv(QmmArgs a, cudaStream_t st, bool pdl, int num_sms) {
     // long rows get 8 warps so each warp keeps a short list of groups
     const int NW = KG > 48 ? 8 : 4;
     const GvLayout L = gv_layout(KG, a.M, RT, NW);
-    if (L.total > 220 * 1024) return cudaErrorInvalidValue;
+    if (L.total > 220 * 1024) return cudaErrorNotSupported;  // no GEMV form fits: the caller takes the GEMM
     if (RT == 2) return NW == 8 ? launch_qgemv_t<2, 8>(a, nrb, L.total, st, pdl) : launch_qgemv_t<2, 4>(a, nrb, L.total, st, pdl);
     return NW == 8 ? launch_qgemv_t<1, 8>(a, nrb, L.total, st, pdl) : launch_qgemv_t<1, 4>(a, nrb, L.total, st, pdl);
 }

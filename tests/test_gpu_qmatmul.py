@@ -60,7 +60,9 @@ def test_qmatmul_4b_shapes(M, K, N):
                                    # warp-ring GEMV (>= one 16-row tile per SM, K a multiple of 512): ragged
                                    # last tile, one-granule tiles with most warps idle, tiles split over many
                                    # warps, eight columns
-                                   (3, 1024, 4741), (1, 512, 2400), (2, 4096, 2371), (8, 1536, 2376)])
+                                   (3, 1024, 4741), (1, 512, 2400), (2, 4096, 2371), (8, 1536, 2376),
+                                   # long rows: 4 warps per CTA (8 columns of 9728 staged inputs)
+                                   (8, 9728, 2560)])
 def test_qmatmul_edges(M, K, N):
     x, w, s, b = _case(M, K, N, seed=7 + M + K + N)
     ref = nm.bf16_round(x @ nm.dequantize(w, s, b).T)
