@@ -678,9 +678,12 @@ int qw_quantized_matmul(const void* x, const void* w, const void* scales, const 
             a.weights_after_wait = 0;
         }
         if (qw::qgemm_tc_supported(a) && !legacy_prefill_gemm()) {
-            // fp16 copy of x for the tensor-core kernel
-            const size_t bytes = qw::qgemm_tc_scratch_bytes(M, K);
-            QW_CUDA(qw::launch_qgemm_tc(a, qmm_scratch(dev, st, bytes), bytes, st));
+            // fp16 copy of x for the tensor-core kernel, then (output tiles
+            // fewer than the SMs) the fp32 partials of a K split
+            const int ksplit = qw::qgemm_tc_ksplit(a, sms);
+            const size_t bytes = ((qw::qgemm_tc_scratch_bytes(M, K) + 255) & ~(size_t)255) +
+                                 qw::qgemm_tc_ksplit_bytes(a, ksplit);
+            QW_CUDA(qw::launch_qgemm_tc(a, qmm_scratch(dev, st, bytes), bytes, st, ksplit));
         } else {
             QW_CUDA(qw::launch_qgemm(a, st, sms));
         }

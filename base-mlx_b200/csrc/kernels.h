@@ -67,6 +67,12 @@ struct QmmArgs {
     // kernel on the stream may have written them (the standalone op), so only
     // L2 prefetch hints run before the wait and the copies after it.
     int weights_after_wait;
+    // tcgen05 GEMM split over K (launch_qgemm_tc sets both): > 1 -> CTA z of
+    // gridDim.z covers whole 8-group chunks [z C / ksplit, (z + 1) C / ksplit)
+    // of the C = K / 512 chunks and stores fp32 partials kpart[z][col][row];
+    // a reduce kernel sums them in z order and applies the epilogue
+    int ksplit;
+    float* kpart;
 };
 
 // Decode / verify path: M <= 8.
@@ -89,7 +95,12 @@ cudaError_t launch_qgemm(QmmArgs a, cudaStream_t st, int num_sms);
 // qgemm_tc_supported is false.
 bool qgemm_tc_supported(const QmmArgs& a);
 size_t qgemm_tc_scratch_bytes(int M, int K);
-cudaError_t launch_qgemm_tc(QmmArgs a, void* scratch, size_t scratch_bytes, cudaStream_t st);
+// K split the standalone op gives a launch whose output tiles leave SMs idle
+// (one segment, plain / fp32 / residual store; 1: no split), and the scratch
+// it needs beyond qgemm_tc_scratch_bytes for the fp32 partials.
+int qgemm_tc_ksplit(const QmmArgs& a, int num_sms);
+size_t qgemm_tc_ksplit_bytes(const QmmArgs& a, int ksplit);
+cudaError_t launch_qgemm_tc(QmmArgs a, void* scratch, size_t scratch_bytes, cudaStream_t st, int ksplit = 1);
 
 // ---- other kernels ------------------------------------------------------
 struct AttnArgs {

@@ -170,6 +170,9 @@ __global__ void __launch_bounds__(TC_NT, 1) qgemm_tc_kernel(const QmmArgs a, con
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int KG = a.K / 64;
     const int rb = blockIdx.x, t0 = blockIdx.y * BN;
+    // this CTA's groups [g0, g0 + nl): all of K, or whole 8-group chunks of a K split
+    const int nch = KG / 8, zs = (int)gridDim.z, z = (int)blockIdx.z;
+    const int g0 = 8 * (z * nch / zs), nl = 8 * ((z + 1) * nch / zs) - g0;
 
     // segment of this row block (q | k | v of the fused qkv launch, or one)
     int si = 0;
@@ -215,7 +218,8 @@ __global__ void __launch_bounds__(TC_NT, 1) qgemm_tc_kernel(const QmmArgs a, con
         // ---- producers: packed words -> fp16 operand tile --------------------------
         const int row = tid & 127, half = tid >> 7;
         const __half2 k1024 = __float2half2_rn(1024.f);
-        for (int gi = 0; gi < KG; ++gi) {
+        for (int gi = 0; gi < nl; ++gi) {
+            // gi counts this CTA's groups (rings and parities); chunks start at multiples of 8
             const int ls = gi % L, as = gi & 1, c = gi >> 3;
             if (ok && (gi & 7) == 0 && !tc_wait(sb_full + (c & 1), (c >> 1) & 1)) ok = false;
             if (ok && !tc_wait(ld_full + ls, (gi / L) & 1)) ok = false;
@@ -250,7 +254,7 @@ __global__ void __launch_bounds__(TC_NT, 1) qgemm_tc_kernel(const QmmArgs a, con
     } else if (warp == 8) {
         if (lane == 0) {
             // ---- MMA issuer ------------------------------------------------------------
-            for (int gi = 0; gi < KG; ++gi) {
+            for (int gi = 0; gi < nl; ++gi) {
                 const int ls = gi % L, as = gi & 1;
                 if (!tc_wait(a_full + as, (gi >> 1) & 1) || !tc_wait(ld_full + ls, (gi / L) & 1)) {
                     ok = false;
@@ -283,10 +287,10 @@ __global__ void __launch_bounds__(TC_NT, 1) qgemm_tc_kernel(const QmmArgs a, con
             smap[rt] = &maps.s[sg];
             bmap[rt] = &maps.b[sg];
         }
-        for (int gi = 0; gi < KG; ++gi) {
-            const int ls = gi % L;
+        for (int gi = 0; gi < nl; ++gi) {
+            const int ls = gi % L, gk = g0 + gi;  // gk: the group's index in K
             if ((gi & 7) == 0) {
-                const int c = gi >> 3;
+                const int c = gi >> 3, ck = gk >> 3;
                 if (c >= 2 && !tc_wait(sb_empty + (c & 1), ((c - 2) >> 1) & 1)) {
                     ok = false;
                     break;
@@ -294,8 +298,8 @@ __global__ void __launch_bounds__(TC_NT, 1) qgemm_tc_kernel(const QmmArgs a, con
                 mbar_arrive_expect_tx(sb_full + (c & 1), RT * 4096);
 #pragma unroll
                 for (int rt = 0; rt < RT; ++rt) {
-                    tma_load_2d(SB_of(c & 1, rt), smap[rt], c * 8, n0, sb_full + (c & 1));
-                    tma_load_2d(SB_of(c & 1, rt) + 2048, bmap[rt], c * 8, n0, sb_full + (c & 1));
+                    tma_load_2d(SB_of(c & 1, rt), smap[rt], ck * 8, n0, sb_full + (c & 1));
+                    tma_load_2d(SB_of(c & 1, rt) + 2048, bmap[rt], ck * 8, n0, sb_full + (c & 1));
                 }
             }
             if (gi >= L && !tc_wait(ld_empty + ls, ((gi - L) / L) & 1)) {
@@ -303,9 +307,9 @@ __global__ void __launch_bounds__(TC_NT, 1) qgemm_tc_kernel(const QmmArgs a, con
                 break;
             }
             mbar_arrive_expect_tx(ld_full + ls, BN * 128 + RT * 4096);
-            tma_load_2d(X_of(ls), &maps.x, gi * 64, t0, ld_full + ls);
+            tma_load_2d(X_of(ls), &maps.x, gk * 64, t0, ld_full + ls);
 #pragma unroll
-            for (int rt = 0; rt < RT; ++rt) tma_load_2d(W_of(ls, rt), wmap[rt], gi * 8, n0, ld_full + ls);
+            for (int rt = 0; rt < RT; ++rt) tma_load_2d(W_of(ls, rt), wmap[rt], gk * 8, n0, ld_full + ls);
         }
     }
     pdl_launch_dependents();
@@ -331,6 +335,8 @@ __global__ void __launch_bounds__(TC_NT, 1) qgemm_tc_kernel(const QmmArgs a, con
                     if (t >= a.M) break;
                     if (RT == 2)
                         store_out(a, 0, EPI_SWIGLU, 0, n, t, v[0][c], v[RT - 1][c]);
+                    else if (a.ksplit > 1)
+                        a.kpart[((size_t)z * a.M + t) * a.seg[0].n + n] = v[0][c];
                     else
                         store_out(a, si, a.epi, n, 0, t, v[0][c], 0.f);
                 }
@@ -371,6 +377,20 @@ __global__ void x_to_f16p_kernel(const bf16* __restrict__ x, int ldx, int M, int
                            *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3));
         }
         *reinterpret_cast<uint4*>(xh + (size_t)row * K + (size_t)c * 8) = o;
+    }
+    pdl_launch_dependents();
+}
+
+// Sum of a K split's fp32 partials in split order, then the epilogue.
+__global__ void ksplit_reduce_kernel(const QmmArgs a) {
+    const int N = a.seg[0].n;
+    const long long total = (long long)a.M * N, plane = total;
+    pdl_wait();
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        float v = __ldcg(a.kpart + i);
+        for (int z = 1; z < a.ksplit; ++z) v += __ldcg(a.kpart + (size_t)z * plane + i);
+        const int t = (int)(i / N), n = (int)(i - (long long)t * N);
+        store_out(a, 0, a.epi, n, 0, t, v, 0.f);
     }
     pdl_launch_dependents();
 }
@@ -443,8 +463,31 @@ bool qgemm_tc_supported(const QmmArgs& a) {
     return true;
 }
 
-cudaError_t launch_qgemm_tc(QmmArgs a, void* scratch, size_t scratch_bytes, cudaStream_t st) {
+int qgemm_tc_ksplit(const QmmArgs& a, int num_sms) {
+    if (!qgemm_tc_supported(a) || a.nseg != 1 || num_sms < 1) return 1;
+    if (a.epi != EPI_STORE && a.epi != EPI_F32 && a.epi != EPI_RESID) return 1;
+    if (std::getenv("QW_TC_BN")) return 1;  // a forced tile width is taken as given
+    const int tiles = (a.seg[0].n + TC_BM - 1) / TC_BM * ((a.M + 127) / 128);
+    if (tiles * 2 > num_sms) return 1;
+    return std::max(1, std::min(a.K / 512, num_sms / tiles));
+}
+
+size_t qgemm_tc_ksplit_bytes(const QmmArgs& a, int ksplit) {
+    return ksplit > 1 ? (size_t)ksplit * a.M * a.seg[0].n * sizeof(float) : 0;
+}
+
+cudaError_t launch_qgemm_tc(QmmArgs a, void* scratch, size_t scratch_bytes, cudaStream_t st, int ksplit) {
     if (!qgemm_tc_supported(a)) return cudaErrorInvalidValue;
+    if (ksplit < 1 || ksplit > a.K / 512 || (ksplit > 1 && (a.nseg != 1 || a.epi == EPI_SWIGLU ||
+                                                           a.epi == EPI_LOGITS || a.epi == EPI_F32_PUSH)))
+        return cudaErrorInvalidValue;
+    a.ksplit = ksplit;
+    a.kpart = nullptr;
+    if (ksplit > 1) {
+        const size_t xb = (qgemm_tc_scratch_bytes(a.M, a.K) + 255) & ~(size_t)255;
+        if (!scratch || scratch_bytes < xb + qgemm_tc_ksplit_bytes(a, ksplit)) return cudaErrorInvalidValue;
+        a.kpart = reinterpret_cast<float*>(static_cast<unsigned char*>(scratch) + xb);
+    }
     // 256 activation rows per tile when that still gives every SM a tile, else 128
     // (QW_TC_BN=128|256 forces one); x is padded to a multiple of 256 rows either way
     const int Mpad = (a.M + TC_BN_MAX - 1) / TC_BN_MAX * TC_BN_MAX;
@@ -468,6 +511,7 @@ cudaError_t launch_qgemm_tc(QmmArgs a, void* scratch, size_t scratch_bytes, cuda
     if (e != cudaSuccess) return e;
     int BN = (long long)nrb * (Mpad / 256) >= 148 ? 256 : 128;
     if (const char* e = std::getenv("QW_TC_BN")) BN = std::atoi(e) == 256 ? 256 : 128;
+    if (ksplit > 1) BN = 128;
     TcMaps maps;
     std::memset(&maps, 0, sizeof(maps));
     if (!make_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh, a.K, Mpad, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B))
@@ -479,7 +523,14 @@ cudaError_t launch_qgemm_tc(QmmArgs a, void* scratch, size_t scratch_bytes, cuda
         maps.s[i] = sm.s;
         maps.b[i] = sm.b;
     }
-    const dim3 grid(nrb, (a.M + BN - 1) / BN);
+    const dim3 grid(nrb, (a.M + BN - 1) / BN, ksplit);
+    if (ksplit > 1) {
+        e = launch_tc_t<1, 128>(a, maps, grid, st);
+        if (e != cudaSuccess) return e;
+        const long long total = (long long)a.M * a.seg[0].n;
+        const int rblocks = (int)std::min<long long>((total + 255) / 256, 148 * 8);
+        return launch_pdl(ksplit_reduce_kernel, dim3(rblocks), dim3(256), 0, st, a);
+    }
     if (BN == 256) {
         if (a.epi == EPI_SWIGLU) return launch_tc_t<2, 256>(a, maps, grid, st);
         return launch_tc_t<1, 256>(a, maps, grid, st);
